@@ -1,0 +1,196 @@
+"""Operator entry points used by the models and the runner.
+
+CUDA tensors go to the sm_100a kernels of the ``inference_systems_b200._C``
+extension (``torch.ops.isb.*``); a missing extension on a CUDA tensor is an
+error, never a silent fallback.  CPU tensors run the plain-PyTorch contracts in
+``ops/reference.py`` (the engine's CPU path and the kernels' test oracle).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from inference_systems_b200.ops import reference as ref
+from inference_systems_b200.ops._ext import cuda_ops
+from inference_systems_b200.utils.context import ForwardBatch
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, zero_centered: bool) -> torch.Tensor:
+    if x.is_cuda:
+        return cuda_ops().rmsnorm(x, w, eps, zero_centered)
+    return ref.rmsnorm(x, w, eps, zero_centered)
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                zero_centered: bool) -> torch.Tensor:
+    if x.is_cuda:
+        return cuda_ops().add_rmsnorm(x, residual, w, eps, zero_centered)
+    return ref.add_rmsnorm(x, residual, w, eps, zero_centered)
+
+
+def embed(ids: torch.Tensor, weight: torch.Tensor, vocab_start: int = 0) -> torch.Tensor:
+    if ids.is_cuda:
+        return cuda_ops().embed(ids, weight, vocab_start)
+    return ref.embed(ids, weight, vocab_start)
+
+
+def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    if x.is_cuda:
+        return cuda_ops().gemm(x, w, 0)
+    return ref.gemm(x, w)
+
+
+def linear_silu_mul(x: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
+    if x.is_cuda:
+        return cuda_ops().gemm(x, w_packed, 1)
+    return ref.gemm_silu_mul(x, w_packed)
+
+
+def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor, k_norm: torch.Tensor,
+                    cos_sin: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, *, num_heads: int,
+                    num_kv_heads: int, head_dim: int, eps: float, gated: bool, zero_centered: bool,
+                    scale: float) -> torch.Tensor:
+    """q/k norm + RoPE + KV store + paged causal attention (+ sigmoid output gate)."""
+    if qkv.is_cuda:
+        c = cuda_ops()
+        q = c.attn_prepare(qkv, batch.positions, batch.slot_mapping, q_norm, k_norm, cos_sin, k_cache, v_cache,
+                           num_heads, num_kv_heads, head_dim, eps, gated, zero_centered)
+        if batch.is_prefill:
+            return c.attention_prefill(q, qkv, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
+                                       batch.block_tables, scale, gated, batch.max_seqlen_q)
+        return c.attention_decode(q, qkv, k_cache, v_cache, batch.context_lens, batch.block_tables, scale, gated)
+    q, gate, k, v = ref.attn_qkv_prepare(qkv, batch.positions, q_norm, k_norm, cos_sin, num_heads, num_kv_heads,
+                                         head_dim, eps, gated, zero_centered)
+    ref.store_kv(k, v, k_cache, v_cache, batch.slot_mapping)
+    return ref.paged_attention(q, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens, batch.block_tables,
+                               scale, gate)
+
+
+def gdn(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool, *,
+        hk: int, hv: int, dk: int, dv: int, eps: float) -> torch.Tensor:
+    """Gated DeltaNet mixer core (conv, norms, delta rule, gated norm); states updated in the pools."""
+    if proj.is_cuda:
+        c = cuda_ops()
+        if batch.is_prefill:
+            return c.gdn_prefill(proj, batch.cu_seqlens_q, batch.state_slots, conv_w, a_log, dt_bias, norm_w,
+                                 rec_pool, conv_pool, hk, hv, dk, dv, eps, batch.max_seqlen_q)
+        return c.gdn_decode(proj, batch.state_slots, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool,
+                            hk, hv, dk, dv, eps)
+    return ref.gdn_forward(proj, batch.cu_seqlens_host, batch.slots_host, conv_w, a_log, dt_bias, norm_w,
+                           rec_pool, conv_pool, hk=hk, hv=hv, dk=dk, dv=dv, eps=eps)
+
+
+def lm_head_sample(hidden: torch.Tensor, weight: torch.Tensor, temperatures: torch.Tensor, rng: torch.Tensor,
+                   vocab_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """LM-head GEMM fused with greedy / Gumbel-max selection over this rank's vocab slice.
+
+    ``rng`` is an int32 device tensor ``[seed, step]`` (read on the device, so a
+    captured CUDA graph samples fresh noise every replay).  Returns
+    ``(score [B] fp32, token [B] int32)`` where ``score`` is the winning
+    (perturbed) logit, comparable across ranks for the cross-rank argmax.
+    """
+    if hidden.is_cuda:
+        return cuda_ops().lm_head_sample(hidden, weight, temperatures, rng, vocab_offset)
+    logits = ref.gemm(hidden, weight).float()
+    seed, step = (int(v) for v in rng.tolist())
+    val, idx = gumbel_select(logits, temperatures, seed, step, vocab_offset)
+    return val, idx.to(torch.int32)
+
+
+# ----------------------------------------------------------------- RNG
+_M32 = 0xFFFFFFFF
+
+
+def _fmix32(h: torch.Tensor) -> torch.Tensor:
+    h = h & _M32
+    h = h ^ (h >> 16)
+    h = (h * 0x85EBCA6B) & _M32
+    h = h ^ (h >> 13)
+    h = (h * 0xC2B2AE35) & _M32
+    h = h ^ (h >> 16)
+    return h
+
+
+def uniform_noise(seed: int, step: int, rows: torch.Tensor, cols: torch.Tensor) -> torch.Tensor:
+    """Counter-based uniform(0,1) noise keyed by (seed, step, row, global vocab id).
+
+    The same integer hash (MurmurHash3's 32-bit finaliser applied to a mixed
+    key) runs in the CUDA sampling epilogue, so a token choice does not depend
+    on the tensor-parallel split of the vocabulary.
+    """
+    key = (seed * 0x9E3779B1 + step * 0x85EBCA77) & _M32
+    h = _fmix32(rows.long() * 0x27D4EB2F + key)
+    h = _fmix32(h ^ (cols.long() * 0x165667B1 & _M32))
+    return ((h >> 8).double() + 0.5) / float(1 << 24)
+
+
+def gumbel_select(logits: torch.Tensor, temperatures: torch.Tensor, seed: int, step: int,
+                  vocab_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
+    b, v = logits.shape
+    greedy = temperatures.float() <= 1e-10
+    rows = torch.arange(b, device=logits.device)[:, None]
+    cols = torch.arange(v, device=logits.device)[None, :] + vocab_offset
+    u = uniform_noise(seed, step, rows, cols)
+    g = (-torch.log(-torch.log(u))).float()
+    t = torch.where(greedy, torch.ones_like(temperatures.float()), temperatures.float())
+    score = torch.where(greedy[:, None], logits, logits / t[:, None] + g)
+    val, idx = score.max(dim=-1)
+    return val, idx + vocab_offset
+
+
+# ------------------------------------------------------- state maintenance
+def gdn_replay_commit(rec_states: torch.Tensor, slot_ids: torch.Tensor, keys: torch.Tensor, deltas: torch.Tensor,
+                      log_decays: torch.Tensor, commit_lengths: torch.Tensor, num_steps: int) -> None:
+    """In place: ``S[l, slot_b] <- fold_{t < len_b} (exp(g_t) S + k_t delta_t^T)``."""
+    if rec_states.is_cuda:
+        cuda_ops().gdn_replay_commit(rec_states, slot_ids, keys, deltas, log_decays, commit_lengths, num_steps)
+        return
+    b = slot_ids.numel()
+    idx = slot_ids.long()
+    state = rec_states.index_select(1, idx)
+    k = keys.view(keys.shape[0], b, num_steps, *keys.shape[2:]).float()
+    d = deltas.view(deltas.shape[0], b, num_steps, *deltas.shape[2:]).float()
+    g = log_decays.view(log_decays.shape[0], b, num_steps, *log_decays.shape[2:]).float()
+    lens = commit_lengths.long()
+    for t in range(num_steps):
+        upd = state * g[:, :, t].exp()[..., None, None] + torch.einsum("lbhd,lbhv->lbhdv", k[:, :, t], d[:, :, t])
+        state = torch.where((lens > t).view(1, b, 1, 1, 1), upd, state)
+    rec_states.index_copy_(1, idx, state)
+
+
+def gdn_conv_commit(conv_states: torch.Tensor, conv_history: torch.Tensor, slot_ids: torch.Tensor,
+                    boundaries: torch.Tensor, num_steps: int) -> None:
+    """``conv[l, slot_b] <- conv_history[l, b * num_steps + boundaries[b]]``."""
+    if conv_states.is_cuda:
+        cuda_ops().gdn_conv_commit(conv_states, conv_history, slot_ids, boundaries, num_steps)
+        return
+    b = slot_ids.numel()
+    rows = torch.arange(b) * num_steps + boundaries.long().cpu()
+    conv_states.index_copy_(1, slot_ids.long(), conv_history.index_select(1, rows.to(conv_history.device)))
+
+
+def quantize_state_int8(state: torch.Tensor, q_out: torch.Tensor, scale_out: torch.Tensor) -> None:
+    """Symmetric int8 along the last (value) dim with an fp32 scale per row."""
+    if state.is_cuda:
+        cuda_ops().quantize_state_int8(state, q_out, scale_out)
+        return
+    s = state.float()
+    scale = (s.abs().amax(dim=-1, keepdim=True) / 127.0).clamp(min=1e-8)
+    q_out.copy_(torch.round(s / scale).clamp(-127, 127).to(torch.int8))
+    scale_out.copy_(scale)
+
+
+def dequantize_state_int8(q: torch.Tensor, scale: torch.Tensor, out: torch.Tensor) -> None:
+    if q.is_cuda:
+        cuda_ops().dequantize_state_int8(q, scale, out)
+        return
+    out.copy_(q.float() * scale)
+
+
+def copy_kv_page(k_cache: torch.Tensor, v_cache: torch.Tensor, src_block: int, dst_block: int, num_tokens: int) -> None:
+    """Copy-on-write of the first ``num_tokens`` rows of a page (all KV heads, K and V)."""
+    if k_cache.is_cuda:
+        cuda_ops().copy_kv_page(k_cache, v_cache, src_block, dst_block, num_tokens)
+        return
+    k_cache[dst_block, :, :num_tokens] = k_cache[src_block, :, :num_tokens]
+    v_cache[dst_block, :, :num_tokens] = v_cache[src_block, :, :num_tokens]

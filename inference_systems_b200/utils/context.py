@@ -1,0 +1,39 @@
+"""Per-step batch metadata handed to every layer.
+
+Parity: the reference keeps the same facts in a module-global ``Context``
+(``nanovllm/utils/context.py:5-28``: ``is_prefill, cu_seqlens_q/k,
+max_seqlen_q/k, slot_mapping, context_lens, block_tables, state_slot_ids``).
+Here it is an explicit object passed down the forward call, so several
+batches (target, MTP draft, verify) can be in flight without global state and
+CUDA-graph captures own their static copies.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+
+@dataclass
+class ForwardBatch:
+    is_prefill: bool
+    input_ids: torch.Tensor            # [T] int64
+    positions: torch.Tensor            # [T] int64
+    cu_seqlens_q: torch.Tensor         # [B+1] int32 (device)
+    context_lens: torch.Tensor         # [B] int32: tokens visible after this step
+    block_tables: torch.Tensor         # [B, max_blocks] int32 (-1 padded)
+    slot_mapping: torch.Tensor         # [T] int32 (-1 = do not store)
+    state_slots: torch.Tensor          # [B] int32 GDN state-slot ids
+    logits_indices: torch.Tensor       # [B] int64: row of each sequence's last token
+    max_seqlen_q: int = 1
+    max_seqlen_k: int = 1
+    cu_seqlens_host: list[int] = field(default_factory=list)
+    slots_host: list[int] = field(default_factory=list)
+    num_seqs: int = 0
+    # GDN state capture for checkpoints / MTP verify: (seq, token offset) -> buffer row
+    gdn_history: dict | None = None
+
+    @property
+    def num_tokens(self) -> int:
+        return int(self.input_ids.shape[0])
