@@ -1,0 +1,489 @@
+// Full-attention kernels over the paged KV cache ([num_blocks, Hkv, 256, hd] bf16 per layer).
+//
+// attn_prepare:      split the fused projection row (per head: query | gate, then k, v),
+//                    per-head RMSNorm of q and k, rotate-half partial RoPE on the
+//                    first ``rotary_dim`` channels, write K/V into the cache at
+//                    ``slot_mapping`` (replaces the reference's Triton store kernel,
+//                    ``nanovllm/layers/attention.py:10-40``, and its torch q/k norm + RoPE).
+// attention_decode:  split-KV flash decoding; one CTA per (KV head, sequence, page)
+//                    serves the whole GQA group; a combine kernel merges the page
+//                    partials and applies the sigmoid output gate.
+// attention_prefill: causal varlen attention of the new tokens over all visible
+//                    cache rows (prefix-cached rows included), online softmax, GQA
+//                    group per CTA, sigmoid output gate fused.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace isb {
+
+namespace {
+
+constexpr int PAGE = 256;
+
+__device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float* v) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    v[2 * i] = f.x;
+    v[2 * i + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* p, const float* v) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// ------------------------------------------------------------------ prepare
+// One warp per (token, head); HD/32 channels per lane (HD in {128, 256}).
+template <int HD>
+__global__ void attn_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int qkv_stride, const int* __restrict__ pos,
+                                    const int* __restrict__ slot_map, const __nv_bfloat16* __restrict__ qn,
+                                    const __nv_bfloat16* __restrict__ kn, const float* __restrict__ cos_sin, int rd,
+                                    __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
+                                    __nv_bfloat16* __restrict__ q_out, int T, int Hq, int Hkv, float eps, bool gated,
+                                    bool zc) {
+  constexpr int E = HD / 32;
+  const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int heads = Hq + 2 * Hkv;
+  const int t = warp_global / heads, hh = warp_global % heads;
+  if (t >= T) return;
+  const __nv_bfloat16* row = qkv + size_t(t) * qkv_stride;
+  const int qw = Hq * HD * (gated ? 2 : 1);
+  float v[E];
+  const __nv_bfloat16* src;
+  int kind;  // 0 q, 1 k, 2 v
+  int head;
+  if (hh < Hq) { kind = 0; head = hh; src = row + head * HD * (gated ? 2 : 1); }
+  else if (hh < Hq + Hkv) { kind = 1; head = hh - Hq; src = row + qw + head * HD; }
+  else { kind = 2; head = hh - Hq - Hkv; src = row + qw + Hkv * HD + head * HD; }
+#pragma unroll
+  for (int i = 0; i < E; ++i) v[i] = __bfloat162float(src[lane * E + i]);
+  const int slot = slot_map[t];
+  if (kind == 2) {
+    if (slot >= 0) {
+      const int blk = slot / PAGE, off = slot % PAGE;
+      __nv_bfloat16* dst = vc + ((size_t(blk) * Hkv + head) * PAGE + off) * HD + lane * E;
+#pragma unroll
+      for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16(v[i]);
+    }
+    return;
+  }
+  // RMSNorm over the head
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < E; ++i) ss += v[i] * v[i];
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / float(HD) + eps);
+  const __nv_bfloat16* w = kind == 0 ? qn : kn;
+#pragma unroll
+  for (int i = 0; i < E; ++i) {
+    const float wi = __bfloat162float(w[lane * E + i]);
+    v[i] = zc ? v[i] * rs * (1.f + wi) : __bfloat162float(__float2bfloat16(v[i] * rs)) * wi;
+    v[i] = __bfloat162float(__float2bfloat16(v[i]));  // the reference rounds normed q/k to the model dtype
+  }
+  // rotate-half RoPE on channels [0, rd): pairs (c, c + rd/2)
+  const int half = rd / 2;
+  const int partner = half / E;  // lane distance between the two halves
+  const int p = pos[t];
+  float other[E];
+#pragma unroll
+  for (int i = 0; i < E; ++i) other[i] = __shfl_xor_sync(0xffffffffu, v[i], partner);
+  if (lane * E < rd) {
+    const bool first = lane * E < half;
+#pragma unroll
+    for (int i = 0; i < E; ++i) {
+      const int c = lane * E + i;
+      const int f = first ? c : c - half;
+      const float cs = cos_sin[size_t(p) * rd + f], sn = cos_sin[size_t(p) * rd + half + f];
+      v[i] = first ? v[i] * cs - other[i] * sn : v[i] * cs + other[i] * sn;
+    }
+  }
+  if (kind == 0) {
+    __nv_bfloat16* dst = q_out + (size_t(t) * Hq + head) * HD + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16(v[i]);
+  } else if (slot >= 0) {
+    const int blk = slot / PAGE, off = slot % PAGE;
+    __nv_bfloat16* dst = kc + ((size_t(blk) * Hkv + head) * PAGE + off) * HD + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) dst[i] = __float2bfloat16(v[i]);
+  }
+}
+
+// ------------------------------------------------------------------ decode
+// grid (Hkv, B, pages); 256 threads. Partials: m, l, o[G][HD] per (b, hq, page).
+template <int HD, int G>
+__global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* __restrict__ q,
+                                                          const __nv_bfloat16* __restrict__ kc,
+                                                          const __nv_bfloat16* __restrict__ vcache,
+                                                          const int* __restrict__ ctx_lens,
+                                                          const int* __restrict__ block_tables, int max_blocks,
+                                                          int Hkv, float scale, float* __restrict__ part_o,
+                                                          float* __restrict__ part_ml, int max_pages) {
+  __shared__ float q_s[G][HD];
+  __shared__ float p_s[G][PAGE];
+  __shared__ float red[8][G];
+  const int kvh = blockIdx.x, b = blockIdx.y, page = blockIdx.z;
+  const int ctx = ctx_lens[b];
+  const int start = page * PAGE;
+  const int Hq = Hkv * G;
+  const size_t pidx = (size_t(b) * Hq + kvh * G) * max_pages + page;  // + g * max_pages
+  if (start >= ctx) {
+    if (threadIdx.x < G) {
+      part_ml[(pidx + threadIdx.x * max_pages) * 2 + 0] = -INFINITY;
+      part_ml[(pidx + threadIdx.x * max_pages) * 2 + 1] = 0.f;
+    }
+    return;
+  }
+  const int n = min(PAGE, ctx - start);
+  const int blk = block_tables[b * max_blocks + page];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int i = tid; i < G * HD; i += 256) {
+    const int g = i / HD, d = i % HD;
+    q_s[g][d] = __bfloat162float(q[(size_t(b) * Hq + kvh * G + g) * HD + d]) * scale;
+  }
+  __syncthreads();
+  const __nv_bfloat16* K = kc + (size_t(blk) * Hkv + kvh) * PAGE * HD;
+  const __nv_bfloat16* V = vcache + (size_t(blk) * Hkv + kvh) * PAGE * HD;
+  constexpr int E = HD / 32;
+  // scores: each warp handles tokens warp, warp+8, ...; a lane holds E channels
+  for (int t = warp; t < n; t += 8) {
+    float kv[E];
+    if constexpr (E == 8) load_bf16x8(K + size_t(t) * HD + lane * E, kv);
+    else {
+#pragma unroll
+      for (int i = 0; i < E; ++i) kv[i] = __bfloat162float(K[size_t(t) * HD + lane * E + i]);
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < E; ++i) s += q_s[g][lane * E + i] * kv[i];
+      s = warp_sum(s);
+      if (lane == 0) p_s[g][t] = s;
+    }
+  }
+  __syncthreads();
+  // softmax partial per head
+  float mloc[G], lsum[G];
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float m = -INFINITY;
+    for (int t = tid; t < n; t += 256) m = fmaxf(m, p_s[g][t]);
+    m = warp_max(m);
+    if (lane == 0) red[warp][g] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float m = red[0][g];
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w][g]);
+    mloc[g] = m;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float l = 0.f;
+    for (int t = tid; t < n; t += 256) {
+      const float e = __expf(p_s[g][t] - mloc[g]);
+      p_s[g][t] = e;
+      l += e;
+    }
+    l = warp_sum(l);
+    if (lane == 0) red[warp][g] = l;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    float l = 0.f;
+    for (int w = 0; w < 8; ++w) l += red[w][g];
+    lsum[g] = l;
+  }
+  // P V: thread owns HD/256... channels: for HD=256 one channel per thread
+  for (int d = tid; d < HD; d += 256) {
+    float acc[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) acc[g] = 0.f;
+    for (int t = 0; t < n; ++t) {
+      const float vv = __bfloat162float(V[size_t(t) * HD + d]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) acc[g] += p_s[g][t] * vv;
+    }
+#pragma unroll
+    for (int g = 0; g < G; ++g) part_o[(pidx + g * max_pages) * HD + d] = acc[g];
+  }
+  if (tid < G) {
+    part_ml[(pidx + tid * max_pages) * 2 + 0] = mloc[tid];
+    part_ml[(pidx + tid * max_pages) * 2 + 1] = lsum[tid];
+  }
+}
+
+// grid (Hq, B); HD threads. Merges page partials, applies the output gate.
+template <int HD>
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_pages,
+                                    const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ qkv,
+                                    int qkv_stride, bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
+  const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
+  const int ctx = ctx_lens[b];
+  const int pages = (ctx + PAGE - 1) / PAGE;
+  const size_t base = (size_t(b) * Hq + h) * max_pages;
+  float m = -INFINITY;
+  for (int p = 0; p < pages; ++p) m = fmaxf(m, part_ml[(base + p) * 2]);
+  float l = 0.f, acc = 0.f;
+  for (int p = 0; p < pages; ++p) {
+    const float w = __expf(part_ml[(base + p) * 2] - m);
+    l += w * part_ml[(base + p) * 2 + 1];
+    acc += w * part_o[(base + p) * HD + d];
+  }
+  float o = pages > 0 && l > 0.f ? acc / l : 0.f;
+  if (gated) {
+    const float gt = __bfloat162float(qkv[size_t(b) * qkv_stride + h * 2 * HD + HD + d]);
+    o *= sigmoidf_(gt);
+  }
+  out[(size_t(b) * Hq + h) * HD + d] = __float2bfloat16(o);
+}
+
+// ----------------------------------------------------------------- prefill
+// grid (q_tiles, Hkv, B); 256 threads; QT queries x G heads per CTA, key tiles of KT.
+template <int HD, int G, int QT>
+__global__ void __launch_bounds__(256) attn_prefill_kernel(
+    const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vcache,
+    const int* __restrict__ cu_q, const int* __restrict__ ctx_lens, const int* __restrict__ block_tables,
+    int max_blocks, int Hkv, float scale, const __nv_bfloat16* __restrict__ qkv, int qkv_stride, bool gated,
+    __nv_bfloat16* __restrict__ out) {
+  constexpr int R = QT * G;        // query rows (query-major, head-minor)
+  constexpr int KT = 32;           // keys per tile
+  extern __shared__ float sm[];
+  float* q_s = sm;                          // [R][HD]
+  float* k_s = q_s + R * HD;                // [KT][HD + 1]
+  float* v_s = k_s + KT * (HD + 1);         // [KT][HD]
+  float* s_s = v_s + KT * HD;               // [R][KT]
+  float* m_s = s_s + R * KT;                // [R]
+  float* l_s = m_s + R;                     // [R]
+  float* a_s = l_s + R;                     // [R] rescale factors
+  const int qt = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int q0 = cu_q[b], nq = cu_q[b + 1] - q0;
+  const int tq0 = qt * QT;
+  if (tq0 >= nq) return;
+  const int ctx = ctx_lens[b];
+  const int past = ctx - nq;          // cached tokens before the first new query
+  const int Hq = Hkv * G;
+  const int tid = threadIdx.x;
+  const int nrows = min(QT, nq - tq0) * G;
+  for (int i = tid; i < R * HD; i += 256) {
+    const int r = i / HD, d = i % HD;
+    const int qi = r / G, g = r % G;
+    float val = 0.f;
+    if (qi < min(QT, nq - tq0)) val = __bfloat162float(q[(size_t(q0 + tq0 + qi) * Hq + kvh * G + g) * HD + d]) * scale;
+    q_s[i] = val;
+  }
+  for (int r = tid; r < R; r += 256) { m_s[r] = -INFINITY; l_s[r] = 0.f; }
+  // each thread owns output rows/channels: R*HD / 256 accumulators
+  constexpr int PER = R * HD / 256;
+  float acc[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) acc[i] = 0.f;
+  const int last_q_pos = past + min(QT, nq - tq0) - 1 + tq0;
+  const int kend = last_q_pos + 1;  // keys [0, kend)
+  __syncthreads();
+  for (int k0 = 0; k0 < kend; k0 += KT) {
+    const int nk = min(KT, kend - k0);
+    for (int i = tid; i < KT * HD; i += 256) {
+      const int kk = i / HD, d = i % HD;
+      float kvv = 0.f, vvv = 0.f;
+      if (kk < nk) {
+        const int pos = k0 + kk;
+        const int blk = block_tables[b * max_blocks + pos / PAGE];
+        const size_t off = ((size_t(blk) * Hkv + kvh) * PAGE + pos % PAGE) * HD + d;
+        kvv = __bfloat162float(kc[off]);
+        vvv = __bfloat162float(vcache[off]);
+      }
+      k_s[kk * (HD + 1) + d] = kvv;
+      v_s[kk * HD + d] = vvv;
+    }
+    __syncthreads();
+    // scores R x KT
+    for (int i = tid; i < R * KT; i += 256) {
+      const int r = i / KT, kk = i % KT;
+      const int qpos = past + tq0 + r / G;
+      float s = -INFINITY;
+      if (r < nrows && kk < nk && k0 + kk <= qpos) {
+        s = 0.f;
+        const float* qr = q_s + r * HD;
+        const float* kr = k_s + kk * (HD + 1);
+#pragma unroll 8
+        for (int d = 0; d < HD; ++d) s += qr[d] * kr[d];
+      }
+      s_s[i] = s;
+    }
+    __syncthreads();
+    // online softmax per row
+    for (int r = tid; r < R; r += 256) {
+      float mx = m_s[r];
+      for (int kk = 0; kk < KT; ++kk) mx = fmaxf(mx, s_s[r * KT + kk]);
+      float l = 0.f;
+      for (int kk = 0; kk < KT; ++kk) {
+        const float e = mx == -INFINITY ? 0.f : __expf(s_s[r * KT + kk] - mx);
+        s_s[r * KT + kk] = e;
+        l += e;
+      }
+      const float alpha = m_s[r] == -INFINITY ? 0.f : __expf(m_s[r] - mx);
+      a_s[r] = alpha;
+      l_s[r] = l_s[r] * alpha + l;
+      m_s[r] = mx;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int idx = tid + i * 256;
+      const int r = idx / HD, d = idx % HD;
+      float a = acc[i] * a_s[r];
+      for (int kk = 0; kk < nk; ++kk) a += s_s[r * KT + kk] * v_s[kk * HD + d];
+      acc[i] = a;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int idx = tid + i * 256;
+    const int r = idx / HD, d = idx % HD;
+    if (r >= nrows) continue;
+    const int qi = r / G, g = r % G;
+    const int t = q0 + tq0 + qi;
+    const int h = kvh * G + g;
+    float o = l_s[r] > 0.f ? acc[i] / l_s[r] : 0.f;
+    if (gated) o *= sigmoidf_(__bfloat162float(qkv[size_t(t) * qkv_stride + h * 2 * HD + HD + d]));
+    out[(size_t(t) * Hq + h) * HD + d] = __float2bfloat16(o);
+  }
+}
+
+void check_cache(const at::Tensor& kc, const at::Tensor& vc, int64_t hd) {
+  TORCH_CHECK(kc.dim() == 4 && kc.size(2) == PAGE && kc.size(3) == hd, "KV cache must be [blocks, Hkv, 256, hd]");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous() && kc.scalar_type() == at::kBFloat16, "KV cache layout");
+}
+
+}  // namespace
+
+at::Tensor attn_prepare(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slot_mapping,
+                        const at::Tensor& qn, const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
+                        at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps, bool gated, bool zc) {
+  check_cache(kc, vc, hd);
+  TORCH_CHECK(qkv.is_contiguous() && qkv.scalar_type() == at::kBFloat16, "qkv must be contiguous bf16");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && slot_mapping.scalar_type() == at::kInt, "int32 metadata");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos/sin table must be fp32");
+  const int T = qkv.size(0);
+  const int rd = cos_sin.size(1);
+  at::Tensor q = at::empty({T, Hq, hd}, qkv.options());
+  if (T == 0) return q;
+  const int warps = T * (Hq + 2 * Hkv);
+  const int threads = 256;
+  const int blocks = (warps * 32 + threads - 1) / threads;
+  auto st = at::cuda::getCurrentCUDAStream();
+#define ISB_PREP(HD_)                                                                                             \
+  attn_prepare_kernel<HD_><<<blocks, threads, 0, st>>>(                                                           \
+      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.size(1), positions.data_ptr<int>(),             \
+      slot_mapping.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(qn.data_ptr()),                        \
+      reinterpret_cast<const __nv_bfloat16*>(kn.data_ptr()), cos_sin.data_ptr<float>(), rd,                       \
+      reinterpret_cast<__nv_bfloat16*>(kc.data_ptr()), reinterpret_cast<__nv_bfloat16*>(vc.data_ptr()),          \
+      reinterpret_cast<__nv_bfloat16*>(q.data_ptr()), T, Hq, Hkv, float(eps), gated, zc)
+  TORCH_CHECK((rd / 2) % (hd / 32) == 0 && rd <= hd, "rotary dim must split evenly across lanes");
+  const int partner = (rd / 2) / (hd / 32);
+  TORCH_CHECK(partner > 0 && (partner & (partner - 1)) == 0, "rotary half must map to a power-of-two lane distance");
+  if (hd == 256) ISB_PREP(256);
+  else if (hd == 128) ISB_PREP(128);
+  else TORCH_CHECK(false, "attn_prepare supports head_dim 128 or 256");
+#undef ISB_PREP
+  return q;
+}
+
+at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+                            const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated) {
+  const int B = q.size(0), Hq = q.size(1), hd = q.size(2);
+  check_cache(kc, vc, hd);
+  const int Hkv = kc.size(1);
+  const int G = Hq / Hkv;
+  const int max_blocks = block_tables.size(1);
+  at::Tensor out = at::empty({B, Hq * hd}, q.options());
+  if (B == 0) return out;
+  const int max_pages = max_blocks;
+  at::Tensor part_o = at::empty({B, Hq, max_pages, hd}, q.options().dtype(at::kFloat));
+  at::Tensor part_ml = at::empty({B, Hq, max_pages, 2}, q.options().dtype(at::kFloat));
+  auto st = at::cuda::getCurrentCUDAStream();
+  const dim3 grid(Hkv, B, max_pages);
+#define ISB_DEC(HD_, G_)                                                                                             \
+  attn_decode_kernel<HD_, G_><<<grid, 256, 0, st>>>(                                                                 \
+      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), \
+      reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), ctx_lens.data_ptr<int>(), block_tables.data_ptr<int>(), \
+      max_blocks, Hkv, float(scale), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), max_pages)
+  if (hd == 256 && G == 4) ISB_DEC(256, 4);
+  else if (hd == 256 && G == 2) ISB_DEC(256, 2);
+  else if (hd == 256 && G == 6) ISB_DEC(256, 6);
+  else if (hd == 256 && G == 3) ISB_DEC(256, 3);
+  else if (hd == 256 && G == 8) ISB_DEC(256, 8);
+  else if (hd == 256 && G == 1) ISB_DEC(256, 1);
+  else if (hd == 128 && G == 2) ISB_DEC(128, 2);
+  else if (hd == 128 && G == 1) ISB_DEC(128, 1);
+  else if (hd == 128 && G == 4) ISB_DEC(128, 4);
+  else TORCH_CHECK(false, "attention_decode: unsupported (head_dim, group) = (", hd, ", ", G, ")");
+#undef ISB_DEC
+#define ISB_COMB(HD_)                                                                                              \
+  attn_combine_kernel<HD_><<<dim3(Hq, B), HD_, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),       \
+                                                       max_pages, ctx_lens.data_ptr<int>(),                          \
+                                                       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),       \
+                                                       qkv.size(1), gated,                                           \
+                                                       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), Hq)
+  if (hd == 256) ISB_COMB(256); else ISB_COMB(128);
+#undef ISB_COMB
+  return out;
+}
+
+at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+                             const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
+                             double scale, bool gated, int64_t max_seqlen_q) {
+  const int T = q.size(0), Hq = q.size(1), hd = q.size(2);
+  check_cache(kc, vc, hd);
+  const int Hkv = kc.size(1);
+  const int G = Hq / Hkv;
+  const int B = ctx_lens.numel();
+  at::Tensor out = at::empty({T, Hq * hd}, q.options());
+  if (T == 0) return out;
+  auto st = at::cuda::getCurrentCUDAStream();
+#define ISB_PRE(HD_, G_, QT_)                                                                                       \
+  do {                                                                                                             \
+    constexpr int R = QT_ * G_;                                                                                   \
+    const int smem = (R * HD_ + 32 * (HD_ + 1) + 32 * HD_ + R * 32 + 3 * R) * 4;                                  \
+    auto kern = attn_prefill_kernel<HD_, G_, QT_>;                                                                 \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                                \
+    const dim3 grid((max_seqlen_q + QT_ - 1) / QT_, Hkv, B);                                                       \
+    kern<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),                           \
+                                  reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()),                          \
+                                  reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), cu_q.data_ptr<int>(),    \
+                                  ctx_lens.data_ptr<int>(), block_tables.data_ptr<int>(), block_tables.size(1),    \
+                                  Hkv, float(scale), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),      \
+                                  qkv.size(1), gated, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));          \
+  } while (0)
+  if (hd == 256 && G == 4) ISB_PRE(256, 4, 16);
+  else if (hd == 256 && G == 2) ISB_PRE(256, 2, 32);
+  else if (hd == 256 && G == 6) ISB_PRE(256, 6, 8);
+  else if (hd == 256 && G == 3) ISB_PRE(256, 3, 16);
+  else if (hd == 256 && G == 8) ISB_PRE(256, 8, 8);
+  else if (hd == 256 && G == 1) ISB_PRE(256, 1, 32);
+  else if (hd == 128 && G == 2) ISB_PRE(128, 2, 32);
+  else if (hd == 128 && G == 1) ISB_PRE(128, 1, 64);
+  else if (hd == 128 && G == 4) ISB_PRE(128, 4, 16);
+  else TORCH_CHECK(false, "attention_prefill: unsupported (head_dim, group) = (", hd, ", ", G, ")");
+#undef ISB_PRE
+  return out;
+}
+
+}  // namespace isb

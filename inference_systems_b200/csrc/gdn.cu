@@ -1,0 +1,387 @@
+// Gated DeltaNet (GDN) kernels, fp32 recurrent state updated IN PLACE in the slot pool.
+//
+// gdn_scan: one CTA per (key head, sequence) runs the whole mixer core for the
+//   key head's group of value heads:
+//     causal depthwise conv (width 4) over q|k|v channels with the conv-state
+//     window in registers -> SiLU -> L2-normalise q, k (q * 1/sqrt(Dk)) ->
+//     beta = sigmoid(b), g = -exp(A_log) * softplus(a + dt_bias) ->
+//     S <- e^g S;  delta = (v - k^T S) beta;  S <- S + k delta^T;  o = q^T S ->
+//     gated RMSNorm: norm(bf16(o)) * w * SiLU(z)
+//   (math: ``nanovllm/models/qwen35_reference.py:52-386``; the reference's CUDA
+//   decode kernel ``nanovllm/csrc/gdn_decode_kernel.cu`` handles only Hk == Hv and
+//   copies states through gather/scatter; here Hv = r * Hk and the pools are
+//   addressed by slot id).
+//   Each thread owns a 16 x 4 register tile of the 128 x 128 state (rows
+//   16*kr .. +15, columns 4*lane .. +3), so k^T S and q^T S are formed in one
+//   pass over the state and the state is read and written exactly once per
+//   sequence (decode: once per token).  One CTA per key head makes the
+//   shared q/k conv-state update race-free when Hv > Hk.
+//   Optional outputs: per-token state history (MTP verify / prefix
+//   checkpoints) and compact replay records (k, delta, g).
+// gdn_replay_commit: fold accepted (k, delta, g) records into the pool.
+// gdn_conv_commit:   copy an accepted conv window from a history into the pool.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace isb {
+
+namespace {
+
+constexpr int D = 128;          // key == value head dim handled by these kernels
+constexpr int KW = 4;           // conv width
+constexpr int kThreads = 256;   // 8 row groups x 32 column groups
+
+struct ScanArgs {
+  const __nv_bfloat16* proj;
+  int proj_stride;
+  const int* cu_seqlens;   // [B+1] or nullptr (one token per sequence)
+  const int* slots;        // [B]
+  const __nv_bfloat16* conv_w;  // [C, 4]
+  const float* A_log;
+  const float* dt_bias;
+  const __nv_bfloat16* norm_w;  // [D]
+  float* rec;              // [S, Hv, D, D]
+  __nv_bfloat16* conv;     // [S, C, 3]
+  __nv_bfloat16* out;      // [T, Hv*D]
+  int Hk, Hv, C;
+  float eps;
+  bool write_final;        // write the final state back to the pool
+  const int* hist_row;     // [T] history row per token (-1: none) or nullptr
+  float* hist_rec;         // [rows, Hv, D, D]
+  __nv_bfloat16* hist_conv;  // [rows, C, 3]
+  float* rec_k;            // [T, Hv, D] replay records or nullptr
+  float* rec_delta;        // [T, Hv, D]
+  float* rec_g;            // [T, Hv]
+};
+
+__device__ __forceinline__ float softplusf(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+__device__ __forceinline__ float block_sum_128(float v, float* scratch, int tid) {
+  // sum over threads 0..127 (4 warps); every caller thread participates in the syncs
+  v = warp_sum(v);
+  if ((tid & 31) == 0 && tid < 128) scratch[tid >> 5] = v;
+  __syncthreads();
+  const float r = scratch[0] + scratch[1] + scratch[2] + scratch[3];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
+  __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
+  __shared__ float red_k[8][D], red_q[8][D];
+  __shared__ float scal[16];
+
+  const int tid = threadIdx.x;
+  const int kr = tid >> 5, vc = (tid & 31) * 4;
+  const int hk = blockIdx.x, b = blockIdx.y;
+  const int r = a.Hv / a.Hk;
+  const int t0 = a.cu_seqlens ? a.cu_seqlens[b] : b;
+  const int t1 = a.cu_seqlens ? a.cu_seqlens[b + 1] : b + 1;
+  const int slot = a.slots[b];
+  const int kd = a.Hk * D;
+  // q/k channel of this thread (threads 0..127: q, 128..255: k)
+  const int qk_ch = tid < 128 ? hk * D + tid : kd + hk * D + (tid - 128);
+  const float wq0 = __bfloat162float(a.conv_w[qk_ch * KW + 0]), wq1 = __bfloat162float(a.conv_w[qk_ch * KW + 1]),
+              wq2 = __bfloat162float(a.conv_w[qk_ch * KW + 2]), wq3 = __bfloat162float(a.conv_w[qk_ch * KW + 3]);
+  const float inv_sqrt_d = rsqrtf(float(D));
+
+  for (int j = 0; j < r; ++j) {
+    const int h = hk * r + j;
+    // conv windows (registers); the pool is not modified until the end
+    __nv_bfloat16* cq = a.conv + (size_t(slot) * a.C + qk_ch) * (KW - 1);
+    float qs0 = __bfloat162float(cq[0]), qs1 = __bfloat162float(cq[1]), qs2 = __bfloat162float(cq[2]);
+    const int v_ch = 2 * kd + h * D + (tid & 127);
+    float vs0 = 0.f, vs1 = 0.f, vs2 = 0.f, wv0 = 0.f, wv1 = 0.f, wv2 = 0.f, wv3 = 0.f;
+    if (tid < 128) {
+      const __nv_bfloat16* cv = a.conv + (size_t(slot) * a.C + v_ch) * (KW - 1);
+      vs0 = __bfloat162float(cv[0]); vs1 = __bfloat162float(cv[1]); vs2 = __bfloat162float(cv[2]);
+      wv0 = __bfloat162float(a.conv_w[v_ch * KW + 0]); wv1 = __bfloat162float(a.conv_w[v_ch * KW + 1]);
+      wv2 = __bfloat162float(a.conv_w[v_ch * KW + 2]); wv3 = __bfloat162float(a.conv_w[v_ch * KW + 3]);
+    }
+    const float A = -expf(a.A_log[h]);
+    const float dtb = a.dt_bias[h];
+    // state tile
+    float* S = a.rec + ((size_t(slot) * a.Hv + h) * D) * D;
+    float4 st[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
+
+    for (int t = t0; t < t1; ++t) {
+      const __nv_bfloat16* x = a.proj + size_t(t) * a.proj_stride;
+      // --- conv + SiLU
+      const float xq = __bfloat162float(x[qk_ch]);
+      const float aq = silu(wq0 * qs0 + wq1 * qs1 + wq2 * qs2 + wq3 * xq);
+      qs0 = qs1; qs1 = qs2; qs2 = xq;
+      if (tid < 128) {
+        q_s[tid] = aq;
+        const float xv = __bfloat162float(x[v_ch]);
+        v_s[tid] = silu(wv0 * vs0 + wv1 * vs1 + wv2 * vs2 + wv3 * xv);
+        vs0 = vs1; vs1 = vs2; vs2 = xv;
+      } else {
+        k_s[tid - 128] = aq;
+      }
+      if (tid == 0) {
+        const float bb = __bfloat162float(x[a.C + a.Hv * D + h]);
+        const float aa = __bfloat162float(x[a.C + a.Hv * D + a.Hv + h]);
+        const float g = A * softplusf(aa + dtb);
+        scal[0] = 1.f / (1.f + expf(-bb));   // beta
+        scal[1] = g;
+        scal[2] = expf(g);                    // decay
+      }
+      __syncthreads();
+      // --- L2 norms of q (threads 0..127) and k (128..255) and q.k
+      {
+        float sq = warp_sum(aq * aq);
+        if ((tid & 31) == 0) red_k[0][tid >> 5] = sq;
+        __syncthreads();
+        const float nq = red_k[0][0] + red_k[0][1] + red_k[0][2] + red_k[0][3];
+        const float nk = red_k[0][4] + red_k[0][5] + red_k[0][6] + red_k[0][7];
+        const float iq = rsqrtf(nq + 1e-6f) * inv_sqrt_d, ik = rsqrtf(nk + 1e-6f);
+        __syncthreads();
+        if (tid < 128) q_s[tid] = aq * iq; else k_s[tid - 128] = aq * ik;
+        __syncthreads();
+      }
+      const float beta = scal[0], g = scal[1], decay = scal[2];
+      // --- k^T S and q^T S for this thread's tile
+      float ks[4] = {0.f, 0.f, 0.f, 0.f}, qsum[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float kk = k_s[kr * 16 + i], qq = q_s[kr * 16 + i];
+        ks[0] += kk * st[i].x; ks[1] += kk * st[i].y; ks[2] += kk * st[i].z; ks[3] += kk * st[i].w;
+        qsum[0] += qq * st[i].x; qsum[1] += qq * st[i].y; qsum[2] += qq * st[i].z; qsum[3] += qq * st[i].w;
+      }
+      *reinterpret_cast<float4*>(&red_k[kr][vc]) = make_float4(ks[0], ks[1], ks[2], ks[3]);
+      *reinterpret_cast<float4*>(&red_q[kr][vc]) = make_float4(qsum[0], qsum[1], qsum[2], qsum[3]);
+      // q.k for the output term
+      float qk_part = tid < 128 ? q_s[tid] * k_s[tid] : 0.f;
+      qk_part = warp_sum(qk_part);
+      if ((tid & 31) == 0 && tid < 128) scal[4 + (tid >> 5)] = qk_part;
+      __syncthreads();
+      float o = 0.f;
+      if (tid < 128) {
+        float kS = 0.f, qS = 0.f;
+#pragma unroll
+        for (int g8 = 0; g8 < 8; ++g8) { kS += red_k[g8][tid]; qS += red_q[g8][tid]; }
+        const float qk = scal[4] + scal[5] + scal[6] + scal[7];
+        const float delta = (v_s[tid] - decay * kS) * beta;
+        d_s[tid] = delta;
+        o = decay * qS + qk * delta;
+        if (a.rec_k) {
+          a.rec_k[(size_t(t) * a.Hv + h) * D + tid] = k_s[tid];
+          a.rec_delta[(size_t(t) * a.Hv + h) * D + tid] = delta;
+          if (tid == 0) a.rec_g[size_t(t) * a.Hv + h] = g;
+        }
+      }
+      __syncthreads();
+      // --- state update
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float kk = k_s[kr * 16 + i];
+        st[i].x = decay * st[i].x + kk * d_s[vc + 0];
+        st[i].y = decay * st[i].y + kk * d_s[vc + 1];
+        st[i].z = decay * st[i].z + kk * d_s[vc + 2];
+        st[i].w = decay * st[i].w + kk * d_s[vc + 3];
+      }
+      const int hrow = a.hist_row ? a.hist_row[t] : -1;
+      if (hrow >= 0) {
+        float* HS = a.hist_rec + ((size_t(hrow) * a.Hv + h) * D) * D;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) *reinterpret_cast<float4*>(HS + (kr * 16 + i) * D + vc) = st[i];
+        __nv_bfloat16* hc = a.hist_conv + size_t(hrow) * a.C * (KW - 1);
+        if (j == 0) {
+          __nv_bfloat16* p = hc + size_t(qk_ch) * (KW - 1);
+          p[0] = __float2bfloat16(qs0); p[1] = __float2bfloat16(qs1); p[2] = __float2bfloat16(qs2);
+        }
+        if (tid < 128) {
+          __nv_bfloat16* p = hc + size_t(v_ch) * (KW - 1);
+          p[0] = __float2bfloat16(vs0); p[1] = __float2bfloat16(vs1); p[2] = __float2bfloat16(vs2);
+        }
+      }
+      // --- gated RMSNorm epilogue
+      const float ob = __bfloat162float(__float2bfloat16(o));
+      const float ss = block_sum_128(tid < 128 ? ob * ob : 0.f, &scal[8], tid);
+      if (tid < 128) {
+        const float z = __bfloat162float(x[a.C + h * D + tid]);
+        const float y = ob * rsqrtf(ss / float(D) + a.eps) * __bfloat162float(a.norm_w[tid]) * silu(z);
+        a.out[size_t(t) * (a.Hv * D) + h * D + tid] = __float2bfloat16(y);
+      }
+    }
+    if (a.write_final) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) *reinterpret_cast<float4*>(S + (kr * 16 + i) * D + vc) = st[i];
+      if (tid < 128) {
+        __nv_bfloat16* cv = a.conv + (size_t(slot) * a.C + v_ch) * (KW - 1);
+        cv[0] = __float2bfloat16(vs0); cv[1] = __float2bfloat16(vs1); cv[2] = __float2bfloat16(vs2);
+      }
+      if (j == r - 1) {
+        // every value head re-read the untouched q/k window; commit it once, last
+        cq[0] = __float2bfloat16(qs0); cq[1] = __float2bfloat16(qs1); cq[2] = __float2bfloat16(qs2);
+      }
+    }
+    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int pool_slots, const int* slots,
+                                                                 const float* keys, const float* deltas,
+                                                                 const float* gs, const int* lens, int steps, int B,
+                                                                 int Hv) {
+  const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z;
+  const int tid = threadIdx.x, kr = tid >> 5, vc = (tid & 31) * 4;
+  const int n = min(max(lens[b], 0), steps);
+  if (n == 0) return;
+  float* S = rec + (((size_t(l) * pool_slots + slots[b]) * Hv + h) * D) * D;
+  float4 st[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
+  for (int t = 0; t < n; ++t) {
+    const size_t row = (size_t(l) * B * steps + size_t(b) * steps + t) * Hv + h;
+    const float e = expf(gs[row]);
+    const float4 dl = *reinterpret_cast<const float4*>(deltas + row * D + vc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float kk = keys[row * D + kr * 16 + i];
+      st[i].x = e * st[i].x + kk * dl.x;
+      st[i].y = e * st[i].y + kk * dl.y;
+      st[i].z = e * st[i].z + kk * dl.z;
+      st[i].w = e * st[i].w + kk * dl.w;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) *reinterpret_cast<float4*>(S + (kr * 16 + i) * D + vc) = st[i];
+}
+
+__global__ void conv_commit_kernel(__nv_bfloat16* conv, int pool_slots, const __nv_bfloat16* hist, int hist_rows,
+                                   const int* slots, const int* bounds, int steps, int elems) {
+  const int b = blockIdx.x, l = blockIdx.y;
+  const int row = b * steps + bounds[b];
+  const __nv_bfloat16* src = hist + (size_t(l) * hist_rows + row) * elems;
+  __nv_bfloat16* dst = conv + (size_t(l) * pool_slots + slots[b]) * elems;
+  for (int i = threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
+}
+
+void check_gdn(const at::Tensor& proj, const at::Tensor& rec, const at::Tensor& conv, int64_t dk, int64_t dv,
+               int64_t hk, int64_t hv) {
+  TORCH_CHECK(dk == D && dv == D, "CUDA GDN kernels handle key/value head dim 128");
+  TORCH_CHECK(hv % hk == 0, "Hv must be a multiple of Hk");
+  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.is_contiguous(), "proj must be contiguous bf16");
+  TORCH_CHECK(rec.scalar_type() == at::kFloat && rec.is_contiguous() && rec.size(1) == hv, "bad recurrent pool");
+  TORCH_CHECK(conv.scalar_type() == at::kBFloat16 && conv.is_contiguous() && conv.size(2) == KW - 1,
+              "bad conv pool");
+}
+
+ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
+                   const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor& rec, at::Tensor& conv,
+                   at::Tensor& out, int64_t hk, int64_t hv, double eps) {
+  ScanArgs a = {};
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.proj_stride = proj.size(1);
+  a.slots = slots.data_ptr<int>();
+  a.conv_w = reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr());
+  a.A_log = A_log.data_ptr<float>();
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  a.rec = rec.data_ptr<float>();
+  a.conv = reinterpret_cast<__nv_bfloat16*>(conv.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.Hk = hk;
+  a.Hv = hv;
+  a.C = conv.size(1);
+  a.eps = float(eps);
+  a.write_final = true;
+  TORCH_CHECK(a.C == 2 * hk * D + hv * D, "conv pool channel count mismatch");
+  TORCH_CHECK(proj.size(1) == a.C + hv * D + 2 * hv, "projection width mismatch");
+  TORCH_CHECK(conv_w.scalar_type() == at::kBFloat16 && conv_w.size(0) == a.C && conv_w.size(1) == KW, "conv weight");
+  TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "A_log/dt_bias must be fp32");
+  TORCH_CHECK(slots.scalar_type() == at::kInt, "slots must be int32");
+  return a;
+}
+
+}  // namespace
+
+at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
+                      const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk,
+                      int64_t hv, int64_t dk, int64_t dv, double eps) {
+  check_gdn(proj, rec, conv, dk, dv, hk, hv);
+  const int B = proj.size(0);
+  at::Tensor out = at::empty({B, hv * D}, proj.options());
+  if (B == 0) return out;
+  ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
+  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  return out;
+}
+
+at::Tensor gdn_prefill(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                       const at::Tensor& conv_w, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                       const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv, int64_t dk,
+                       int64_t dv, double eps, int64_t max_seqlen) {
+  check_gdn(proj, rec, conv, dk, dv, hk, hv);
+  const int T = proj.size(0), B = slots.numel();
+  at::Tensor out = at::empty({T, hv * D}, proj.options());
+  if (T == 0 || B == 0) return out;
+  ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
+  a.cu_seqlens = cu_seqlens.data_ptr<int>();
+  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  return out;
+}
+
+// Scan with per-token state history and/or replay records; optionally leaves the pool untouched.
+at::Tensor gdn_scan_history(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                            const at::Tensor& conv_w, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                            const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv,
+                            double eps, bool write_final, const c10::optional<at::Tensor>& hist_row,
+                            c10::optional<at::Tensor> hist_rec, c10::optional<at::Tensor> hist_conv,
+                            c10::optional<at::Tensor> rec_k, c10::optional<at::Tensor> rec_delta,
+                            c10::optional<at::Tensor> rec_g) {
+  check_gdn(proj, rec, conv, D, D, hk, hv);
+  const int T = proj.size(0), B = slots.numel();
+  at::Tensor out = at::empty({T, hv * D}, proj.options());
+  if (T == 0 || B == 0) return out;
+  ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
+  a.cu_seqlens = cu_seqlens.data_ptr<int>();
+  a.write_final = write_final;
+  if (hist_row.has_value()) {
+    TORCH_CHECK(hist_rec.has_value() && hist_conv.has_value(), "history needs recurrent and conv buffers");
+    a.hist_row = hist_row->data_ptr<int>();
+    a.hist_rec = hist_rec->data_ptr<float>();
+    a.hist_conv = reinterpret_cast<__nv_bfloat16*>(hist_conv->data_ptr());
+  }
+  if (rec_k.has_value()) {
+    a.rec_k = rec_k->data_ptr<float>();
+    a.rec_delta = rec_delta->data_ptr<float>();
+    a.rec_g = rec_g->data_ptr<float>();
+  }
+  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  return out;
+}
+
+void gdn_replay_commit(at::Tensor rec, const at::Tensor& slots, const at::Tensor& keys, const at::Tensor& deltas,
+                       const at::Tensor& gs, const at::Tensor& lens, int64_t steps) {
+  TORCH_CHECK(rec.dim() == 5 && rec.size(3) == D && rec.size(4) == D, "recurrent pool must be [L, S, Hv, 128, 128]");
+  const int L = rec.size(0), B = slots.numel(), Hv = rec.size(2);
+  if (B == 0) return;
+  at::Tensor k = keys.to(at::kFloat).contiguous(), d = deltas.to(at::kFloat).contiguous(),
+             g = gs.to(at::kFloat).contiguous();
+  at::Tensor sl = slots.to(at::kInt).contiguous(), ln = lens.to(at::kInt).contiguous();
+  replay_commit_kernel<<<dim3(Hv, B, L), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      rec.data_ptr<float>(), rec.size(1), sl.data_ptr<int>(), k.data_ptr<float>(), d.data_ptr<float>(),
+      g.data_ptr<float>(), ln.data_ptr<int>(), int(steps), B, Hv);
+}
+
+void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& slots, const at::Tensor& bounds,
+                     int64_t steps) {
+  TORCH_CHECK(conv.dim() == 4 && hist.dim() == 4, "conv pool [L,S,C,3], history [L,rows,C,3]");
+  const int L = conv.size(0), B = slots.numel();
+  if (B == 0) return;
+  at::Tensor sl = slots.to(at::kInt).contiguous(), bd = bounds.to(at::kInt).contiguous();
+  at::Tensor h = hist.contiguous();
+  conv_commit_kernel<<<dim3(B, L), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(conv.data_ptr()), conv.size(1),
+      reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), h.size(1), sl.data_ptr<int>(), bd.data_ptr<int>(),
+      int(steps), int(conv.size(2) * conv.size(3)));
+}
+
+}  // namespace isb

@@ -1,0 +1,588 @@
+// tcgen05 GEMM for sm_100a: C = A[M,K] . B[N,K]^T, bf16 inputs, fp32 accumulation in TMEM.
+//
+// Structure (one output tile per CTA, 192 threads):
+//   warp 0      TMA producer: 128x64 "P" tile + BNx64 "Q" tile per stage into
+//               128-byte-swizzled shared memory, mbarrier complete_tx.
+//   warp 1      TMEM allocator + MMA issuer: 4 x tcgen05.mma (K=16) per stage,
+//               tcgen05.commit releases the stage / signals the accumulator.
+//   warps 2..5  epilogue: tcgen05.ld 32 lanes x 32 columns per warp, fused
+//               epilogue (plain store | SiLU(gate)*up | LM-head argmax with
+//               Gumbel-max sampling).
+// Operand roles: the 128-row MMA "M" side (P) is the activation matrix for
+// large token counts and the WEIGHT matrix for <= 128 tokens (swap-AB), so a
+// decode GEMM streams weights through the 128-lane tensor-core tile while the
+// handful of tokens form the MMA N dimension.
+// Split-K: gridDim.z CTAs of a thread-block cluster each own a K range; the
+// partial accumulators are reduced through distributed shared memory by the
+// cluster's rank-0 CTA (no global scratch, deterministic order).
+// No TMA multicast is used anywhere in this file.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <cudaTypedefs.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace isb {
+
+__device__ unsigned int g_gemm_err;
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int STAGES = BN <= 32 ? 8 : (BN <= 128 ? 6 : 4);
+  static constexpr int P_BYTES = BM * BK * 2;
+  static constexpr int Q_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = P_BYTES + Q_BYTES;
+  static constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+  static constexpr int RED_STRIDE = BN + 4;
+  static constexpr int BAR_BYTES = 256;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + BAR_BYTES;
+  static_assert(BM * RED_STRIDE * 4 + 64 * RED_STRIDE * 4 <= STAGES * STAGE_BYTES || BN > 128,
+                "split-K / SiLU staging must fit in the stage buffers");
+};
+
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kArgmax = 2 };
+
+struct GemmArgs {
+  __nv_bfloat16* out;      // kStore / kSiluMul output
+  int P_rows, Q_rows, K;
+  int ldo;                 // output row stride (elements)
+  int kb_per_split;
+  // kArgmax
+  const float* temps;      // [tokens]
+  const int* rng;          // [seed, step]
+  float* part_val;         // [num_vocab_tiles, tokens]
+  int* part_idx;
+  int vocab_offset;
+};
+
+ISB_DEVICE uint32_t fmix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x85EBCA6Bu;
+  h ^= h >> 13;
+  h *= 0xC2B2AE35u;
+  h ^= h >> 16;
+  return h;
+}
+
+// Counter-based uniform noise; identical to ``ops.uniform_noise`` on the host.
+ISB_DEVICE float gumbel_noise(int seed, int step, int row, int col) {
+  const uint32_t key = uint32_t(seed) * 0x9E3779B1u + uint32_t(step) * 0x85EBCA77u;
+  uint32_t h = fmix32(uint32_t(row) * 0x27D4EB2Fu + key);
+  h = fmix32(h ^ (uint32_t(col) * 0x165667B1u));
+  const float u = (float(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+
+template <int BN, bool SWAP, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ, GemmArgs args) {
+  using Cfg = GemmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);
+  uint64_t* empty = full + Cfg::STAGES;
+  uint64_t* acc_full = empty + Cfg::STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tile_p = blockIdx.x, tile_q = blockIdx.y;
+  const int kb_total = (args.K + BK - 1) / BK;
+  const int kb_begin = blockIdx.z * args.kb_per_split;
+  const int kb_end = min(kb_total, kb_begin + args.kb_per_split);
+  const int nkb = max(kb_end - kb_begin, 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmP);
+    prefetch_tmap(&tmQ);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % Cfg::STAGES;
+        const uint32_t ph = (i / Cfg::STAGES) & 1;
+        if (!mbar_wait(&empty[s], ph ^ 1)) { atomicOr(&g_gemm_err, 1u); break; }
+        uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
+        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+        const int kx = (kb_begin + i) * BK;
+        tma_load_2d(sp, &tmP, &full[s], kx, tile_p * BM);
+        tma_load_2d(sp + Cfg::P_BYTES, &tmQ, &full[s], kx, tile_q * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int s = i % Cfg::STAGES;
+        const uint32_t ph = (i / Cfg::STAGES) & 1;
+        if (!mbar_wait(&full[s], ph)) { atomicOr(&g_gemm_err, 2u); break; }
+        tc_fence_after();
+        uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
+        const uint64_t pd = smem_desc_sw128(sp);
+        const uint64_t qd = smem_desc_sw128(sp + Cfg::P_BYTES);
+#pragma unroll
+        for (int k = 0; k < BK / 16; ++k) {
+          // advance 16 bf16 = 32 bytes inside the swizzle atom: +2 in the >>4 address field
+          mma_bf16(tmem, pd + 2 * k, qd + 2 * k, idesc, (i > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&empty[s]);
+      }
+      mma_commit(acc_full);
+    }
+  }
+
+  // ------------------------------------------------------------ epilogue
+  const bool epi = warp >= 2;
+  const int quarter = warp & 3;           // TMEM lane quarter this warp may access
+  const int row = quarter * 32 + lane;    // row of the P tile == TMEM lane
+  const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
+  const uint32_t nranks = cluster_nctarank();
+  const uint32_t rank = cluster_ctarank();
+  float* red = reinterpret_cast<float*>(smem);                 // [BM][RED_STRIDE] partials
+  float* xbuf = red + BM * Cfg::RED_STRIDE;                    // [64][RED_STRIDE] SiLU exchange
+  constexpr int CH = BN < 32 ? 16 : 32;
+
+  bool acc_ok = true;
+  if (epi) {
+    acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
+    if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 4u);
+    tc_fence_after();
+  }
+
+  auto load_chunk = [&](int c, float* v) {
+    if (!acc_ok) {
+#pragma unroll
+      for (int j = 0; j < CH; ++j) v[j] = 0.f;
+      return;
+    }
+    if constexpr (CH == 16) tmem_ld16(lane_addr + c * CH, v); else tmem_ld32(lane_addr + c * CH, v);
+  };
+
+  if (nranks > 1) {
+    if (epi && rank != 0) {
+      for (int c = 0; c < BN / CH; ++c) {
+        float v[CH];
+        load_chunk(c, v);
+        float4* dst = reinterpret_cast<float4*>(red + row * Cfg::RED_STRIDE + c * CH);
+#pragma unroll
+        for (int j = 0; j < CH / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      }
+    }
+    cluster_sync();
+  }
+
+  if (epi && (nranks == 1 || rank == 0)) {
+    const int p0 = tile_p * BM, q0 = tile_q * BN;
+    // Row-wise SiLU pairs in swap mode: rows >= 64 (up) hand their values to rows < 64 (gate).
+    for (int c = 0; c < BN / CH; ++c) {
+      if constexpr (EPI == kSiluMul && !SWAP) {
+        if ((c * CH) % 128 >= 64) continue;  // up chunks are consumed with their gate chunk
+      }
+      float v[CH];
+      load_chunk(c, v);
+      for (uint32_t r = 1; r < nranks; ++r) {
+        const uint32_t a = mapa_shared(smem_u32(red + row * Cfg::RED_STRIDE + c * CH), r);
+#pragma unroll
+        for (int j = 0; j < CH / 4; ++j) {
+          const float4 w = ld_dsmem_f4(a + 16 * j);
+          v[4 * j] += w.x; v[4 * j + 1] += w.y; v[4 * j + 2] += w.z; v[4 * j + 3] += w.w;
+        }
+      }
+      if constexpr (EPI == kStore) {
+        if constexpr (SWAP) {
+          const int f = p0 + row;
+          if (f < args.P_rows) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int t = q0 + c * CH + j;
+              if (t < args.Q_rows) args.out[size_t(t) * args.ldo + f] = __float2bfloat16(v[j]);
+            }
+          }
+        } else {
+          const int t = p0 + row;
+          const int col0 = q0 + c * CH;
+          if (t < args.P_rows) {
+            __nv_bfloat16* o = args.out + size_t(t) * args.ldo + col0;
+            if (col0 + CH <= args.Q_rows && (args.ldo % 8) == 0) {
+#pragma unroll
+              for (int j = 0; j < CH / 8; ++j) {
+                uint4 pk;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+                reinterpret_cast<uint4*>(o)[j] = pk;
+              }
+            } else {
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (col0 + j < args.Q_rows) o[j] = __float2bfloat16(v[j]);
+            }
+          }
+        }
+      } else if constexpr (EPI == kSiluMul) {
+        if constexpr (SWAP) {
+          // gate rows 0..63, up rows 64..127 of this weight tile
+          if (row >= 64) {
+#pragma unroll
+            for (int j = 0; j < CH; ++j) xbuf[(row - 64) * Cfg::RED_STRIDE + c * CH + j] = v[j];
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (row < 64) {
+            const int f = tile_p * 64 + row;
+            if (f < args.P_rows / 2) {
+#pragma unroll
+              for (int j = 0; j < CH; ++j) {
+                const int t = q0 + c * CH + j;
+                const float u = xbuf[row * Cfg::RED_STRIDE + c * CH + j];
+                if (t < args.Q_rows) args.out[size_t(t) * args.ldo + f] = __float2bfloat16(silu(v[j]) * u);
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        } else {
+          // columns [g*128, g*128+64) gate, [g*128+64, g*128+128) up; handle gate chunks, fetch up chunks
+          const int within = (c * CH) % 128;
+          if (within < 64) {
+            float u[CH];
+            load_chunk(c + 64 / CH, u);
+            for (uint32_t r = 1; r < nranks; ++r) {
+              const uint32_t a = mapa_shared(smem_u32(red + row * Cfg::RED_STRIDE + c * CH + 64), r);
+#pragma unroll
+              for (int j = 0; j < CH / 4; ++j) {
+                const float4 w = ld_dsmem_f4(a + 16 * j);
+                u[4 * j] += w.x; u[4 * j + 1] += w.y; u[4 * j + 2] += w.z; u[4 * j + 3] += w.w;
+              }
+            }
+            const int t = p0 + row;
+            const int g = (c * CH) / 128;
+            const int col0 = q0 / 2 + g * 64 + within;
+            if (t < args.P_rows) {
+#pragma unroll
+              for (int j = 0; j < CH; ++j)
+                if (col0 + j < args.Q_rows / 2)
+                  args.out[size_t(t) * args.ldo + col0 + j] = __float2bfloat16(silu(v[j]) * u[j]);
+            }
+          }
+        }
+      } else {  // kArgmax: LM head fused with greedy / Gumbel-max selection
+        const int seed = args.rng[0], step = args.rng[1];
+        if constexpr (SWAP) {
+          // rows = vocab entries, columns = tokens: reduce over rows per column
+          const int vrow = p0 + row;
+          const bool valid = vrow < args.P_rows;
+          float* sval = xbuf;                                   // [4 warps][BN]
+          int* sidx = reinterpret_cast<int*>(xbuf + 4 * BN);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            const int t = q0 + c * CH + j;
+            float s = -INFINITY;
+            if (valid && t < args.Q_rows) {
+              const float temp = args.temps[t];
+              s = v[j];
+              if (temp > 1e-10f) s = s / temp + gumbel_noise(seed, step, t, args.vocab_offset + vrow);
+            }
+            int bi = vrow;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const float os = __shfl_xor_sync(0xffffffffu, s, o);
+              const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+              if (os > s || (os == s && oi < bi)) { s = os; bi = oi; }
+            }
+            if (lane == 0) { sval[quarter * BN + c * CH + j] = s; sidx[quarter * BN + c * CH + j] = bi; }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          for (int j = threadIdx.x - 64; j < CH; j += 128) {
+            const int col = c * CH + j;
+            const int t = q0 + col;
+            float s = sval[col];
+            int bi = sidx[col];
+            for (int w = 1; w < 4; ++w) {
+              const float os = sval[w * BN + col];
+              const int oi = sidx[w * BN + col];
+              if (os > s || (os == s && oi < bi)) { s = os; bi = oi; }
+            }
+            if (t < args.Q_rows) {
+              args.part_val[size_t(tile_p) * args.Q_rows + t] = s;
+              args.part_idx[size_t(tile_p) * args.Q_rows + t] = bi;
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        } else {
+          // rows = tokens, columns = vocab: thread-local reduction, then combine chunks in registers
+          const int t = p0 + row;
+          if (t < args.P_rows) {
+            const float temp = args.temps[t];
+            float best = -INFINITY;
+            int bi = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < CH; ++j) {
+              const int vcol = q0 + c * CH + j;
+              if (vcol < args.Q_rows) {
+                float s = v[j];
+                if (temp > 1e-10f) s = s / temp + gumbel_noise(seed, step, t, args.vocab_offset + vcol);
+                if (s > best) { best = s; bi = vcol; }
+              }
+            }
+            // chunk partials are merged across chunks through the partial buffer slot of this tile
+            const size_t slot = size_t(tile_q) * args.P_rows + t;
+            if (c == 0 || best > args.part_val[slot] || (best == args.part_val[slot] && bi < args.part_idx[slot])) {
+              args.part_val[slot] = best;
+              args.part_idx[slot] = bi;
+            }
+          }
+        }
+      }
+    }
+  }
+  if (nranks > 1) cluster_sync();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+// Second stage of the fused LM-head selection: best (score, index) over vocab tiles.
+__global__ void argmax_tiles_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int ntiles, int tokens,
+                                    int vocab_offset, float* __restrict__ out_val, int* __restrict__ out_idx) {
+  const int t = blockIdx.x;
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
+    const float s = pv[size_t(i) * tokens + t];
+    const int ix = pi[size_t(i) * tokens + t];
+    if (s > best || (s == best && ix < bi)) { best = s; bi = ix; }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (os > best || (os == best && oi < bi)) { best = os; bi = oi; }
+  }
+  if ((threadIdx.x & 31) == 0) { sv[threadIdx.x >> 5] = best; si[threadIdx.x >> 5] = bi; }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < int(blockDim.x >> 5); ++w)
+      if (sv[w] > best || (sv[w] == best && si[w] < bi)) { best = sv[w]; bi = si[w]; }
+    out_val[t] = best;
+    out_idx[t] = bi + vocab_offset;
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    TORCH_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+                    q == cudaDriverEntryPointSuccess && p,
+                "cannot resolve cuTensorMapEncodeTiled");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 K-major map: dims {K, rows}, box {64, box_rows}, 128-byte swizzle, zero OOB fill.
+CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", int(r));
+  return m;
+}
+
+template <int BN, bool SWAP, int EPI>
+static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a, int tiles_p, int tiles_q, int splits,
+                        cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, SWAP, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess);
+    attr = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(tiles_p, tiles_q, splits);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Cfg::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = 1;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = splits;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tp, tq, a);
+  TORCH_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e));
+}
+
+static int pick_bn_swap(int tokens) {
+  if (tokens <= 16) return 16;
+  if (tokens <= 32) return 32;
+  if (tokens <= 64) return 64;
+  return 128;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+// Choose the split-K factor (cluster size) so that the grid covers the SMs.
+static int pick_splits(int tiles, int kb_total, int max_split = 8) {
+  int s = 1;
+  const int sms = num_sms();
+  while (s < max_split && tiles * (s * 2) <= sms + sms / 2 && kb_total / (s * 2) >= 2) s *= 2;
+  return s;
+}
+
+template <int EPI, bool SWAP>
+static void dispatch_bn(int bn, const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a, int tp_, int tq_, int s,
+                        cudaStream_t st) {
+  switch (bn) {
+    case 16: launch_gemm<16, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
+    case 32: launch_gemm<32, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
+    case 64: launch_gemm<64, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
+    case 128: launch_gemm<128, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
+    default: TORCH_CHECK(false, "unsupported tile width");
+  }
+}
+
+struct Plan {
+  bool swap;
+  int bn, tiles_p, tiles_q, splits, kb_per;
+  CUtensorMap tp, tq;
+};
+
+static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split) {
+  const int M = a.size(0), K = a.size(1), N = b.size(0);
+  Plan p;
+  p.swap = M <= 128;
+  const int kb_total = (K + BK - 1) / BK;
+  if (p.swap) {
+    p.bn = pick_bn_swap(M);
+    p.tiles_p = (N + BM - 1) / BM;
+    p.tiles_q = (M + p.bn - 1) / p.bn;
+    p.tp = make_kmajor_map(b.data_ptr(), N, K, BM);
+    p.tq = make_kmajor_map(a.data_ptr(), M, K, p.bn);
+  } else {
+    p.bn = 256;
+    p.tiles_p = (M + BM - 1) / BM;
+    p.tiles_q = (N + 255) / 256;
+    p.tp = make_kmajor_map(a.data_ptr(), M, K, BM);
+    p.tq = make_kmajor_map(b.data_ptr(), N, K, 256);
+  }
+  int s = allow_split ? pick_splits(p.tiles_p * p.tiles_q, kb_total) : 1;
+  p.kb_per = (kb_total + s - 1) / s;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  return p;
+}
+
+static void check_operands(const at::Tensor& a, const at::Tensor& b) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "gemm operands must be CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm expects bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "gemm shape mismatch");
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous(), "gemm operands must be contiguous");
+  TORCH_CHECK(a.size(1) % 8 == 0, "K must be a multiple of 8 (16-byte TMA row stride)");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              "gemm operands must be 16-byte aligned");
+}
+
+at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm: unknown epilogue");
+  const int out_cols = epilogue == kSiluMul ? N / 2 : N;
+  at::Tensor out = at::empty({M, out_cols}, a.options());
+  if (M == 0) return out;
+  Plan p = plan_gemm(a, b, true);
+  GemmArgs args = {};
+  args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  args.K = a.size(1);
+  args.ldo = out_cols;
+  args.kb_per_split = p.kb_per;
+  if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (epilogue == kStore) {
+    if (p.swap) dispatch_bn<kStore, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+    else launch_gemm<256, false, kStore>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+  } else {
+    TORCH_CHECK(N % 128 == 0 || !p.swap, "packed gate/up rows must be a multiple of 128");
+    if (p.swap) dispatch_bn<kSiluMul, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+    else launch_gemm<256, false, kSiluMul>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
+  return out;
+}
+
+std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const at::Tensor& w, const at::Tensor& temps,
+                                                  const at::Tensor& rng, int64_t vocab_offset) {
+  at::Tensor h = h_in.contiguous();
+  check_operands(h, w);
+  TORCH_CHECK(temps.scalar_type() == at::kFloat && rng.scalar_type() == at::kInt, "temps fp32 / rng int32");
+  const int B = h.size(0), V = w.size(0);
+  at::Tensor val = at::empty({B}, h.options().dtype(at::kFloat));
+  at::Tensor idx = at::empty({B}, h.options().dtype(at::kInt));
+  if (B == 0) return {val, idx};
+  Plan p = plan_gemm(h, w, false);
+  const int vtiles = p.swap ? p.tiles_p : p.tiles_q;
+  at::Tensor pv = at::empty({vtiles, B}, val.options());
+  at::Tensor pi = at::empty({vtiles, B}, idx.options());
+  GemmArgs args = {};
+  args.K = h.size(1);
+  args.kb_per_split = p.kb_per;
+  args.temps = temps.data_ptr<float>();
+  args.rng = rng.data_ptr<int>();
+  args.part_val = pv.data_ptr<float>();
+  args.part_idx = pi.data_ptr<int>();
+  args.vocab_offset = int(vocab_offset);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.swap) {
+    args.P_rows = V; args.Q_rows = B;
+    dispatch_bn<kArgmax, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, 1, st);
+  } else {
+    args.P_rows = B; args.Q_rows = V;
+    launch_gemm<256, false, kArgmax>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, 1, st);
+  }
+  argmax_tiles_kernel<<<B, 256, 0, st>>>(pv.data_ptr<float>(), pi.data_ptr<int>(), vtiles, B, int(vocab_offset),
+                                         val.data_ptr<float>(), idx.data_ptr<int>());
+  return {val, idx};
+}
+
+int64_t gemm_error_word() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gemm_err, sizeof(v));
+  const unsigned int z = 0;
+  cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(z));
+  return v;
+}
+
+}  // namespace isb

@@ -1,0 +1,113 @@
+// Operator registry of the sm_100a kernel library: ``torch.ops.isb.*``.
+//
+// Parity: the reference registers its CUDA ops with ``TORCH_LIBRARY(nanovllm)``
+// (``nanovllm/csrc/ops.cpp:48-80``); this library exposes the kernels of this
+// engine the same way so they are graph-capturable torch ops.
+
+#include <torch/extension.h>
+
+namespace isb {
+at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t epilogue);
+std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h, const at::Tensor& w, const at::Tensor& temps,
+                                                  const at::Tensor& rng, int64_t vocab_offset);
+int64_t gemm_error_word();
+at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& w, double eps, bool zc);
+at::Tensor add_rmsnorm(const at::Tensor& x, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
+std::tuple<at::Tensor, at::Tensor> embed_rmsnorm(const at::Tensor& ids, const at::Tensor& table, const at::Tensor& w,
+                                                 double eps, bool zc);
+at::Tensor embed(const at::Tensor& ids, const at::Tensor& table, int64_t vocab_start);
+at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
+                      const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk,
+                      int64_t hv, int64_t dk, int64_t dv, double eps);
+at::Tensor gdn_prefill(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                       const at::Tensor& conv_w, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                       const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv, int64_t dk,
+                       int64_t dv, double eps, int64_t max_seqlen);
+at::Tensor gdn_scan_history(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                            const at::Tensor& conv_w, const at::Tensor& A_log, const at::Tensor& dt_bias,
+                            const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv,
+                            double eps, bool write_final, const c10::optional<at::Tensor>& hist_row,
+                            c10::optional<at::Tensor> hist_rec, c10::optional<at::Tensor> hist_conv,
+                            c10::optional<at::Tensor> rec_k, c10::optional<at::Tensor> rec_delta,
+                            c10::optional<at::Tensor> rec_g);
+void gdn_replay_commit(at::Tensor rec, const at::Tensor& slots, const at::Tensor& keys, const at::Tensor& deltas,
+                       const at::Tensor& gs, const at::Tensor& lens, int64_t steps);
+void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& slots, const at::Tensor& bounds,
+                     int64_t steps);
+at::Tensor attn_prepare(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slot_mapping,
+                        const at::Tensor& qn, const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
+                        at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps, bool gated, bool zc);
+at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+                            const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated);
+at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+                             const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
+                             double scale, bool gated, int64_t max_seqlen_q);
+void quantize_state_int8(const at::Tensor& state, at::Tensor q, at::Tensor scale);
+void dequantize_state_int8(const at::Tensor& q, const at::Tensor& scale, at::Tensor out);
+void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_t n);
+
+int64_t error_word() { return gemm_error_word(); }
+}  // namespace isb
+
+TORCH_LIBRARY(isb, m) {
+  m.def("gemm(Tensor a, Tensor b, int epilogue) -> Tensor");
+  m.def("lm_head_sample(Tensor hidden, Tensor weight, Tensor temps, Tensor rng, int vocab_offset) -> (Tensor, Tensor)");
+  m.def("rmsnorm(Tensor x, Tensor w, float eps, bool zero_centered) -> Tensor");
+  m.def("add_rmsnorm(Tensor x, Tensor(a!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
+  m.def("embed_rmsnorm(Tensor ids, Tensor table, Tensor w, float eps, bool zero_centered) -> (Tensor, Tensor)");
+  m.def("embed(Tensor ids, Tensor table, int vocab_start) -> Tensor");
+  m.def(
+      "gdn_decode(Tensor proj, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
+      "Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps) -> Tensor");
+  m.def(
+      "gdn_prefill(Tensor proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
+      "Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps, int max_seqlen) "
+      "-> Tensor");
+  m.def(
+      "gdn_scan_history(Tensor proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
+      "Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, float eps, bool write_final, "
+      "Tensor? hist_row, Tensor(c!)? hist_rec, Tensor(d!)? hist_conv, Tensor(e!)? rec_k, Tensor(f!)? rec_delta, "
+      "Tensor(g!)? rec_g) -> Tensor");
+  m.def(
+      "gdn_replay_commit(Tensor(a!) rec, Tensor slots, Tensor keys, Tensor deltas, Tensor gs, Tensor lens, "
+      "int steps) -> ()");
+  m.def("gdn_conv_commit(Tensor(a!) conv, Tensor hist, Tensor slots, Tensor bounds, int steps) -> ()");
+  m.def(
+      "attn_prepare(Tensor qkv, Tensor positions, Tensor slot_mapping, Tensor qn, Tensor kn, Tensor cos_sin, "
+      "Tensor(a!) k_cache, Tensor(b!) v_cache, int Hq, int Hkv, int hd, float eps, bool gated, bool zero_centered) "
+      "-> Tensor");
+  m.def(
+      "attention_decode(Tensor q, Tensor qkv, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
+      "Tensor block_tables, float scale, bool gated) -> Tensor");
+  m.def(
+      "attention_prefill(Tensor q, Tensor qkv, Tensor k_cache, Tensor v_cache, Tensor cu_seqlens_q, "
+      "Tensor context_lens, Tensor block_tables, float scale, bool gated, int max_seqlen_q) -> Tensor");
+  m.def("quantize_state_int8(Tensor state, Tensor(a!) q, Tensor(b!) scale) -> ()");
+  m.def("dequantize_state_int8(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
+  m.def("copy_kv_page(Tensor(a!) k_cache, Tensor(b!) v_cache, int src, int dst, int n) -> ()");
+  m.def("error_word() -> int");
+}
+
+TORCH_LIBRARY_IMPL(isb, CUDA, m) {
+  m.impl("gemm", &isb::gemm);
+  m.impl("lm_head_sample", &isb::lm_head_sample);
+  m.impl("rmsnorm", &isb::rmsnorm);
+  m.impl("add_rmsnorm", &isb::add_rmsnorm);
+  m.impl("embed_rmsnorm", &isb::embed_rmsnorm);
+  m.impl("embed", &isb::embed);
+  m.impl("gdn_decode", &isb::gdn_decode);
+  m.impl("gdn_prefill", &isb::gdn_prefill);
+  m.impl("gdn_scan_history", &isb::gdn_scan_history);
+  m.impl("gdn_replay_commit", &isb::gdn_replay_commit);
+  m.impl("gdn_conv_commit", &isb::gdn_conv_commit);
+  m.impl("attn_prepare", &isb::attn_prepare);
+  m.impl("attention_decode", &isb::attention_decode);
+  m.impl("attention_prefill", &isb::attention_prefill);
+  m.impl("quantize_state_int8", &isb::quantize_state_int8);
+  m.impl("dequantize_state_int8", &isb::dequantize_state_int8);
+  m.impl("copy_kv_page", &isb::copy_kv_page);
+}
+
+TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) { m.impl("error_word", &isb::error_word); }
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "sm_100a kernels (torch.ops.isb)"; }
