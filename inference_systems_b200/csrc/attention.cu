@@ -34,13 +34,6 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float* v) {
   }
 }
 
-__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* p, const float* v) {
-  uint4 raw;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = raw;
-}
 
 // ------------------------------------------------------------------ prepare
 // One warp per (token, head); HD/32 channels per lane (HD in {128, 256}).
@@ -121,7 +114,26 @@ __global__ void attn_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int q
 }
 
 // ------------------------------------------------------------------ decode
-// grid (Hkv, B, pages); 256 threads. Partials: m, l, o[G][HD] per (b, hq, page).
+// grid (Hkv, B, chunks of 64 tokens); 256 threads (8 warps).
+//   The chunk's K and V rows (contiguous inside a page) are pulled into shared
+//   memory with two bulk asynchronous copies completing on one mbarrier, so a
+//   CTA keeps 2 x 64 x HD x 2 bytes in flight with no per-thread address math.
+//   phase 1: half-warps compute q.k for the whole GQA group (16-lane shuffles;
+//            the loop is warp-uniform so every lane reaches every shuffle)
+//   phase 2: warp g computes max / exp / sum for head g
+//   phase 3: warp w owns HD/8 output channels and accumulates p * v over the chunk
+// Partials (o[G][HD], m, l) per (sequence, q head, chunk) are merged by attn_combine_kernel.
+constexpr int DCHUNK = 64;
+
+__device__ unsigned int g_attn_err;
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 template <int HD, int G>
 __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* __restrict__ q,
                                                           const __nv_bfloat16* __restrict__ kc,
@@ -129,123 +141,137 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
                                                           const int* __restrict__ ctx_lens,
                                                           const int* __restrict__ block_tables, int max_blocks,
                                                           int Hkv, float scale, float* __restrict__ part_o,
-                                                          float* __restrict__ part_ml, int max_pages) {
-  __shared__ float q_s[G][HD];
-  __shared__ float p_s[G][PAGE];
-  __shared__ float red[8][G];
-  const int kvh = blockIdx.x, b = blockIdx.y, page = blockIdx.z;
+                                                          float* __restrict__ part_ml, int max_chunks) {
+  constexpr int ED = HD / 16;   // channels per lane in phase 1
+  constexpr int DW = HD / 8;    // output channels per warp in phase 3
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __nv_bfloat16* k_s = reinterpret_cast<__nv_bfloat16*>(dsm_raw);   // [64][HD]
+  __nv_bfloat16* v_s = k_s + DCHUNK * HD;                            // [64][HD]
+  float* q_s = reinterpret_cast<float*>(v_s + DCHUNK * HD);          // [G][HD]
+  float* s_s = q_s + G * HD;                                         // [G][64]
+  __shared__ uint64_t bar;
+  __shared__ float m_s[G], l_s[G];
+  const int kvh = blockIdx.x, b = blockIdx.y, chunk = blockIdx.z;
   const int ctx = ctx_lens[b];
-  const int start = page * PAGE;
+  const int start = chunk * DCHUNK;
   const int Hq = Hkv * G;
-  const size_t pidx = (size_t(b) * Hq + kvh * G) * max_pages + page;  // + g * max_pages
+  const size_t pidx = (size_t(b) * Hq + kvh * G) * max_chunks + chunk;  // + g * max_chunks
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (start >= ctx) {
-    if (threadIdx.x < G) {
-      part_ml[(pidx + threadIdx.x * max_pages) * 2 + 0] = -INFINITY;
-      part_ml[(pidx + threadIdx.x * max_pages) * 2 + 1] = 0.f;
+    if (tid < G) {
+      part_ml[(pidx + tid * max_chunks) * 2 + 0] = -INFINITY;
+      part_ml[(pidx + tid * max_chunks) * 2 + 1] = 0.f;
     }
     return;
   }
-  const int n = min(PAGE, ctx - start);
-  const int blk = block_tables[b * max_blocks + page];
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  for (int i = tid; i < G * HD; i += 256) {
-    const int g = i / HD, d = i % HD;
-    q_s[g][d] = __bfloat162float(q[(size_t(b) * Hq + kvh * G + g) * HD + d]) * scale;
+  const int n = min(DCHUNK, ctx - start);
+  const int blk = block_tables[b * max_blocks + start / PAGE];
+  const size_t row0 = (size_t(blk) * Hkv + kvh) * PAGE + start % PAGE;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
-  const __nv_bfloat16* K = kc + (size_t(blk) * Hkv + kvh) * PAGE * HD;
-  const __nv_bfloat16* V = vcache + (size_t(blk) * Hkv + kvh) * PAGE * HD;
-  constexpr int E = HD / 32;
-  // scores: each warp handles tokens warp, warp+8, ...; a lane holds E channels
-  for (int t = warp; t < n; t += 8) {
-    float kv[E];
-    if constexpr (E == 8) load_bf16x8(K + size_t(t) * HD + lane * E, kv);
-    else {
+  if (tid == 0) {
+    const uint32_t bytes = uint32_t(n) * HD * 2;
+    mbar_arrive_expect_tx(&bar, 2 * bytes);
+    bulk_g2s(k_s, kc + row0 * HD, bytes, &bar);
+    bulk_g2s(v_s, vcache + row0 * HD, bytes, &bar);
+  }
+  for (int i = tid; i < G * HD; i += 256) q_s[i] = __bfloat162float(q[(size_t(b) * Hq + kvh * G) * HD + i]) * scale;
+  __syncthreads();
+  if (!mbar_wait(&bar, 0)) atomicOr(&g_attn_err, 1u);
+  // ---- phase 1: scores
+  {
+    const int hl = lane & 15;
+    for (int t0 = warp * 2; t0 < n; t0 += 16) {
+      const int t = t0 + (lane >> 4);
+      const bool valid = t < n;
+      float kv[ED];
 #pragma unroll
-      for (int i = 0; i < E; ++i) kv[i] = __bfloat162float(K[size_t(t) * HD + lane * E + i]);
+      for (int j = 0; j < ED / 8; ++j) {
+        if (valid) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(k_s + t * HD + hl * ED + j * 8);
+          const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h2[e]);
+            kv[j * 8 + 2 * e] = f.x;
+            kv[j * 8 + 2 * e + 1] = f.y;
+          }
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) kv[j * 8 + e] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const float4* qv = reinterpret_cast<const float4*>(q_s + g * HD + hl * ED);
+        float sacc = 0.f;
+#pragma unroll
+        for (int j = 0; j < ED / 4; ++j) {
+          const float4 qq = qv[j];
+          sacc += qq.x * kv[4 * j] + qq.y * kv[4 * j + 1] + qq.z * kv[4 * j + 2] + qq.w * kv[4 * j + 3];
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
+        if (valid && hl == 0) s_s[g * DCHUNK + t] = sacc;
+      }
     }
-#pragma unroll
-    for (int g = 0; g < G; ++g) {
-      float s = 0.f;
-#pragma unroll
-      for (int i = 0; i < E; ++i) s += q_s[g][lane * E + i] * kv[i];
-      s = warp_sum(s);
-      if (lane == 0) p_s[g][t] = s;
-    }
   }
   __syncthreads();
-  // softmax partial per head
-  float mloc[G], lsum[G];
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = -INFINITY;
-    for (int t = tid; t < n; t += 256) m = fmaxf(m, p_s[g][t]);
-    m = warp_max(m);
-    if (lane == 0) red[warp][g] = m;
+  // ---- phase 2: warp g owns head g (G <= 8)
+  if (warp < G) {
+    const int g = warp;
+    const float a0 = lane < n ? s_s[g * DCHUNK + lane] : -INFINITY;
+    const float a1 = lane + 32 < n ? s_s[g * DCHUNK + lane + 32] : -INFINITY;
+    const float m = warp_max(fmaxf(a0, a1));
+    const float e0 = lane < n ? __expf(a0 - m) : 0.f;
+    const float e1 = lane + 32 < n ? __expf(a1 - m) : 0.f;
+    s_s[g * DCHUNK + lane] = e0;
+    s_s[g * DCHUNK + lane + 32] = e1;
+    const float l = warp_sum(e0 + e1);
+    if (lane == 0) { m_s[g] = m; l_s[g] = l; }
   }
   __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float m = red[0][g];
-    for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w][g]);
-    mloc[g] = m;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = 0.f;
-    for (int t = tid; t < n; t += 256) {
-      const float e = __expf(p_s[g][t] - mloc[g]);
-      p_s[g][t] = e;
-      l += e;
-    }
-    l = warp_sum(l);
-    if (lane == 0) red[warp][g] = l;
-  }
-  __syncthreads();
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    float l = 0.f;
-    for (int w = 0; w < 8; ++w) l += red[w][g];
-    lsum[g] = l;
-  }
-  // P V: thread owns HD/256... channels: for HD=256 one channel per thread
-  for (int d = tid; d < HD; d += 256) {
+  // ---- phase 3: P V, warp w owns channels [w*DW, (w+1)*DW)
+  if (lane < DW) {
+    const int d = warp * DW + lane;
     float acc[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) acc[g] = 0.f;
     for (int t = 0; t < n; ++t) {
-      const float vv = __bfloat162float(V[size_t(t) * HD + d]);
+      const float vv = __bfloat162float(v_s[t * HD + d]);
 #pragma unroll
-      for (int g = 0; g < G; ++g) acc[g] += p_s[g][t] * vv;
+      for (int g = 0; g < G; ++g) acc[g] += s_s[g * DCHUNK + t] * vv;
     }
 #pragma unroll
-    for (int g = 0; g < G; ++g) part_o[(pidx + g * max_pages) * HD + d] = acc[g];
+    for (int g = 0; g < G; ++g) part_o[(pidx + g * max_chunks) * HD + d] = acc[g];
   }
   if (tid < G) {
-    part_ml[(pidx + tid * max_pages) * 2 + 0] = mloc[tid];
-    part_ml[(pidx + tid * max_pages) * 2 + 1] = lsum[tid];
+    part_ml[(pidx + tid * max_chunks) * 2 + 0] = m_s[tid];
+    part_ml[(pidx + tid * max_chunks) * 2 + 1] = l_s[tid];
   }
 }
 
-// grid (Hq, B); HD threads. Merges page partials, applies the output gate.
+// grid (Hq, B); HD threads. Merges chunk partials, applies the output gate.
 template <int HD>
-__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_pages,
-                                    const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ qkv,
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_chunks,
+                                    int chunk, const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ qkv,
                                     int qkv_stride, bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = ctx_lens[b];
-  const int pages = (ctx + PAGE - 1) / PAGE;
-  const size_t base = (size_t(b) * Hq + h) * max_pages;
+  const int chunks = (ctx + chunk - 1) / chunk;
+  const size_t base = (size_t(b) * Hq + h) * max_chunks;
   float m = -INFINITY;
-  for (int p = 0; p < pages; ++p) m = fmaxf(m, part_ml[(base + p) * 2]);
+  for (int p = 0; p < chunks; ++p) m = fmaxf(m, part_ml[(base + p) * 2]);
   float l = 0.f, acc = 0.f;
-  for (int p = 0; p < pages; ++p) {
+  for (int p = 0; p < chunks; ++p) {
     const float w = __expf(part_ml[(base + p) * 2] - m);
     l += w * part_ml[(base + p) * 2 + 1];
     acc += w * part_o[(base + p) * HD + d];
   }
-  float o = pages > 0 && l > 0.f ? acc / l : 0.f;
+  float o = chunks > 0 && l > 0.f ? acc / l : 0.f;
   if (gated) {
     const float gt = __bfloat162float(qkv[size_t(b) * qkv_stride + h * 2 * HD + HD + d]);
     o *= sigmoidf_(gt);
@@ -410,41 +436,58 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at
                             const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated) {
   const int B = q.size(0), Hq = q.size(1), hd = q.size(2);
   check_cache(kc, vc, hd);
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == at::kBFloat16, "q must be contiguous bf16");
+  TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && block_tables.scalar_type() == at::kInt, "int32 metadata");
   const int Hkv = kc.size(1);
   const int G = Hq / Hkv;
   const int max_blocks = block_tables.size(1);
   at::Tensor out = at::empty({B, Hq * hd}, q.options());
   if (B == 0) return out;
-  const int max_pages = max_blocks;
-  at::Tensor part_o = at::empty({B, Hq, max_pages, hd}, q.options().dtype(at::kFloat));
-  at::Tensor part_ml = at::empty({B, Hq, max_pages, 2}, q.options().dtype(at::kFloat));
+  const int max_chunks = max_blocks * (PAGE / DCHUNK);
+  at::Tensor part_o = at::empty({B, Hq, max_chunks, hd}, q.options().dtype(at::kFloat));
+  at::Tensor part_ml = at::empty({B, Hq, max_chunks, 2}, q.options().dtype(at::kFloat));
   auto st = at::cuda::getCurrentCUDAStream();
-  const dim3 grid(Hkv, B, max_pages);
-#define ISB_DEC(HD_, G_)                                                                                             \
-  attn_decode_kernel<HD_, G_><<<grid, 256, 0, st>>>(                                                                 \
-      reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()), \
-      reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), ctx_lens.data_ptr<int>(), block_tables.data_ptr<int>(), \
-      max_blocks, Hkv, float(scale), part_o.data_ptr<float>(), part_ml.data_ptr<float>(), max_pages)
-  if (hd == 256 && G == 4) ISB_DEC(256, 4);
-  else if (hd == 256 && G == 2) ISB_DEC(256, 2);
-  else if (hd == 256 && G == 6) ISB_DEC(256, 6);
-  else if (hd == 256 && G == 3) ISB_DEC(256, 3);
-  else if (hd == 256 && G == 8) ISB_DEC(256, 8);
-  else if (hd == 256 && G == 1) ISB_DEC(256, 1);
-  else if (hd == 128 && G == 2) ISB_DEC(128, 2);
-  else if (hd == 128 && G == 1) ISB_DEC(128, 1);
-  else if (hd == 128 && G == 4) ISB_DEC(128, 4);
-  else TORCH_CHECK(false, "attention_decode: unsupported (head_dim, group) = (", hd, ", ", G, ")");
-#undef ISB_DEC
+  const dim3 grid(Hkv, B, max_chunks);
+  bool launched = false;
+  auto launch = [&](auto hd_c, auto g_c) {
+    constexpr int HD_ = decltype(hd_c)::value, G_ = decltype(g_c)::value;
+    if (hd != HD_ || G != G_ || launched) return;
+    const int smem = 2 * DCHUNK * HD_ * 2 + (G_ * HD_ + G_ * DCHUNK) * 4;
+    auto kern = attn_decode_kernel<HD_, G_>;
+    static bool attr = false;
+    if (!attr) {
+      TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess);
+      attr = true;
+    }
+    kern<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+                                  reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()),
+                                  reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), ctx_lens.data_ptr<int>(),
+                                  block_tables.data_ptr<int>(), max_blocks, Hkv, float(scale),
+                                  part_o.data_ptr<float>(), part_ml.data_ptr<float>(), max_chunks);
+    launched = true;
+  };
+#define ISB_DEC_G(HD_, G_) launch(std::integral_constant<int, HD_>{}, std::integral_constant<int, G_>{});
+  ISB_DEC_G(256, 1) ISB_DEC_G(256, 2) ISB_DEC_G(256, 3) ISB_DEC_G(256, 4) ISB_DEC_G(256, 6) ISB_DEC_G(256, 8)
+  ISB_DEC_G(128, 1) ISB_DEC_G(128, 2) ISB_DEC_G(128, 4)
+#undef ISB_DEC_G
+  TORCH_CHECK(launched, "attention_decode: unsupported (head_dim, group) = (", hd, ", ", G, ")");
 #define ISB_COMB(HD_)                                                                                              \
   attn_combine_kernel<HD_><<<dim3(Hq, B), HD_, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),       \
-                                                       max_pages, ctx_lens.data_ptr<int>(),                          \
+                                                       max_chunks, DCHUNK, ctx_lens.data_ptr<int>(),                  \
                                                        reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),       \
                                                        qkv.size(1), gated,                                           \
                                                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), Hq)
   if (hd == 256) ISB_COMB(256); else ISB_COMB(128);
 #undef ISB_COMB
   return out;
+}
+
+int64_t attn_error_word() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_attn_err, sizeof(v));
+  const unsigned int z = 0;
+  cudaMemcpyToSymbol(g_attn_err, &z, sizeof(z));
+  return v;
 }
 
 at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,

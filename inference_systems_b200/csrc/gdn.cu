@@ -293,7 +293,7 @@ ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Te
   a.eps = float(eps);
   a.write_final = true;
   TORCH_CHECK(a.C == 2 * hk * D + hv * D, "conv pool channel count mismatch");
-  TORCH_CHECK(proj.size(1) == a.C + hv * D + 2 * hv, "projection width mismatch");
+  TORCH_CHECK(proj.size(1) >= a.C + hv * D + 2 * hv, "projection width mismatch");
   TORCH_CHECK(conv_w.scalar_type() == at::kBFloat16 && conv_w.size(0) == a.C && conv_w.size(1) == KW, "conv weight");
   TORCH_CHECK(A_log.scalar_type() == at::kFloat && dt_bias.scalar_type() == at::kFloat, "A_log/dt_bias must be fp32");
   TORCH_CHECK(slots.scalar_type() == at::kInt, "slots must be int32");

@@ -58,7 +58,17 @@ struct GemmArgs {
   float* part_val;         // [num_vocab_tiles, tokens]
   int* part_idx;
   int vocab_offset;
+  unsigned long long* dbg;  // optional per-CTA phase timestamps [ctas][8] (diagnostics)
+  float* ws;                // split-K partials [tiles][splits][BM][BN] fp32
+  unsigned int* counters;   // split-K arrival counters (self-resetting)
 };
+
+// Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
+// slices (round-robin on the host) so consecutive split-K GEMMs never share
+// counters; the last CTA of a tile resets its counter to zero.
+constexpr int kCounterSlots = 8;
+constexpr int kCountersPerSlot = 8192;
+__device__ unsigned int g_splitk_counters[kCounterSlots * kCountersPerSlot];
 
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
   h ^= h >> 16;
@@ -80,7 +90,8 @@ ISB_DEVICE float gumbel_noise(int seed, int step, int row, int col) {
 
 template <int BN, bool SWAP, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ, GemmArgs args) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                   const __grid_constant__ CUtensorMap tmO, GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -95,6 +106,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int kb_begin = blockIdx.z * args.kb_per_split;
   const int kb_end = min(kb_total, kb_begin + args.kb_per_split);
   const int nkb = max(kb_end - kb_begin, 0);
+  const size_t cta_id = (size_t(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  unsigned long long* dbg = args.dbg ? args.dbg + cta_id * 8 : nullptr;
+  if (dbg && threadIdx.x == 0) dbg[0] = globaltimer_ns();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
@@ -105,16 +119,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmP);
     prefetch_tmap(&tmQ);
+    if constexpr (SWAP && (EPI == kStore || EPI == kSiluMul)) prefetch_tmap(&tmO);
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (dbg && threadIdx.x == 0) dbg[1] = globaltimer_ns();
 
   if (warp == 0) {
     if (lane == 0) {
       for (int i = 0; i < nkb; ++i) {
+        if (dbg && i == 0) dbg[2] = globaltimer_ns();
         const int s = i % Cfg::STAGES;
         const uint32_t ph = (i / Cfg::STAGES) & 1;
         if (!mbar_wait(&empty[s], ph ^ 1)) { atomicOr(&g_gemm_err, 1u); break; }
@@ -132,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % Cfg::STAGES;
         const uint32_t ph = (i / Cfg::STAGES) & 1;
         if (!mbar_wait(&full[s], ph)) { atomicOr(&g_gemm_err, 2u); break; }
+        if (dbg && i == 0) dbg[3] = globaltimer_ns();
         tc_fence_after();
         uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
         const uint64_t pd = smem_desc_sw128(sp);
@@ -143,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mma_commit(&empty[s]);
       }
+      if (dbg) dbg[4] = globaltimer_ns();
       mma_commit(acc_full);
     }
   }
@@ -152,124 +171,119 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int quarter = warp & 3;           // TMEM lane quarter this warp may access
   const int row = quarter * 32 + lane;    // row of the P tile == TMEM lane
   const uint32_t lane_addr = tmem + (uint32_t(quarter * 32) << 16);
-  const uint32_t nranks = cluster_nctarank();
-  const uint32_t rank = cluster_ctarank();
-  float* red = reinterpret_cast<float*>(smem);                 // [BM][RED_STRIDE] partials
-  float* xbuf = red + BM * Cfg::RED_STRIDE;                    // [64][RED_STRIDE] SiLU exchange
+  const int nsplit = gridDim.z;
+  const int tile_id = tile_p * gridDim.y + tile_q;
   constexpr int CH = BN < 32 ? 16 : 32;
+  // shared-memory regions reused after the mainloop (every MMA has completed)
+  float* xbuf = reinterpret_cast<float*>(smem);                                  // [64][RED_STRIDE]
+  constexpr int XBUF_BYTES = ((64 * Cfg::RED_STRIDE * 4) + 1023) / 1024 * 1024;
+  __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(smem + XBUF_BYTES);  // [BN][128] bf16
+  __shared__ int s_last;
 
-  bool acc_ok = true;
   if (epi) {
-    acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
+    bool acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
     if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 4u);
     tc_fence_after();
-  }
+    if (dbg && threadIdx.x == 64) dbg[5] = globaltimer_ns();
 
-  auto load_chunk = [&](int c, float* v) {
-    if (!acc_ok) {
+    auto load_chunk = [&](int c, float* v) {
+      if (!acc_ok) {
 #pragma unroll
-      for (int j = 0; j < CH; ++j) v[j] = 0.f;
-      return;
-    }
-    if constexpr (CH == 16) tmem_ld16(lane_addr + c * CH, v); else tmem_ld32(lane_addr + c * CH, v);
-  };
+        for (int j = 0; j < CH; ++j) v[j] = 0.f;
+        return;
+      }
+      if constexpr (CH == 16) tmem_ld16(lane_addr + c * CH, v); else tmem_ld32(lane_addr + c * CH, v);
+    };
 
-  if (nranks > 1) {
-    if (epi && rank != 0) {
+    // ---- split-K: publish the fp32 partial to L2; the last CTA of the tile reduces
+    bool reduce_here = true;
+    if (nsplit > 1) {
+      // column-major partial [BN][BM]: a warp's 32 rows of one column are 128 contiguous bytes
+      float* mine = args.ws + (size_t(tile_id) * nsplit + blockIdx.z) * BN * BM + row;
       for (int c = 0; c < BN / CH; ++c) {
         float v[CH];
         load_chunk(c, v);
-        float4* dst = reinterpret_cast<float4*>(red + row * Cfg::RED_STRIDE + c * CH);
 #pragma unroll
-        for (int j = 0; j < CH / 4; ++j) dst[j] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+        for (int j = 0; j < CH; ++j) __stcg(mine + size_t(c * CH + j) * BM, v[j]);
       }
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        unsigned int* cnt = args.counters + tile_id;
+        const unsigned int old = atomicAdd(cnt, 1u);
+        s_last = old == unsigned(nsplit - 1);
+        if (s_last) *cnt = 0u;  // every split has arrived: reset for the next launch
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      reduce_here = s_last != 0;
+      if (reduce_here) __threadfence();
     }
-    cluster_sync();
-  }
 
-  if (epi && (nranks == 1 || rank == 0)) {
-    const int p0 = tile_p * BM, q0 = tile_q * BN;
-    // Row-wise SiLU pairs in swap mode: rows >= 64 (up) hand their values to rows < 64 (gate).
-    for (int c = 0; c < BN / CH; ++c) {
-      if constexpr (EPI == kSiluMul && !SWAP) {
-        if ((c * CH) % 128 >= 64) continue;  // up chunks are consumed with their gate chunk
-      }
-      float v[CH];
-      load_chunk(c, v);
-      for (uint32_t r = 1; r < nranks; ++r) {
-        const uint32_t a = mapa_shared(smem_u32(red + row * Cfg::RED_STRIDE + c * CH), r);
-#pragma unroll
-        for (int j = 0; j < CH / 4; ++j) {
-          const float4 w = ld_dsmem_f4(a + 16 * j);
-          v[4 * j] += w.x; v[4 * j + 1] += w.y; v[4 * j + 2] += w.z; v[4 * j + 3] += w.w;
+    if (reduce_here) {
+      const int p0 = tile_p * BM, q0 = tile_q * BN;
+      for (int c = 0; c < BN / CH; ++c) {
+        if constexpr (EPI == kSiluMul && !SWAP) {
+          if ((c * CH) % 128 >= 64) continue;  // up chunks are consumed with their gate chunk
         }
-      }
-      if constexpr (EPI == kStore) {
-        if constexpr (SWAP) {
-          const int f = p0 + row;
-          if (f < args.P_rows) {
+        float v[CH];
+        load_chunk(c, v);
+        auto add_partials = [&](float* acc, int col0) {
+          for (int z = 0; z < nsplit; ++z) {
+            if (z == int(blockIdx.z)) continue;
+            const float* src = args.ws + (size_t(tile_id) * nsplit + z) * BN * BM + size_t(col0) * BM + row;
 #pragma unroll
-            for (int j = 0; j < CH; ++j) {
-              const int t = q0 + c * CH + j;
-              if (t < args.Q_rows) args.out[size_t(t) * args.ldo + f] = __float2bfloat16(v[j]);
-            }
+            for (int j = 0; j < CH; ++j) acc[j] += __ldcg(src + size_t(j) * BM);
           }
-        } else {
-          const int t = p0 + row;
-          const int col0 = q0 + c * CH;
-          if (t < args.P_rows) {
-            __nv_bfloat16* o = args.out + size_t(t) * args.ldo + col0;
-            if (col0 + CH <= args.Q_rows && (args.ldo % 8) == 0) {
+        };
+        if (nsplit > 1) add_partials(v, c * CH);
+        if constexpr (EPI == kStore) {
+          if constexpr (SWAP) {
+            // transpose through shared memory: ostage[token][feature]
 #pragma unroll
-              for (int j = 0; j < CH / 8; ++j) {
-                uint4 pk;
-                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+            for (int j = 0; j < CH; ++j) ostage[(c * CH + j) * BM + row] = __float2bfloat16(v[j]);
+          } else {
+            const int t = p0 + row;
+            const int col0 = q0 + c * CH;
+            if (t < args.P_rows) {
+              __nv_bfloat16* o = args.out + size_t(t) * args.ldo + col0;
+              if (col0 + CH <= args.Q_rows && (args.ldo % 8) == 0) {
 #pragma unroll
-                for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
-                reinterpret_cast<uint4*>(o)[j] = pk;
+                for (int j = 0; j < CH / 8; ++j) {
+                  uint4 pk;
+                  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+                  reinterpret_cast<uint4*>(o)[j] = pk;
+                }
+              } else {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                  if (col0 + j < args.Q_rows) o[j] = __float2bfloat16(v[j]);
               }
-            } else {
-#pragma unroll
-              for (int j = 0; j < CH; ++j)
-                if (col0 + j < args.Q_rows) o[j] = __float2bfloat16(v[j]);
             }
           }
-        }
-      } else if constexpr (EPI == kSiluMul) {
-        if constexpr (SWAP) {
-          // gate rows 0..63, up rows 64..127 of this weight tile
-          if (row >= 64) {
+        } else if constexpr (EPI == kSiluMul) {
+          if constexpr (SWAP) {
+            // gate rows 0..63, up rows 64..127 of this weight tile
+            if (row >= 64) {
 #pragma unroll
-            for (int j = 0; j < CH; ++j) xbuf[(row - 64) * Cfg::RED_STRIDE + c * CH + j] = v[j];
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (row < 64) {
-            const int f = tile_p * 64 + row;
-            if (f < args.P_rows / 2) {
+              for (int j = 0; j < CH; ++j) xbuf[(row - 64) * Cfg::RED_STRIDE + c * CH + j] = v[j];
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (row < 64) {
 #pragma unroll
               for (int j = 0; j < CH; ++j) {
-                const int t = q0 + c * CH + j;
                 const float u = xbuf[row * Cfg::RED_STRIDE + c * CH + j];
-                if (t < args.Q_rows) args.out[size_t(t) * args.ldo + f] = __float2bfloat16(silu(v[j]) * u);
+                ostage[(c * CH + j) * 64 + row] = __float2bfloat16(silu(v[j]) * u);
               }
             }
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-        } else {
-          // columns [g*128, g*128+64) gate, [g*128+64, g*128+128) up; handle gate chunks, fetch up chunks
-          const int within = (c * CH) % 128;
-          if (within < 64) {
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          } else {
             float u[CH];
             load_chunk(c + 64 / CH, u);
-            for (uint32_t r = 1; r < nranks; ++r) {
-              const uint32_t a = mapa_shared(smem_u32(red + row * Cfg::RED_STRIDE + c * CH + 64), r);
-#pragma unroll
-              for (int j = 0; j < CH / 4; ++j) {
-                const float4 w = ld_dsmem_f4(a + 16 * j);
-                u[4 * j] += w.x; u[4 * j + 1] += w.y; u[4 * j + 2] += w.z; u[4 * j + 3] += w.w;
-              }
-            }
+            if (nsplit > 1) add_partials(u, c * CH + 64);
             const int t = p0 + row;
+            const int within = (c * CH) % 128;
             const int g = (c * CH) / 128;
             const int col0 = q0 / 2 + g * 64 + within;
             if (t < args.P_rows) {
@@ -279,81 +293,93 @@ __global__ void __launch_bounds__(kThreads, 1)
                   args.out[size_t(t) * args.ldo + col0 + j] = __float2bfloat16(silu(v[j]) * u[j]);
             }
           }
-        }
-      } else {  // kArgmax: LM head fused with greedy / Gumbel-max selection
-        const int seed = args.rng[0], step = args.rng[1];
-        if constexpr (SWAP) {
-          // rows = vocab entries, columns = tokens: reduce over rows per column
-          const int vrow = p0 + row;
-          const bool valid = vrow < args.P_rows;
-          float* sval = xbuf;                                   // [4 warps][BN]
-          int* sidx = reinterpret_cast<int*>(xbuf + 4 * BN);
-#pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            const int t = q0 + c * CH + j;
-            float s = -INFINITY;
-            if (valid && t < args.Q_rows) {
-              const float temp = args.temps[t];
-              s = v[j];
-              if (temp > 1e-10f) s = s / temp + gumbel_noise(seed, step, t, args.vocab_offset + vrow);
-            }
-            int bi = vrow;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-              const float os = __shfl_xor_sync(0xffffffffu, s, o);
-              const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-              if (os > s || (os == s && oi < bi)) { s = os; bi = oi; }
-            }
-            if (lane == 0) { sval[quarter * BN + c * CH + j] = s; sidx[quarter * BN + c * CH + j] = bi; }
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          for (int j = threadIdx.x - 64; j < CH; j += 128) {
-            const int col = c * CH + j;
-            const int t = q0 + col;
-            float s = sval[col];
-            int bi = sidx[col];
-            for (int w = 1; w < 4; ++w) {
-              const float os = sval[w * BN + col];
-              const int oi = sidx[w * BN + col];
-              if (os > s || (os == s && oi < bi)) { s = os; bi = oi; }
-            }
-            if (t < args.Q_rows) {
-              args.part_val[size_t(tile_p) * args.Q_rows + t] = s;
-              args.part_idx[size_t(tile_p) * args.Q_rows + t] = bi;
-            }
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-        } else {
-          // rows = tokens, columns = vocab: thread-local reduction, then combine chunks in registers
-          const int t = p0 + row;
-          if (t < args.P_rows) {
-            const float temp = args.temps[t];
-            float best = -INFINITY;
-            int bi = 0x7fffffff;
+        } else {  // kArgmax: LM head fused with greedy / Gumbel-max selection
+          const int seed = args.rng[0], step = args.rng[1];
+          if constexpr (SWAP) {
+            const int vrow = p0 + row;
+            const bool valid = vrow < args.P_rows;
+            float* sval = xbuf;                                   // [4 warps][BN]
+            int* sidx = reinterpret_cast<int*>(xbuf + 4 * BN);
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
-              const int vcol = q0 + c * CH + j;
-              if (vcol < args.Q_rows) {
-                float s = v[j];
-                if (temp > 1e-10f) s = s / temp + gumbel_noise(seed, step, t, args.vocab_offset + vcol);
-                if (s > best) { best = s; bi = vcol; }
+              const int t = q0 + c * CH + j;
+              float sc = -INFINITY;
+              if (valid && t < args.Q_rows) {
+                const float temp = args.temps[t];
+                sc = v[j];
+                if (temp > 1e-10f) sc = sc / temp + gumbel_noise(seed, step, t, args.vocab_offset + vrow);
+              }
+              int bi = vrow;
+#pragma unroll
+              for (int o = 16; o > 0; o >>= 1) {
+                const float os = __shfl_xor_sync(0xffffffffu, sc, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (os > sc || (os == sc && oi < bi)) { sc = os; bi = oi; }
+              }
+              if (lane == 0) { sval[quarter * BN + c * CH + j] = sc; sidx[quarter * BN + c * CH + j] = bi; }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int j = threadIdx.x - 64; j < CH; j += 128) {
+              const int col = c * CH + j;
+              const int t = q0 + col;
+              float sc = sval[col];
+              int bi = sidx[col];
+              for (int w = 1; w < 4; ++w) {
+                const float os = sval[w * BN + col];
+                const int oi = sidx[w * BN + col];
+                if (os > sc || (os == sc && oi < bi)) { sc = os; bi = oi; }
+              }
+              if (t < args.Q_rows) {
+                args.part_val[size_t(tile_p) * args.Q_rows + t] = sc;
+                args.part_idx[size_t(tile_p) * args.Q_rows + t] = bi;
               }
             }
-            // chunk partials are merged across chunks through the partial buffer slot of this tile
-            const size_t slot = size_t(tile_q) * args.P_rows + t;
-            if (c == 0 || best > args.part_val[slot] || (best == args.part_val[slot] && bi < args.part_idx[slot])) {
-              args.part_val[slot] = best;
-              args.part_idx[slot] = bi;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+          } else {
+            const int t = p0 + row;
+            if (t < args.P_rows) {
+              const float temp = args.temps[t];
+              float best = -INFINITY;
+              int bi = 0x7fffffff;
+#pragma unroll
+              for (int j = 0; j < CH; ++j) {
+                const int vcol = q0 + c * CH + j;
+                if (vcol < args.Q_rows) {
+                  float sc = v[j];
+                  if (temp > 1e-10f) sc = sc / temp + gumbel_noise(seed, step, t, args.vocab_offset + vcol);
+                  if (sc > best) { best = sc; bi = vcol; }
+                }
+              }
+              const size_t slot = size_t(tile_q) * args.P_rows + t;
+              if (c == 0 || best > args.part_val[slot] || (best == args.part_val[slot] && bi < args.part_idx[slot])) {
+                args.part_val[slot] = best;
+                args.part_idx[slot] = bi;
+              }
             }
           }
         }
       }
+      // swap-AB stores leave through one TMA tensor store of the staged tile
+      if constexpr (SWAP && (EPI == kStore || EPI == kSiluMul)) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) {
+          const int x0 = EPI == kSiluMul ? tile_p * 64 : tile_p * BM;
+          asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                           reinterpret_cast<uint64_t>(&tmO)),
+                       "r"(x0), "r"(q0), "r"(smem_u32(ostage))
+                       : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+        }
+      }
     }
   }
-  if (nranks > 1) cluster_sync();
+  if (dbg && threadIdx.x == 64) dbg[6] = globaltimer_ns();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  if (dbg && threadIdx.x == 0) dbg[7] = globaltimer_ns();
 }
 
 // Second stage of the fused LM-head selection: best (score, index) over vocab tiles.
@@ -414,8 +440,8 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int box_ro
 }
 
 template <int BN, bool SWAP, int EPI>
-static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a, int tiles_p, int tiles_q, int splits,
-                        cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& to, GemmArgs a, int tiles_p,
+                        int tiles_q, int splits, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<BN, SWAP, EPI>;
   static bool attr = false;
@@ -423,20 +449,23 @@ static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a
     TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess);
     attr = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(tiles_p, tiles_q, splits);
-  cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = Cfg::SMEM;
-  cfg.stream = stream;
-  cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = 1;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = splits;
-  cfg.attrs = at;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tp, tq, a);
+  kern<<<dim3(tiles_p, tiles_q, splits), kThreads, Cfg::SMEM, stream>>>(tp, tq, to, a);
+  const cudaError_t e = cudaGetLastError();
   TORCH_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e));
+}
+
+// 2-D bf16 row-major output map for the swap-AB TMA store: dims {cols, rows}, box {box_cols, box_rows}.
+static CUtensorMap make_store_map(const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * 2};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed: ", int(r));
+  return m;
 }
 
 static int pick_bn_swap(int tokens) {
@@ -456,22 +485,35 @@ static int num_sms() {
   return n;
 }
 
-// Choose the split-K factor (cluster size) so that the grid covers the SMs.
+// Split-K factor: grow while the grid stays within ~1.5 waves and every split keeps >= 2 k-blocks.
 static int pick_splits(int tiles, int kb_total, int max_split = 8) {
   int s = 1;
   const int sms = num_sms();
-  while (s < max_split && tiles * (s * 2) <= sms + sms / 2 && kb_total / (s * 2) >= 2) s *= 2;
+  while (s < max_split && tiles * (s * 2) <= 2 * sms && kb_total / (s * 2) >= 2) s *= 2;
   return s;
 }
 
+static unsigned int* counter_slot() {
+  static unsigned int* base[64] = {};
+  static unsigned int next = 0;
+  int dev;
+  cudaGetDevice(&dev);
+  if (!base[dev]) {
+    void* p = nullptr;
+    TORCH_CHECK(cudaGetSymbolAddress(&p, g_splitk_counters) == cudaSuccess, "split-K counters unavailable");
+    base[dev] = static_cast<unsigned int*>(p);
+  }
+  return base[dev] + (next++ % kCounterSlots) * kCountersPerSlot;
+}
+
 template <int EPI, bool SWAP>
-static void dispatch_bn(int bn, const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a, int tp_, int tq_, int s,
-                        cudaStream_t st) {
+static void dispatch_bn(int bn, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& to, GemmArgs a,
+                        int tp_, int tq_, int s, cudaStream_t st) {
   switch (bn) {
-    case 16: launch_gemm<16, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
-    case 32: launch_gemm<32, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
-    case 64: launch_gemm<64, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
-    case 128: launch_gemm<128, SWAP, EPI>(tp, tq, a, tp_, tq_, s, st); break;
+    case 16: launch_gemm<16, SWAP, EPI>(tp, tq, to, a, tp_, tq_, s, st); break;
+    case 32: launch_gemm<32, SWAP, EPI>(tp, tq, to, a, tp_, tq_, s, st); break;
+    case 64: launch_gemm<64, SWAP, EPI>(tp, tq, to, a, tp_, tq_, s, st); break;
+    case 128: launch_gemm<128, SWAP, EPI>(tp, tq, to, a, tp_, tq_, s, st); break;
     default: TORCH_CHECK(false, "unsupported tile width");
   }
 }
@@ -482,7 +524,7 @@ struct Plan {
   CUtensorMap tp, tq;
 };
 
-static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split) {
+static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split, int force_splits = 0) {
   const int M = a.size(0), K = a.size(1), N = b.size(0);
   Plan p;
   p.swap = M <= 128;
@@ -501,8 +543,10 @@ static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split
     p.tq = make_kmajor_map(b.data_ptr(), N, K, 256);
   }
   int s = allow_split ? pick_splits(p.tiles_p * p.tiles_q, kb_total) : 1;
+  if (force_splits > 0) s = std::min(force_splits, kb_total);
   p.kb_per = (kb_total + s - 1) / s;
   p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  TORCH_CHECK(p.tiles_p * p.tiles_q <= kCountersPerSlot || p.splits == 1, "too many split-K tiles");
   return p;
 }
 
@@ -516,31 +560,64 @@ static void check_operands(const at::Tensor& a, const at::Tensor& b) {
               "gemm operands must be 16-byte aligned");
 }
 
-at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue) {
-  at::Tensor a = a_in.contiguous();
-  check_operands(a, b);
+// Shared launch path of the plain and SiLU-mul GEMMs.
+static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int epilogue, int force_splits,
+                     unsigned long long* dbg) {
   const int M = a.size(0), N = b.size(0);
-  TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm: unknown epilogue");
-  const int out_cols = epilogue == kSiluMul ? N / 2 : N;
-  at::Tensor out = at::empty({M, out_cols}, a.options());
-  if (M == 0) return out;
-  Plan p = plan_gemm(a, b, true);
+  const int out_cols = out.size(1);
+  Plan p = plan_gemm(a, b, true, force_splits);
   GemmArgs args = {};
   args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   args.K = a.size(1);
   args.ldo = out_cols;
   args.kb_per_split = p.kb_per;
+  args.dbg = dbg;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  at::Tensor ws;
+  if (p.splits > 1) {
+    ws = at::empty({int64_t(p.tiles_p) * p.tiles_q * p.splits * BM * p.bn}, a.options().dtype(at::kFloat));
+    args.ws = ws.data_ptr<float>();
+    args.counters = counter_slot();
+  }
+  CUtensorMap to = p.tp;
+  if (p.swap) {
+    TORCH_CHECK(out_cols % 8 == 0, "swap-AB GEMM output width must be a multiple of 8 (16-byte rows)");
+    to = make_store_map(out.data_ptr(), M, out_cols, epilogue == kSiluMul ? 64 : BM, p.bn);
+  }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (epilogue == kStore) {
-    if (p.swap) dispatch_bn<kStore, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
-    else launch_gemm<256, false, kStore>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+    if (p.swap) dispatch_bn<kStore, true>(p.bn, p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
+    else launch_gemm<256, false, kStore>(p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
   } else {
     TORCH_CHECK(N % 128 == 0 || !p.swap, "packed gate/up rows must be a multiple of 128");
-    if (p.swap) dispatch_bn<kSiluMul, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
-    else launch_gemm<256, false, kSiluMul>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st);
+    if (p.swap) dispatch_bn<kSiluMul, true>(p.bn, p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
+    else launch_gemm<256, false, kSiluMul>(p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
   }
+}
+
+at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, int64_t splits) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm: unknown epilogue");
+  at::Tensor out = at::empty({M, epilogue == kSiluMul ? N / 2 : N}, a.options());
+  if (M == 0) return out;
+  run_gemm(a, b, out, int(epilogue), int(splits), nullptr);
   return out;
+}
+
+// Diagnostics: run the plain GEMM and return per-CTA phase timestamps (ns, %globaltimer):
+// [entry, setup done, first TMA issued, first stage landed, last MMA issued, accumulator ready,
+//  epilogue done, exit].
+at::Tensor gemm_timeline(const at::Tensor& a_in, const at::Tensor& b, int64_t splits) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  at::Tensor out = at::empty({M, N}, a.options());
+  Plan p = plan_gemm(a, b, true, int(splits));
+  at::Tensor ts = at::zeros({int64_t(p.tiles_p) * p.tiles_q * p.splits, 8}, a.options().dtype(at::kLong));
+  run_gemm(a, b, out, kStore, int(splits), reinterpret_cast<unsigned long long*>(ts.data_ptr()));
+  return ts;
 }
 
 std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const at::Tensor& w, const at::Tensor& temps,
@@ -567,10 +644,10 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const 
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (p.swap) {
     args.P_rows = V; args.Q_rows = B;
-    dispatch_bn<kArgmax, true>(p.bn, p.tp, p.tq, args, p.tiles_p, p.tiles_q, 1, st);
+    dispatch_bn<kArgmax, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
   } else {
     args.P_rows = B; args.Q_rows = V;
-    launch_gemm<256, false, kArgmax>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, 1, st);
+    launch_gemm<256, false, kArgmax>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
   }
   argmax_tiles_kernel<<<B, 256, 0, st>>>(pv.data_ptr<float>(), pi.data_ptr<int>(), vtiles, B, int(vocab_offset),
                                          val.data_ptr<float>(), idx.data_ptr<int>());

@@ -7,10 +7,11 @@
 #include <torch/extension.h>
 
 namespace isb {
-at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t epilogue);
+at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t epilogue, int64_t splits);
 std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h, const at::Tensor& w, const at::Tensor& temps,
                                                   const at::Tensor& rng, int64_t vocab_offset);
 int64_t gemm_error_word();
+at::Tensor gemm_timeline(const at::Tensor& a, const at::Tensor& b, int64_t splits);
 at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& w, double eps, bool zc);
 at::Tensor add_rmsnorm(const at::Tensor& x, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
 std::tuple<at::Tensor, at::Tensor> embed_rmsnorm(const at::Tensor& ids, const at::Tensor& table, const at::Tensor& w,
@@ -46,11 +47,13 @@ void quantize_state_int8(const at::Tensor& state, at::Tensor q, at::Tensor scale
 void dequantize_state_int8(const at::Tensor& q, const at::Tensor& scale, at::Tensor out);
 void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_t n);
 
-int64_t error_word() { return gemm_error_word(); }
+int64_t attn_error_word();
+
+int64_t error_word() { return gemm_error_word() | (attn_error_word() << 8); }
 }  // namespace isb
 
 TORCH_LIBRARY(isb, m) {
-  m.def("gemm(Tensor a, Tensor b, int epilogue) -> Tensor");
+  m.def("gemm(Tensor a, Tensor b, int epilogue, int splits=0) -> Tensor");
   m.def("lm_head_sample(Tensor hidden, Tensor weight, Tensor temps, Tensor rng, int vocab_offset) -> (Tensor, Tensor)");
   m.def("rmsnorm(Tensor x, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("add_rmsnorm(Tensor x, Tensor(a!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
@@ -86,6 +89,7 @@ TORCH_LIBRARY(isb, m) {
   m.def("dequantize_state_int8(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
   m.def("copy_kv_page(Tensor(a!) k_cache, Tensor(b!) v_cache, int src, int dst, int n) -> ()");
   m.def("error_word() -> int");
+  m.def("gemm_timeline(Tensor a, Tensor b, int splits) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(isb, CUDA, m) {
@@ -106,6 +110,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("quantize_state_int8", &isb::quantize_state_int8);
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);
   m.impl("copy_kv_page", &isb::copy_kv_page);
+  m.impl("gemm_timeline", &isb::gemm_timeline);
 }
 
 TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) { m.impl("error_word", &isb::error_word); }

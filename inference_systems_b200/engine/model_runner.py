@@ -40,6 +40,20 @@ from inference_systems_b200.utils.context import ForwardBatch
 from inference_systems_b200.utils.loader import init_dummy, load_model
 
 
+def count_graph_kernels(handle: int) -> int:
+    """Number of kernel nodes in a captured CUDA graph (-1 if the bindings are unavailable)."""
+    try:
+        from cuda.bindings import runtime as rt
+
+        graph = rt.cudaGraph_t(init_value=handle)
+        err, _, n = rt.cudaGraphGetNodes(graph, 0)
+        err, nodes, n = rt.cudaGraphGetNodes(graph, n)
+        kernel = rt.cudaGraphNodeType.cudaGraphNodeTypeKernel
+        return sum(1 for node in nodes if rt.cudaGraphNodeGetType(node)[1] == kernel)
+    except Exception:  # pragma: no cover - depends on cuda-python
+        return -1
+
+
 def _bucket_sizes(max_bs: int) -> list[int]:
     sizes = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512]
     out = [s for s in sizes if s < max_bs] + [max_bs]
@@ -120,6 +134,7 @@ class ModelRunner:
         self.sample_step = 0
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_bufs: dict[int, dict] = {}
+        self.graph_kernels: dict[int, int] = {}
         if self.device.type == "cuda" and not self.enforce_eager:
             self.capture_cudagraph()
         if self.mtp is not None:
@@ -368,11 +383,13 @@ class ModelRunner:
             # warm up (kernel autotuning / lazy init) outside the capture
             self._forward_sample(batch, rng, temps)
             torch.cuda.synchronize(self.device)
-            g = torch.cuda.CUDAGraph()
+            g = torch.cuda.CUDAGraph(keep_graph=True)
             with torch.cuda.graph(g, pool=pool):
                 toks = self._forward_sample(batch, rng, temps)
+            g.instantiate()
             if pool is None:
                 pool = g.pool()
+            self.graph_kernels[bs_] = count_graph_kernels(g.raw_cuda_graph())
             self.graphs[bs_] = g
             self.graph_bufs[bs_] = {"meta": meta_dev, "tokens": toks, "layout": layout}
         torch.cuda.synchronize(self.device)
@@ -466,6 +483,34 @@ class ModelRunner:
         if self.mtp is not None:
             m["mtp"] = self.mtp_driver.metrics()
         return m
+
+    # ============================================================ bench
+    @torch.inference_mode()
+    def bench_replay(self, batch_size: int, warmup: int, steps: int) -> float:
+        """Device time (ms, max over ranks) of ``steps`` back-to-back decode-graph replays."""
+        g = self.graphs[self._graph_bucket(batch_size)]
+        for _ in range(warmup):
+            g.replay()
+        if self.world_size > 1:
+            dist.barrier()
+        torch.cuda.synchronize(self.device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(self.device)
+        if self.world_size > 1:
+            dist.barrier()
+        ms = e0.elapsed_time(e1)
+        if self.world_size > 1:
+            t = torch.tensor([ms], device=self.device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+        return ms
+
+    def graph_kernel_count(self, batch_size: int) -> int:
+        return self.graph_kernels.get(self._graph_bucket(batch_size), -1)
 
     # ====================================================== speculative
     def run_speculative(self, seqs: list[Sequence]):

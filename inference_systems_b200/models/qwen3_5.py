@@ -133,7 +133,9 @@ class GDNMixer(nn.Module):
         self.key_dim, self.value_dim = self.hk * self.dk, self.hv * self.dv
         self.conv_dim = 2 * self.key_dim + self.value_dim
         self.proj_width = self.conv_dim + self.value_dim + 2 * self.hv
-        self.in_proj = nn.Parameter(torch.empty(self.proj_width, h), requires_grad=False)
+        # rows padded to a multiple of 64 so every projection row is 16-byte aligned for TMA
+        self.proj_rows = (self.proj_width + 63) // 64 * 64
+        self.in_proj = nn.Parameter(torch.empty(self.proj_rows, h), requires_grad=False)
         self.conv_w = nn.Parameter(torch.empty(self.conv_dim, self.kernel), requires_grad=False)
         self.A_log = nn.Parameter(torch.empty(self.hv, dtype=torch.float32), requires_grad=False)
         self.dt_bias = nn.Parameter(torch.empty(self.hv, dtype=torch.float32), requires_grad=False)
@@ -157,7 +159,9 @@ class GDNMixer(nn.Module):
             z = _rows(get(keys[1]), tp.rank, tp.size)
             b = _rows(get(keys[2]), tp.rank, tp.size)
             a = _rows(get(keys[3]), tp.rank, tp.size)
-            return torch.cat((qkv, z, b, a), 0)
+            w = torch.cat((qkv, z, b, a), 0)
+            pad = self.proj_rows - w.shape[0]
+            return torch.cat((w, w.new_zeros(pad, w.shape[1])), 0) if pad else w
 
         return {
             "in_proj": (keys, in_proj),

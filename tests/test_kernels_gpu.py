@@ -12,6 +12,11 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+@pytest.fixture(scope="module", autouse=True)
+def _load_kernels():
+    ops.cuda_ops()  # registers torch.ops.isb.* before tests call them directly
+
+
 def _rel(a, b):
     a, b = a.float().cpu(), b.float().cpu()
     return ((a - b).norm() / (b.norm() + 1e-12)).item()
