@@ -15,6 +15,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace isb {
@@ -37,8 +39,20 @@ __device__ __forceinline__ void load_bf16x8(const __nv_bfloat16* p, float* v) {
 
 // ------------------------------------------------------------------ prepare
 // One warp per (token, head); HD/32 channels per lane (HD in {128, 256}).
-template <int HD>
-__global__ void attn_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int qkv_stride, const int* __restrict__ pos,
+template <typename TIn>
+__device__ __forceinline__ float take_in(TIn* row, int idx) {
+  if constexpr (std::is_same_v<TIn, float>) {
+    const float v = row[idx];
+    row[idx] = 0.f;  // fp32 accumulator input: its only reader re-zeroes it
+    return v;
+  } else {
+    return __bfloat162float(row[idx]);
+  }
+}
+
+template <int HD, typename TIn>
+__global__ void attn_prepare_kernel(TIn* __restrict__ qkv, int qkv_stride, __nv_bfloat16* __restrict__ gate_out,
+                                    const int* __restrict__ pos,
                                     const int* __restrict__ slot_map, const __nv_bfloat16* __restrict__ qn,
                                     const __nv_bfloat16* __restrict__ kn, const float* __restrict__ cos_sin, int rd,
                                     __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
@@ -50,17 +64,22 @@ __global__ void attn_prepare_kernel(const __nv_bfloat16* __restrict__ qkv, int q
   const int heads = Hq + 2 * Hkv;
   const int t = warp_global / heads, hh = warp_global % heads;
   if (t >= T) return;
-  const __nv_bfloat16* row = qkv + size_t(t) * qkv_stride;
+  TIn* row = qkv + size_t(t) * qkv_stride;
   const int qw = Hq * HD * (gated ? 2 : 1);
   float v[E];
-  const __nv_bfloat16* src;
+  TIn* src;
   int kind;  // 0 q, 1 k, 2 v
   int head;
   if (hh < Hq) { kind = 0; head = hh; src = row + head * HD * (gated ? 2 : 1); }
   else if (hh < Hq + Hkv) { kind = 1; head = hh - Hq; src = row + qw + head * HD; }
   else { kind = 2; head = hh - Hq - Hkv; src = row + qw + Hkv * HD + head * HD; }
 #pragma unroll
-  for (int i = 0; i < E; ++i) v[i] = __bfloat162float(src[lane * E + i]);
+  for (int i = 0; i < E; ++i) v[i] = take_in(src, lane * E + i);
+  if (kind == 0 && gated) {
+    __nv_bfloat16* gdst = gate_out + (size_t(t) * Hq + head) * HD + lane * E;
+#pragma unroll
+    for (int i = 0; i < E; ++i) gdst[i] = __float2bfloat16(take_in(src + HD, lane * E + i));
+  }
   const int slot = slot_map[t];
   if (kind == 2) {
     if (slot >= 0) {
@@ -181,17 +200,27 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
   for (int i = tid; i < G * HD; i += 256) q_s[i] = __bfloat162float(q[(size_t(b) * Hq + kvh * G) * HD + i]) * scale;
   __syncthreads();
   if (!mbar_wait(&bar, 0)) atomicOr(&g_attn_err, 1u);
-  // ---- phase 1: scores
+  // ---- phase 1: scores.  Lane hl of a half-warp owns channels {j*128 + hl*8 .. +8}, so each
+  // 16-byte K read of a half-warp covers 256 contiguous bytes (no bank conflicts) and the
+  // query slice lives in registers.
   {
     const int hl = lane & 15;
+    constexpr int NJ = ED / 8;  // 16-byte chunks per lane
+    float qr[G][ED];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) qr[g][j * 8 + e] = q_s[g * HD + j * 128 + hl * 8 + e];
     for (int t0 = warp * 2; t0 < n; t0 += 16) {
       const int t = t0 + (lane >> 4);
       const bool valid = t < n;
       float kv[ED];
 #pragma unroll
-      for (int j = 0; j < ED / 8; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         if (valid) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(k_s + t * HD + hl * ED + j * 8);
+          const uint4 raw = *reinterpret_cast<const uint4*>(k_s + t * HD + j * 128 + hl * 8);
           const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
@@ -206,13 +235,9 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
       }
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        const float4* qv = reinterpret_cast<const float4*>(q_s + g * HD + hl * ED);
         float sacc = 0.f;
 #pragma unroll
-        for (int j = 0; j < ED / 4; ++j) {
-          const float4 qq = qv[j];
-          sacc += qq.x * kv[4 * j] + qq.y * kv[4 * j + 1] + qq.z * kv[4 * j + 2] + qq.w * kv[4 * j + 3];
-        }
+        for (int i = 0; i < ED; ++i) sacc += qr[g][i] * kv[i];
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, o);
         if (valid && hl == 0) s_s[g * DCHUNK + t] = sacc;
@@ -257,8 +282,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
 // grid (Hq, B); HD threads. Merges chunk partials, applies the output gate.
 template <int HD>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_chunks,
-                                    int chunk, const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ qkv,
-                                    int qkv_stride, bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
+                                    int chunk, const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ gate,
+                                    bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = ctx_lens[b];
   const int chunks = (ctx + chunk - 1) / chunk;
@@ -273,8 +298,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   }
   float o = chunks > 0 && l > 0.f ? acc / l : 0.f;
   if (gated) {
-    const float gt = __bfloat162float(qkv[size_t(b) * qkv_stride + h * 2 * HD + HD + d]);
-    o *= sigmoidf_(gt);
+    o *= sigmoidf_(__bfloat162float(gate[(size_t(b) * Hq + h) * HD + d]));
   }
   out[(size_t(b) * Hq + h) * HD + d] = __float2bfloat16(o);
 }
@@ -285,7 +309,7 @@ template <int HD, int G, int QT>
 __global__ void __launch_bounds__(256) attn_prefill_kernel(
     const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ kc, const __nv_bfloat16* __restrict__ vcache,
     const int* __restrict__ cu_q, const int* __restrict__ ctx_lens, const int* __restrict__ block_tables,
-    int max_blocks, int Hkv, float scale, const __nv_bfloat16* __restrict__ qkv, int qkv_stride, bool gated,
+    int max_blocks, int Hkv, float scale, const __nv_bfloat16* __restrict__ gate, bool gated,
     __nv_bfloat16* __restrict__ out) {
   constexpr int R = QT * G;        // query rows (query-major, head-minor)
   constexpr int KT = 32;           // keys per tile
@@ -388,7 +412,7 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
     const int t = q0 + tq0 + qi;
     const int h = kvh * G + g;
     float o = l_s[r] > 0.f ? acc[i] / l_s[r] : 0.f;
-    if (gated) o *= sigmoidf_(__bfloat162float(qkv[size_t(t) * qkv_stride + h * 2 * HD + HD + d]));
+    if (gated) o *= sigmoidf_(__bfloat162float(gate[(size_t(t) * Hq + h) * HD + d]));
     out[(size_t(t) * Hq + h) * HD + d] = __float2bfloat16(o);
   }
 }
@@ -400,39 +424,44 @@ void check_cache(const at::Tensor& kc, const at::Tensor& vc, int64_t hd) {
 
 }  // namespace
 
-at::Tensor attn_prepare(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slot_mapping,
-                        const at::Tensor& qn, const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
-                        at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps, bool gated, bool zc) {
+std::tuple<at::Tensor, at::Tensor> attn_prepare(const at::Tensor& qkv, const at::Tensor& positions,
+                                                const at::Tensor& slot_mapping, const at::Tensor& qn,
+                                                const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
+                                                at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps,
+                                                bool gated, bool zc) {
   check_cache(kc, vc, hd);
-  TORCH_CHECK(qkv.is_contiguous() && qkv.scalar_type() == at::kBFloat16, "qkv must be contiguous bf16");
+  TORCH_CHECK(qkv.is_contiguous() && (qkv.scalar_type() == at::kBFloat16 || qkv.scalar_type() == at::kFloat),
+              "qkv must be contiguous bf16 (or an fp32 accumulator, consumed)");
   TORCH_CHECK(positions.scalar_type() == at::kInt && slot_mapping.scalar_type() == at::kInt, "int32 metadata");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "cos/sin table must be fp32");
-  const int T = qkv.size(0);
+  const int T = positions.numel();
   const int rd = cos_sin.size(1);
-  at::Tensor q = at::empty({T, Hq, hd}, qkv.options());
-  if (T == 0) return q;
+  at::Tensor q = at::empty({T, Hq, hd}, kc.options());
+  at::Tensor gate = at::empty({gated ? T : 0, Hq * hd}, kc.options());
+  if (T == 0) return {q, gate};
+  TORCH_CHECK((rd / 2) % (hd / 32) == 0 && rd <= hd, "rotary dim must split evenly across lanes");
+  const int partner = (rd / 2) / (hd / 32);
+  TORCH_CHECK(partner > 0 && (partner & (partner - 1)) == 0, "rotary half must map to a power-of-two lane distance");
   const int warps = T * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto st = at::cuda::getCurrentCUDAStream();
-#define ISB_PREP(HD_)                                                                                             \
-  attn_prepare_kernel<HD_><<<blocks, threads, 0, st>>>(                                                           \
-      reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.size(1), positions.data_ptr<int>(),             \
-      slot_mapping.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(qn.data_ptr()),                        \
+#define ISB_PREP(HD_, T_)                                                                                         \
+  attn_prepare_kernel<HD_, T_><<<blocks, threads, 0, st>>>(                                                       \
+      reinterpret_cast<T_*>(qkv.data_ptr()), qkv.size(1), reinterpret_cast<__nv_bfloat16*>(gate.data_ptr()),      \
+      positions.data_ptr<int>(), slot_mapping.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(qn.data_ptr()), \
       reinterpret_cast<const __nv_bfloat16*>(kn.data_ptr()), cos_sin.data_ptr<float>(), rd,                       \
       reinterpret_cast<__nv_bfloat16*>(kc.data_ptr()), reinterpret_cast<__nv_bfloat16*>(vc.data_ptr()),          \
       reinterpret_cast<__nv_bfloat16*>(q.data_ptr()), T, Hq, Hkv, float(eps), gated, zc)
-  TORCH_CHECK((rd / 2) % (hd / 32) == 0 && rd <= hd, "rotary dim must split evenly across lanes");
-  const int partner = (rd / 2) / (hd / 32);
-  TORCH_CHECK(partner > 0 && (partner & (partner - 1)) == 0, "rotary half must map to a power-of-two lane distance");
-  if (hd == 256) ISB_PREP(256);
-  else if (hd == 128) ISB_PREP(128);
+  const bool f32 = qkv.scalar_type() == at::kFloat;
+  if (hd == 256) { if (f32) ISB_PREP(256, float); else ISB_PREP(256, __nv_bfloat16); }
+  else if (hd == 128) { if (f32) ISB_PREP(128, float); else ISB_PREP(128, __nv_bfloat16); }
   else TORCH_CHECK(false, "attn_prepare supports head_dim 128 or 256");
 #undef ISB_PREP
-  return q;
+  return {q, gate};
 }
 
-at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                             const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated) {
   const int B = q.size(0), Hq = q.size(1), hd = q.size(2);
   check_cache(kc, vc, hd);
@@ -474,8 +503,8 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at
 #define ISB_COMB(HD_)                                                                                              \
   attn_combine_kernel<HD_><<<dim3(Hq, B), HD_, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),       \
                                                        max_chunks, DCHUNK, ctx_lens.data_ptr<int>(),                  \
-                                                       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),       \
-                                                       qkv.size(1), gated,                                           \
+                                                       reinterpret_cast<const __nv_bfloat16*>(gate.data_ptr()),      \
+                                                       gated,                                                        \
                                                        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), Hq)
   if (hd == 256) ISB_COMB(256); else ISB_COMB(128);
 #undef ISB_COMB
@@ -490,7 +519,7 @@ int64_t attn_error_word() {
   return v;
 }
 
-at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                              double scale, bool gated, int64_t max_seqlen_q) {
   const int T = q.size(0), Hq = q.size(1), hd = q.size(2);
@@ -512,8 +541,8 @@ at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const a
                                   reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()),                          \
                                   reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), cu_q.data_ptr<int>(),    \
                                   ctx_lens.data_ptr<int>(), block_tables.data_ptr<int>(), block_tables.size(1),    \
-                                  Hkv, float(scale), reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()),      \
-                                  qkv.size(1), gated, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));          \
+                                  Hkv, float(scale), reinterpret_cast<const __nv_bfloat16*>(gate.data_ptr()),     \
+                                  gated, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));                       \
   } while (0)
   if (hd == 256 && G == 4) ISB_PRE(256, 4, 16);
   else if (hd == 256 && G == 2) ISB_PRE(256, 2, 32);

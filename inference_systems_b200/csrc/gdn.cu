@@ -24,6 +24,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace isb {
@@ -35,7 +37,7 @@ constexpr int KW = 4;           // conv width
 constexpr int kThreads = 256;   // 8 row groups x 32 column groups
 
 struct ScanArgs {
-  const __nv_bfloat16* proj;
+  const void* proj;        // [T, proj_stride] bf16, or fp32 accumulator that is consumed (read, then zeroed)
   int proj_stride;
   const int* cu_seqlens;   // [B+1] or nullptr (one token per sequence)
   const int* slots;        // [B]
@@ -69,6 +71,19 @@ __device__ __forceinline__ float block_sum_128(float v, float* scratch, int tid)
   return r;
 }
 
+template <typename TIn>
+__device__ __forceinline__ float take(const TIn* row, int idx, bool consume) {
+  if constexpr (std::is_same_v<TIn, float>) {
+    float* p = const_cast<float*>(row) + idx;
+    const float v = *p;
+    if (consume) *p = 0.f;
+    return v;
+  } else {
+    return __bfloat162float(row[idx]);
+  }
+}
+
+template <typename TIn>
 __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
   __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
   __shared__ float red_k[8][D], red_q[8][D];
@@ -110,22 +125,22 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
 
     for (int t = t0; t < t1; ++t) {
-      const __nv_bfloat16* x = a.proj + size_t(t) * a.proj_stride;
-      // --- conv + SiLU
-      const float xq = __bfloat162float(x[qk_ch]);
+      const TIn* x = static_cast<const TIn*>(a.proj) + size_t(t) * a.proj_stride;
+      // --- conv + SiLU (an fp32 accumulator input is re-zeroed by its only reader)
+      const float xq = take(x, qk_ch, j == r - 1);
       const float aq = silu(wq0 * qs0 + wq1 * qs1 + wq2 * qs2 + wq3 * xq);
       qs0 = qs1; qs1 = qs2; qs2 = xq;
       if (tid < 128) {
         q_s[tid] = aq;
-        const float xv = __bfloat162float(x[v_ch]);
+        const float xv = take(x, v_ch, true);
         v_s[tid] = silu(wv0 * vs0 + wv1 * vs1 + wv2 * vs2 + wv3 * xv);
         vs0 = vs1; vs1 = vs2; vs2 = xv;
       } else {
         k_s[tid - 128] = aq;
       }
       if (tid == 0) {
-        const float bb = __bfloat162float(x[a.C + a.Hv * D + h]);
-        const float aa = __bfloat162float(x[a.C + a.Hv * D + a.Hv + h]);
+        const float bb = take(x, a.C + a.Hv * D + h, true);
+        const float aa = take(x, a.C + a.Hv * D + a.Hv + h, true);
         const float g = A * softplusf(aa + dtb);
         scal[0] = 1.f / (1.f + expf(-bb));   // beta
         scal[1] = g;
@@ -204,7 +219,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
       const float ob = __bfloat162float(__float2bfloat16(o));
       const float ss = block_sum_128(tid < 128 ? ob * ob : 0.f, &scal[8], tid);
       if (tid < 128) {
-        const float z = __bfloat162float(x[a.C + h * D + tid]);
+        const float z = take(x, a.C + h * D + tid, true);
         const float y = ob * rsqrtf(ss / float(D) + a.eps) * __bfloat162float(a.norm_w[tid]) * silu(z);
         a.out[size_t(t) * (a.Hv * D) + h * D + tid] = __float2bfloat16(y);
       }
@@ -267,7 +282,8 @@ void check_gdn(const at::Tensor& proj, const at::Tensor& rec, const at::Tensor& 
                int64_t hk, int64_t hv) {
   TORCH_CHECK(dk == D && dv == D, "CUDA GDN kernels handle key/value head dim 128");
   TORCH_CHECK(hv % hk == 0, "Hv must be a multiple of Hk");
-  TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && proj.is_contiguous(), "proj must be contiguous bf16");
+  TORCH_CHECK((proj.scalar_type() == at::kBFloat16 || proj.scalar_type() == at::kFloat) && proj.is_contiguous(),
+              "proj must be contiguous bf16 (or an fp32 accumulator)");
   TORCH_CHECK(rec.scalar_type() == at::kFloat && rec.is_contiguous() && rec.size(1) == hv, "bad recurrent pool");
   TORCH_CHECK(conv.scalar_type() == at::kBFloat16 && conv.is_contiguous() && conv.size(2) == KW - 1,
               "bad conv pool");
@@ -277,7 +293,7 @@ ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Te
                    const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor& rec, at::Tensor& conv,
                    at::Tensor& out, int64_t hk, int64_t hv, double eps) {
   ScanArgs a = {};
-  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.proj = proj.data_ptr();
   a.proj_stride = proj.size(1);
   a.slots = slots.data_ptr<int>();
   a.conv_w = reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr());
@@ -300,6 +316,12 @@ ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Te
   return a;
 }
 
+void launch_scan(const ScanArgs& a, const at::Tensor& proj, int64_t hk, int B) {
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (proj.scalar_type() == at::kFloat) gdn_scan_kernel<float><<<dim3(hk, B), kThreads, 0, st>>>(a);
+  else gdn_scan_kernel<__nv_bfloat16><<<dim3(hk, B), kThreads, 0, st>>>(a);
+}
+
 }  // namespace
 
 at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
@@ -307,10 +329,10 @@ at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at:
                       int64_t hv, int64_t dk, int64_t dv, double eps) {
   check_gdn(proj, rec, conv, dk, dv, hk, hv);
   const int B = proj.size(0);
-  at::Tensor out = at::empty({B, hv * D}, proj.options());
+  at::Tensor out = at::empty({B, hv * D}, proj.options().dtype(at::kBFloat16));
   if (B == 0) return out;
   ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
-  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  launch_scan(a, proj, hk, B);
   return out;
 }
 
@@ -320,11 +342,11 @@ at::Tensor gdn_prefill(const at::Tensor& proj, const at::Tensor& cu_seqlens, con
                        int64_t dv, double eps, int64_t max_seqlen) {
   check_gdn(proj, rec, conv, dk, dv, hk, hv);
   const int T = proj.size(0), B = slots.numel();
-  at::Tensor out = at::empty({T, hv * D}, proj.options());
+  at::Tensor out = at::empty({T, hv * D}, proj.options().dtype(at::kBFloat16));
   if (T == 0 || B == 0) return out;
   ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
   a.cu_seqlens = cu_seqlens.data_ptr<int>();
-  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  launch_scan(a, proj, hk, B);
   return out;
 }
 
@@ -338,7 +360,7 @@ at::Tensor gdn_scan_history(const at::Tensor& proj, const at::Tensor& cu_seqlens
                             c10::optional<at::Tensor> rec_g) {
   check_gdn(proj, rec, conv, D, D, hk, hv);
   const int T = proj.size(0), B = slots.numel();
-  at::Tensor out = at::empty({T, hv * D}, proj.options());
+  at::Tensor out = at::empty({T, hv * D}, proj.options().dtype(at::kBFloat16));
   if (T == 0 || B == 0) return out;
   ScanArgs a = make_args(proj, slots, conv_w, A_log, dt_bias, norm_w, rec, conv, out, hk, hv, eps);
   a.cu_seqlens = cu_seqlens.data_ptr<int>();
@@ -354,7 +376,7 @@ at::Tensor gdn_scan_history(const at::Tensor& proj, const at::Tensor& cu_seqlens
     a.rec_delta = rec_delta->data_ptr<float>();
     a.rec_g = rec_g->data_ptr<float>();
   }
-  gdn_scan_kernel<<<dim3(hk, B), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(a);
+  launch_scan(a, proj, hk, B);
   return out;
 }
 

@@ -19,6 +19,8 @@
 
 #include <ATen/cuda/CUDAContext.h>
 #include <cudaTypedefs.h>
+
+#include <cstdlib>
 #include <torch/extension.h>
 
 #include "common.cuh"
@@ -45,7 +47,7 @@ struct GemmCfg {
                 "split-K / SiLU staging must fit in the stage buffers");
 };
 
-enum Epilogue : int { kStore = 0, kSiluMul = 1, kArgmax = 2 };
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kArgmax = 2, kRedAdd = 3 };
 
 struct GemmArgs {
   __nv_bfloat16* out;      // kStore / kSiluMul output
@@ -60,6 +62,7 @@ struct GemmArgs {
   int vocab_offset;
   unsigned long long* dbg;  // optional per-CTA phase timestamps [ctas][8] (diagnostics)
   float* ws;                // split-K partials [tiles][splits][BM][BN] fp32
+  float* acc;               // kRedAdd: fp32 accumulator [tokens][features], atomically added to
   unsigned int* counters;   // split-K arrival counters (self-resetting)
 };
 
@@ -69,6 +72,11 @@ struct GemmArgs {
 constexpr int kCounterSlots = 8;
 constexpr int kCountersPerSlot = 8192;
 __device__ unsigned int g_splitk_counters[kCounterSlots * kCountersPerSlot];
+
+ISB_DEVICE void red_add_v4(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
 
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
   h ^= h >> 16;
@@ -197,7 +205,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- split-K: publish the fp32 partial to L2; the last CTA of the tile reduces
     bool reduce_here = true;
-    if (nsplit > 1) {
+    if (nsplit > 1 && EPI != kRedAdd) {
       // column-major partial [BN][BM]: a warp's 32 rows of one column are 128 contiguous bytes
       float* mine = args.ws + (size_t(tile_id) * nsplit + blockIdx.z) * BN * BM + row;
       for (int c = 0; c < BN / CH; ++c) {
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < CH; ++j) acc[j] += __ldcg(src + size_t(j) * BM);
           }
         };
-        if (nsplit > 1) add_partials(v, c * CH);
+        if (nsplit > 1 && EPI != kRedAdd) add_partials(v, c * CH);
         if constexpr (EPI == kStore) {
           if constexpr (SWAP) {
             // transpose through shared memory: ostage[token][feature]
@@ -293,48 +301,64 @@ __global__ void __launch_bounds__(kThreads, 1)
                   args.out[size_t(t) * args.ldo + col0 + j] = __float2bfloat16(silu(v[j]) * u[j]);
             }
           }
+        } else if constexpr (EPI == kRedAdd) {
+          if constexpr (SWAP) {
+            float* fstage = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 (token-major)
+#pragma unroll
+            for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
+          } else {
+            const int t = p0 + row;
+            const int col0 = q0 + c * CH;
+            if (t < args.P_rows) {
+              float* dst = args.acc + size_t(t) * args.ldo + col0;
+              if (col0 + CH <= args.Q_rows && (args.ldo % 4) == 0) {
+#pragma unroll
+                for (int j = 0; j < CH / 4; ++j) red_add_v4(dst + 4 * j, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+              } else {
+#pragma unroll
+                for (int j = 0; j < CH; ++j)
+                  if (col0 + j < args.Q_rows) atomicAdd(dst + j, v[j]);
+              }
+            }
+          }
         } else {  // kArgmax: LM head fused with greedy / Gumbel-max selection
           const int seed = args.rng[0], step = args.rng[1];
           if constexpr (SWAP) {
+            // rows = vocab entries, columns = tokens.  Scores go to shared memory
+            // ([row][col], stride BN+1: conflict-free both ways) and one thread per
+            // token column scans the 128 rows, keeping the first maximum.
+            float* sc_s = xbuf;                                   // [BM][BN + 1]
+            float* temp_s = xbuf + BM * (BN + 1);                 // [BN]
+            if (c == 0) {
+              for (int j = threadIdx.x - 64; j < BN; j += 128) temp_s[j] = q0 + j < args.Q_rows ? args.temps[q0 + j] : 0.f;
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
             const int vrow = p0 + row;
             const bool valid = vrow < args.P_rows;
-            float* sval = xbuf;                                   // [4 warps][BN]
-            int* sidx = reinterpret_cast<int*>(xbuf + 4 * BN);
 #pragma unroll
             for (int j = 0; j < CH; ++j) {
-              const int t = q0 + c * CH + j;
-              float sc = -INFINITY;
-              if (valid && t < args.Q_rows) {
-                const float temp = args.temps[t];
-                sc = v[j];
-                if (temp > 1e-10f) sc = sc / temp + gumbel_noise(seed, step, t, args.vocab_offset + vrow);
-              }
-              int bi = vrow;
-#pragma unroll
-              for (int o = 16; o > 0; o >>= 1) {
-                const float os = __shfl_xor_sync(0xffffffffu, sc, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (os > sc || (os == sc && oi < bi)) { sc = os; bi = oi; }
-              }
-              if (lane == 0) { sval[quarter * BN + c * CH + j] = sc; sidx[quarter * BN + c * CH + j] = bi; }
-            }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int j = threadIdx.x - 64; j < CH; j += 128) {
               const int col = c * CH + j;
-              const int t = q0 + col;
-              float sc = sval[col];
-              int bi = sidx[col];
-              for (int w = 1; w < 4; ++w) {
-                const float os = sval[w * BN + col];
-                const int oi = sidx[w * BN + col];
-                if (os > sc || (os == sc && oi < bi)) { sc = os; bi = oi; }
-              }
-              if (t < args.Q_rows) {
-                args.part_val[size_t(tile_p) * args.Q_rows + t] = sc;
-                args.part_idx[size_t(tile_p) * args.Q_rows + t] = bi;
+              float sc = valid ? v[j] : -INFINITY;
+              const float temp = temp_s[col];
+              if (valid && temp > 1e-10f) sc = sc / temp + gumbel_noise(seed, step, q0 + col, args.vocab_offset + vrow);
+              sc_s[row * (BN + 1) + col] = sc;
+            }
+            if (c == BN / CH - 1) {
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+              for (int col = threadIdx.x - 64; col < BN; col += 128) {
+                const int t = q0 + col;
+                float best = -INFINITY;
+                int bi = 0;
+                for (int r = 0; r < BM; ++r) {
+                  const float x = sc_s[r * (BN + 1) + col];
+                  if (x > best) { best = x; bi = r; }
+                }
+                if (t < args.Q_rows) {
+                  args.part_val[size_t(tile_p) * args.Q_rows + t] = best;
+                  args.part_idx[size_t(tile_p) * args.Q_rows + t] = p0 + bi;
+                }
               }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
           } else {
             const int t = p0 + row;
             if (t < args.P_rows) {
@@ -356,6 +380,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 args.part_idx[slot] = bi;
               }
             }
+          }
+        }
+      }
+      // swap-AB accumulation: 4 consecutive features per vector atomic from the staged tile
+      if constexpr (SWAP && EPI == kRedAdd) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        const float* fstage = reinterpret_cast<const float*>(smem);
+        const int tid = threadIdx.x - 64;
+        const bool vec_ok = (args.ldo % 4) == 0;
+        for (int i = tid; i < BN * (BM / 4); i += 128) {
+          const int t = i / (BM / 4), f4 = (i % (BM / 4)) * 4;
+          const int tok = q0 + t, f = p0 + f4;
+          if (tok >= args.Q_rows || f >= args.P_rows) continue;
+          const float4 w = *reinterpret_cast<const float4*>(fstage + t * BM + f4);
+          float* dst = args.acc + size_t(tok) * args.ldo + f;
+          if (vec_ok && f + 3 < args.P_rows) {
+            red_add_v4(dst, w.x, w.y, w.z, w.w);
+          } else {
+            const float e[4] = {w.x, w.y, w.z, w.w};
+            for (int k = 0; k < 4 && f + k < args.P_rows; ++k) atomicAdd(dst + k, e[k]);
           }
         }
       }
@@ -426,6 +470,17 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 // 2-D bf16 K-major map: dims {K, rows}, box {64, box_rows}, 128-byte swizzle, zero OOB fill.
+static CUtensorMapL2promotion promo_mode() {
+  static int mode = -1;
+  if (mode < 0) {
+    const char* e = std::getenv("ISB_TMA_PROMO");
+    mode = e ? std::atoi(e) : 3;
+  }
+  return mode == 0 ? CU_TENSOR_MAP_L2_PROMOTION_NONE
+                   : mode == 1 ? CU_TENSOR_MAP_L2_PROMOTION_L2_64B
+                               : mode == 2 ? CU_TENSOR_MAP_L2_PROMOTION_L2_128B : CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+}
+
 CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int box_rows) {
   CUtensorMap m;
   cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
@@ -433,8 +488,8 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int box_ro
   cuuint32_t box[2] = {cuuint32_t(BK), cuuint32_t(box_rows)};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo_mode(),
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed: ", int(r));
   return m;
 }
@@ -565,7 +620,7 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
                      unsigned long long* dbg) {
   const int M = a.size(0), N = b.size(0);
   const int out_cols = out.size(1);
-  Plan p = plan_gemm(a, b, true, force_splits);
+  Plan p = plan_gemm(a, b, false, force_splits);
   GemmArgs args = {};
   args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   args.K = a.size(1);
@@ -595,6 +650,36 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
   }
 }
 
+// acc[M, N] (fp32) += a[M, K] . b[N, K]^T.  Every CTA (including every split-K
+// slice) adds its tile with vector atomics, so the split count only sets the
+// parallelism; the consumer of ``acc`` is expected to read and re-zero it.
+void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int64_t splits) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) >= M && acc.size(1) == N,
+              "accumulator must be contiguous fp32 [>= M, N]");
+  if (M == 0) return;
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  Plan p = plan_gemm(a, b, false, 1);
+  int sp = splits > 0 ? int(splits) : 1;
+  if (splits <= 0) {  // fill the machine: one to two waves of CTAs
+    const int tiles = p.tiles_p * p.tiles_q;
+    while (sp < 16 && tiles * sp * 2 <= 2 * num_sms() && kb_total / (sp * 2) >= 2) sp *= 2;
+  }
+  p.kb_per = (kb_total + sp - 1) / sp;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  GemmArgs args = {};
+  args.acc = acc.data_ptr<float>();
+  args.K = a.size(1);
+  args.ldo = N;
+  args.kb_per_split = p.kb_per;
+  if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+}
+
 at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, int64_t splits) {
   at::Tensor a = a_in.contiguous();
   check_operands(a, b);
@@ -613,8 +698,34 @@ at::Tensor gemm_timeline(const at::Tensor& a_in, const at::Tensor& b, int64_t sp
   at::Tensor a = a_in.contiguous();
   check_operands(a, b);
   const int M = a.size(0), N = b.size(0);
+  if (splits < 0) {  // LM-head argmax epilogue (greedy)
+    Plan p = plan_gemm(a, b, false);
+    at::Tensor ts = at::zeros({int64_t(p.tiles_p) * p.tiles_q, 8}, a.options().dtype(at::kLong));
+    const int vtiles = p.swap ? p.tiles_p : p.tiles_q;
+    at::Tensor pv = at::empty({vtiles, M}, a.options().dtype(at::kFloat));
+    at::Tensor pi = at::empty({vtiles, M}, a.options().dtype(at::kInt));
+    at::Tensor temps = at::zeros({M}, a.options().dtype(at::kFloat));
+    at::Tensor rng = at::zeros({2}, a.options().dtype(at::kInt));
+    GemmArgs args = {};
+    args.K = a.size(1);
+    args.kb_per_split = p.kb_per;
+    args.temps = temps.data_ptr<float>();
+    args.rng = rng.data_ptr<int>();
+    args.part_val = pv.data_ptr<float>();
+    args.part_idx = pi.data_ptr<int>();
+    args.dbg = reinterpret_cast<unsigned long long*>(ts.data_ptr());
+    cudaStream_t st = at::cuda::getCurrentCUDAStream();
+    if (p.swap) {
+      args.P_rows = N; args.Q_rows = M;
+      dispatch_bn<kArgmax, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
+    } else {
+      args.P_rows = M; args.Q_rows = N;
+      launch_gemm<256, false, kArgmax>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
+    }
+    return ts;
+  }
   at::Tensor out = at::empty({M, N}, a.options());
-  Plan p = plan_gemm(a, b, true, int(splits));
+  Plan p = plan_gemm(a, b, false, int(splits));
   at::Tensor ts = at::zeros({int64_t(p.tiles_p) * p.tiles_q * p.splits, 8}, a.options().dtype(at::kLong));
   run_gemm(a, b, out, kStore, int(splits), reinterpret_cast<unsigned long long*>(ts.data_ptr()));
   return ts;

@@ -12,6 +12,9 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h, const at:
                                                   const at::Tensor& rng, int64_t vocab_offset);
 int64_t gemm_error_word();
 at::Tensor gemm_timeline(const at::Tensor& a, const at::Tensor& b, int64_t splits);
+void gemm_accum(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, int64_t splits);
+at::Tensor add_rmsnorm_acc(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
+at::Tensor silu_mul_acc(at::Tensor acc, int64_t rows);
 at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& w, double eps, bool zc);
 at::Tensor add_rmsnorm(const at::Tensor& x, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
 std::tuple<at::Tensor, at::Tensor> embed_rmsnorm(const at::Tensor& ids, const at::Tensor& table, const at::Tensor& w,
@@ -35,12 +38,14 @@ void gdn_replay_commit(at::Tensor rec, const at::Tensor& slots, const at::Tensor
                        const at::Tensor& gs, const at::Tensor& lens, int64_t steps);
 void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& slots, const at::Tensor& bounds,
                      int64_t steps);
-at::Tensor attn_prepare(const at::Tensor& qkv, const at::Tensor& positions, const at::Tensor& slot_mapping,
-                        const at::Tensor& qn, const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
-                        at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps, bool gated, bool zc);
-at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+std::tuple<at::Tensor, at::Tensor> attn_prepare(const at::Tensor& qkv, const at::Tensor& positions,
+                                                const at::Tensor& slot_mapping, const at::Tensor& qn,
+                                                const at::Tensor& kn, const at::Tensor& cos_sin, at::Tensor kc,
+                                                at::Tensor vc, int64_t Hq, int64_t Hkv, int64_t hd, double eps,
+                                                bool gated, bool zc);
+at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                             const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated);
-at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                              double scale, bool gated, int64_t max_seqlen_q);
 void quantize_state_int8(const at::Tensor& state, at::Tensor q, at::Tensor scale);
@@ -60,14 +65,14 @@ TORCH_LIBRARY(isb, m) {
   m.def("embed_rmsnorm(Tensor ids, Tensor table, Tensor w, float eps, bool zero_centered) -> (Tensor, Tensor)");
   m.def("embed(Tensor ids, Tensor table, int vocab_start) -> Tensor");
   m.def(
-      "gdn_decode(Tensor proj, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
+      "gdn_decode(Tensor(c!) proj, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
       "Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps) -> Tensor");
   m.def(
-      "gdn_prefill(Tensor proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
+      "gdn_prefill(Tensor(c!) proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
       "Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps, int max_seqlen) "
       "-> Tensor");
   m.def(
-      "gdn_scan_history(Tensor proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
+      "gdn_scan_history(Tensor(h!) proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
       "Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, float eps, bool write_final, "
       "Tensor? hist_row, Tensor(c!)? hist_rec, Tensor(d!)? hist_conv, Tensor(e!)? rec_k, Tensor(f!)? rec_delta, "
       "Tensor(g!)? rec_g) -> Tensor");
@@ -76,20 +81,23 @@ TORCH_LIBRARY(isb, m) {
       "int steps) -> ()");
   m.def("gdn_conv_commit(Tensor(a!) conv, Tensor hist, Tensor slots, Tensor bounds, int steps) -> ()");
   m.def(
-      "attn_prepare(Tensor qkv, Tensor positions, Tensor slot_mapping, Tensor qn, Tensor kn, Tensor cos_sin, "
+      "attn_prepare(Tensor(c!) qkv, Tensor positions, Tensor slot_mapping, Tensor qn, Tensor kn, Tensor cos_sin, "
       "Tensor(a!) k_cache, Tensor(b!) v_cache, int Hq, int Hkv, int hd, float eps, bool gated, bool zero_centered) "
-      "-> Tensor");
+      "-> (Tensor, Tensor)");
   m.def(
-      "attention_decode(Tensor q, Tensor qkv, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
+      "attention_decode(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
   m.def(
-      "attention_prefill(Tensor q, Tensor qkv, Tensor k_cache, Tensor v_cache, Tensor cu_seqlens_q, "
+      "attention_prefill(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor cu_seqlens_q, "
       "Tensor context_lens, Tensor block_tables, float scale, bool gated, int max_seqlen_q) -> Tensor");
   m.def("quantize_state_int8(Tensor state, Tensor(a!) q, Tensor(b!) scale) -> ()");
   m.def("dequantize_state_int8(Tensor q, Tensor scale, Tensor(a!) out) -> ()");
   m.def("copy_kv_page(Tensor(a!) k_cache, Tensor(b!) v_cache, int src, int dst, int n) -> ()");
   m.def("error_word() -> int");
   m.def("gemm_timeline(Tensor a, Tensor b, int splits) -> Tensor");
+  m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
+  m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
+  m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(isb, CUDA, m) {
@@ -111,6 +119,9 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);
   m.impl("copy_kv_page", &isb::copy_kv_page);
   m.impl("gemm_timeline", &isb::gemm_timeline);
+  m.impl("gemm_accum", &isb::gemm_accum);
+  m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);
+  m.impl("silu_mul_acc", &isb::silu_mul_acc);
 }
 
 TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) { m.impl("error_word", &isb::error_word); }

@@ -112,6 +112,10 @@ class ModelRunner:
         else:
             self.comm = None
 
+        if self.device.type == "cuda":
+            spec_rows = config.max_num_seqs * (self.num_speculative_tokens + 1)
+            self.model.set_accumulator(max(config.max_num_batched_tokens, config.max_num_seqs, spec_rows), self.device)
+
         # ------------------------------------------------------ GDN state
         self.state_manager = None
         geo = self.model.gdn_geometry()

@@ -43,11 +43,39 @@ class TPInfo:
         self.rank, self.size = rank, size
 
 
+class ColumnScratch:
+    """Shared fp32 buffer for decode-sized column-parallel projections.
+
+    For up to ``rows`` tokens the projection GEMM adds its split-K tiles into
+    this buffer with vector atomics (so the split count only sets parallelism)
+    and the single consumer (GDN scan, attention prepare, SiLU*mul) reads the
+    fp32 values and re-zeroes them; the buffer is therefore all-zero between
+    uses and one buffer serves every layer in turn.
+    """
+
+    def __init__(self):
+        self.buf: torch.Tensor | None = None
+        self.rows = 0
+
+    def allocate(self, rows: int, width: int, device) -> None:
+        self.rows = rows
+        self.buf = torch.zeros(rows * width, dtype=torch.float32, device=device)
+
+    def project(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor | None:
+        t, n = x.shape[0], w.shape[0]
+        if self.buf is None or not x.is_cuda or t > self.rows or t * n > self.buf.numel():
+            return None
+        acc = self.buf[: t * n].view(t, n)
+        ops.linear_accumulate(x, w, acc)
+        return acc
+
+
 class AttentionMixer(nn.Module):
     def __init__(self, cfg, tp: TPInfo, gated: bool, zero_centered: bool, prefix: str):
         super().__init__()
         self.prefix = prefix
         self.tp = tp
+        self.scratch: ColumnScratch | None = None
         self.gated = gated
         self.zero_centered = zero_centered
         self.total_heads = cfg.num_attention_heads
@@ -106,7 +134,9 @@ class AttentionMixer(nn.Module):
     def forward(self, x: torch.Tensor, batch: ForwardBatch, kv: tuple[torch.Tensor, torch.Tensor],
                 cos_sin: torch.Tensor) -> torch.Tensor:
         """Returns the rank-local pre-o_proj activation ``[T, Hq_local*hd]``."""
-        qkv = ops.linear(x, self.qkv_proj)
+        qkv = self.scratch.project(x, self.qkv_proj) if self.scratch is not None else None
+        if qkv is None:
+            qkv = ops.linear(x, self.qkv_proj)
         k_cache, v_cache = kv
         return ops.attention_block(qkv, batch, self.q_norm, self.k_norm, cos_sin, k_cache, v_cache,
                                    num_heads=self.num_heads, num_kv_heads=self.num_kv_heads,
@@ -119,6 +149,7 @@ class GDNMixer(nn.Module):
         super().__init__()
         self.prefix = prefix
         self.tp = tp
+        self.scratch: ColumnScratch | None = None
         thk, thv = cfg.linear_num_key_heads, cfg.linear_num_value_heads
         if thk % tp.size or thv % tp.size:
             raise ValueError("GDN head counts must be divisible by tensor parallel size")
@@ -173,7 +204,9 @@ class GDNMixer(nn.Module):
         }
 
     def forward(self, x: torch.Tensor, batch: ForwardBatch, pools: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
-        proj = ops.linear(x, self.in_proj)
+        proj = self.scratch.project(x, self.in_proj) if self.scratch is not None else None
+        if proj is None:
+            proj = ops.linear(x, self.in_proj)
         rec_pool, conv_pool = pools
         return ops.gdn(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool, conv_pool,
                        hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
@@ -183,6 +216,7 @@ class MLP(nn.Module):
     def __init__(self, cfg, tp: TPInfo, prefix: str):
         super().__init__()
         self.prefix, self.tp = prefix, tp
+        self.scratch: ColumnScratch | None = None
         if cfg.intermediate_size % tp.size:
             raise ValueError("intermediate size must be divisible by tensor parallel size")
         self.inter = cfg.intermediate_size // tp.size
@@ -200,6 +234,9 @@ class MLP(nn.Module):
         }
 
     def forward_pre_down(self, x: torch.Tensor) -> torch.Tensor:
+        acc = self.scratch.project(x, self.gate_up) if self.scratch is not None else None
+        if acc is not None:
+            return ops.silu_mul_acc(acc, x.shape[0])
         return ops.linear_silu_mul(x, self.gate_up)
 
 
@@ -268,6 +305,7 @@ class HybridCausalLM(nn.Module):
         self.linear_layer_ids = [i for i, l in enumerate(self.layers) if l.is_linear]
         self.attn_layer_ids = [i for i, l in enumerate(self.layers) if not l.is_linear]
         self._cos_sin: torch.Tensor | None = None
+        self.column_scratch = ColumnScratch()
         self.comm = None  # set by the runner (parallel.comm.TPComm) when tp_size > 1
 
     # ------------------------------------------------------------ weights
@@ -313,10 +351,30 @@ class HybridCausalLM(nn.Module):
         return self._cos_sin
 
     # ------------------------------------------------------------ forward
+    def set_accumulator(self, max_tokens: int, device) -> None:
+        """Persistent fp32 ``[max_tokens, hidden]`` buffer that row-parallel GEMMs add into.
+
+        Every CTA of the output-projection GEMMs adds its (split-K) tile with
+        vector atomics and the following add+RMSNorm kernel consumes and
+        re-zeroes the rows it read, so the buffer is zero between uses.
+        """
+        self.acc = torch.zeros(max_tokens, self.hidden_size, dtype=torch.float32, device=device)
+        if getattr(self, "use_column_scratch", False):
+            widths = [m.shape[0] for m in self.parameters() if m.dim() == 2 and m.shape[1] == self.hidden_size
+                      and m.shape[0] != self.vocab_size and m.shape[0] != self.vocab_per_rank]
+            self.column_scratch.allocate(min(max_tokens, 256), max(widths), device)
+            for mod in self.modules():
+                if isinstance(mod, (AttentionMixer, GDNMixer, MLP)):
+                    mod.scratch = self.column_scratch
+
     def _row_parallel(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor) -> torch.Tensor:
         """``residual += x @ w^T`` (summed over TP ranks); return RMSNorm(residual)."""
         if self.comm is not None and self.tp.size > 1:
             return self.comm.row_parallel_residual_norm(x, w, residual, norm_w, self.eps, self.hybrid)
+        acc = getattr(self, "acc", None)
+        if x.is_cuda and acc is not None and x.shape[0] <= acc.shape[0]:
+            ops.linear_accumulate(x, w, acc)
+            return ops.add_rmsnorm_acc(acc, residual, norm_w, self.eps, self.hybrid)
         y = ops.linear(x, w)
         return ops.add_rmsnorm(y, residual, norm_w, self.eps, self.hybrid)
 
@@ -327,9 +385,9 @@ class HybridCausalLM(nn.Module):
         ``state_pools[j] = (recurrent_pool, conv_pool)`` for the j-th GDN layer.
         """
         cos_sin = self.cos_sin(batch.input_ids.device)
-        residual = ops.embed(batch.input_ids, self.embed_tokens, 0)
         layers = self.layers
-        x = ops.rmsnorm(residual, layers[0].input_layernorm, self.eps, self.hybrid)
+        residual, x = ops.embed_rmsnorm(batch.input_ids, self.embed_tokens, layers[0].input_layernorm, self.eps,
+                                        self.hybrid)
         attn_j = gdn_j = 0
         for i, layer in enumerate(layers):
             if layer.is_linear:

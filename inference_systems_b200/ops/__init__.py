@@ -40,6 +40,43 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     return ref.gemm(x, w)
 
 
+def linear_accumulate(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor) -> None:
+    """``acc[:T] += x @ w^T`` in fp32 (the consumer re-zeroes ``acc``)."""
+    if x.is_cuda:
+        cuda_ops().gemm_accum(x, w, acc, 0)
+        return
+    acc[: x.shape[0]] += x.float() @ w.float().t()
+
+
+def add_rmsnorm_acc(acc: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                    zero_centered: bool) -> torch.Tensor:
+    """``s = acc + residual``; ``residual <- s`` (rounded); return RMSNorm(s); ``acc <- 0``."""
+    if residual.is_cuda:
+        return cuda_ops().add_rmsnorm_acc(acc, residual, w, eps, zero_centered)
+    t = residual.shape[0]
+    out = ref.add_rmsnorm(acc[:t], residual, w, eps, zero_centered).to(residual.dtype)
+    acc[:t].zero_()
+    return out
+
+
+def silu_mul_acc(acc: torch.Tensor, rows: int) -> torch.Tensor:
+    """Consume a packed fp32 gate/up accumulator ``[>=rows, 2I]``: return ``SiLU(gate) * up`` (bf16), re-zero it."""
+    if acc.is_cuda:
+        return cuda_ops().silu_mul_acc(acc, rows)
+    out = ref.silu_mul_packed(acc[:rows]).to(torch.bfloat16)
+    acc[:rows].zero_()
+    return out
+
+
+def embed_rmsnorm(ids: torch.Tensor, table: torch.Tensor, w: torch.Tensor, eps: float,
+                  zero_centered: bool) -> tuple[torch.Tensor, torch.Tensor]:
+    """First-layer fusion: ``residual = table[ids]``, ``out = RMSNorm(residual)``."""
+    if ids.is_cuda:
+        return cuda_ops().embed_rmsnorm(ids, table, w, eps, zero_centered)
+    residual = ref.embed(ids, table, 0)
+    return residual, ref.rmsnorm(residual, w, eps, zero_centered)
+
+
 def linear_silu_mul(x: torch.Tensor, w_packed: torch.Tensor) -> torch.Tensor:
     if x.is_cuda:
         return cuda_ops().gemm(x, w_packed, 1)
@@ -53,12 +90,12 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
     """q/k norm + RoPE + KV store + paged causal attention (+ sigmoid output gate)."""
     if qkv.is_cuda:
         c = cuda_ops()
-        q = c.attn_prepare(qkv, batch.positions, batch.slot_mapping, q_norm, k_norm, cos_sin, k_cache, v_cache,
-                           num_heads, num_kv_heads, head_dim, eps, gated, zero_centered)
+        q, gate = c.attn_prepare(qkv, batch.positions, batch.slot_mapping, q_norm, k_norm, cos_sin, k_cache,
+                                 v_cache, num_heads, num_kv_heads, head_dim, eps, gated, zero_centered)
         if batch.is_prefill:
-            return c.attention_prefill(q, qkv, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
+            return c.attention_prefill(q, gate, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
                                        batch.block_tables, scale, gated, batch.max_seqlen_q)
-        return c.attention_decode(q, qkv, k_cache, v_cache, batch.context_lens, batch.block_tables, scale, gated)
+        return c.attention_decode(q, gate, k_cache, v_cache, batch.context_lens, batch.block_tables, scale, gated)
     q, gate, k, v = ref.attn_qkv_prepare(qkv, batch.positions, q_norm, k_norm, cos_sin, num_heads, num_kv_heads,
                                          head_dim, eps, gated, zero_centered)
     ref.store_kv(k, v, k_cache, v_cache, batch.slot_mapping)

@@ -128,8 +128,10 @@ def test_gdn_decode(b, hk, hv):
     exp = ref.gdn_forward(proj, cu, slots.tolist(), conv_w, a_log, dt_bias, norm_w, rec_c, conv_c,
                           hk=hk, hv=hv, dk=128, dv=128, eps=1e-6)
     rec_g, conv_g = rec.to(DEV), conv.to(DEV)
-    out = torch.ops.isb.gdn_decode(proj.to(DEV), slots.to(DEV), conv_w.to(DEV), a_log.to(DEV), dt_bias.to(DEV),
+    proj_acc = proj.float().to(DEV)  # fp32 accumulator input, consumed by the kernel
+    out = torch.ops.isb.gdn_decode(proj_acc, slots.to(DEV), conv_w.to(DEV), a_log.to(DEV), dt_bias.to(DEV),
                                    norm_w.to(DEV), rec_g, conv_g, hk, hv, 128, 128, 1e-6)
+    assert torch.count_nonzero(proj_acc) == 0
     assert _rel(out.cpu(), exp) < 2e-2
     assert _rel(rec_g.cpu(), rec_c) < 1e-4
     assert torch.equal(conv_g.cpu(), conv_c)
@@ -152,6 +154,11 @@ def test_gdn_prefill(lens, hk, hv):
     assert _rel(out.cpu(), exp) < 2e-2
     assert _rel(rec_g.cpu(), rec_c) < 1e-3
     assert torch.equal(conv_g.cpu(), conv_c)
+
+
+def gate_ref(qkv, hq, hd):
+    t = qkv.shape[0]
+    return qkv[:, : hq * hd * 2].reshape(t, hq, 2 * hd)[..., hd:].reshape(t, hq * hd)
 
 
 def _attn_case(seed, hq, hkv, hd, lens_new, lens_past, gated=True):
@@ -200,11 +207,13 @@ def test_attention_prefill(hq, hkv, new, past):
     ref.store_kv(k, v, kc_r, vc_r, m["slot_mapping"])
     exp = ref.paged_attention(q, kc_r, vc_r, m["cu"], m["ctx"], m["bt"], hd ** -0.5, gate)
     kc_g, vc_g = kc.to(DEV), vc.to(DEV)
-    qg = torch.ops.isb.attn_prepare(qkv.to(DEV), m["positions"].to(DEV), m["slot_mapping"].to(DEV), qn.to(DEV),
-                                    kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6, True, True)
+    qg, gate = torch.ops.isb.attn_prepare(qkv.to(DEV), m["positions"].to(DEV), m["slot_mapping"].to(DEV),
+                                          qn.to(DEV), kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6,
+                                          True, True)
     assert _rel(qg.cpu(), q) < 1e-2
+    assert _rel(gate.cpu(), gate_ref(qkv, hq, hd)) == 0
     assert _rel(kc_g.cpu(), kc_r) < 1e-2 and _rel(vc_g.cpu(), vc_r) < 1e-2
-    out = torch.ops.isb.attention_prefill(qg, qkv.to(DEV), kc_g, vc_g, m["cu"].to(DEV), m["ctx"].to(DEV),
+    out = torch.ops.isb.attention_prefill(qg, gate, kc_g, vc_g, m["cu"].to(DEV), m["ctx"].to(DEV),
                                           m["bt"].to(DEV), hd ** -0.5, True, max(new))
     assert _rel(out.cpu(), exp) < 2e-2
 
@@ -220,9 +229,12 @@ def test_attention_decode(hq, hkv, past):
     ref.store_kv(k, v, kc_r, vc_r, m["slot_mapping"])
     exp = ref.paged_attention(q, kc_r, vc_r, m["cu"], m["ctx"], m["bt"], hd ** -0.5, gate)
     kc_g, vc_g = kc.to(DEV), vc.to(DEV)
-    qg = torch.ops.isb.attn_prepare(qkv.to(DEV), m["positions"].to(DEV), m["slot_mapping"].to(DEV), qn.to(DEV),
-                                    kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6, True, True)
-    out = torch.ops.isb.attention_decode(qg, qkv.to(DEV), kc_g, vc_g, m["ctx"].to(DEV), m["bt"].to(DEV),
+    # fp32 accumulator input path: the prepare kernel consumes (re-zeroes) the projection
+    qkv_acc = qkv.float().to(DEV)
+    qg, gate = torch.ops.isb.attn_prepare(qkv_acc, m["positions"].to(DEV), m["slot_mapping"].to(DEV), qn.to(DEV),
+                                          kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6, True, True)
+    assert torch.count_nonzero(qkv_acc) == 0
+    out = torch.ops.isb.attention_decode(qg, gate, kc_g, vc_g, m["ctx"].to(DEV), m["bt"].to(DEV),
                                          hd ** -0.5, True)
     assert _rel(out.cpu(), exp) < 2e-2
 
@@ -244,3 +256,40 @@ def test_state_int8_roundtrip_and_page_copy():
     ops.copy_kv_page(kc, vc, 1, 3, 100)
     assert torch.equal(kc[3, :, :100], k0[1, :, :100]) and torch.equal(kc[3, :, 100:], k0[3, :, 100:])
     assert torch.equal(vc[3, :, :100], v0[1, :, :100])
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1024, 2048), (37, 1024, 3584), (128, 1024, 2048), (300, 1024, 3584)])
+def test_gemm_accumulate_and_norm(m, n, k):
+    g = torch.Generator(device=DEV).manual_seed(m + k)
+    a = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    b = (torch.randn(n, k, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    acc = torch.zeros(m + 3, n, device=DEV)
+    ops.linear_accumulate(a, b, acc)
+    exp = a.float() @ b.float().t()
+    assert _rel(acc[:m], exp) < 1e-3
+    assert torch.count_nonzero(acc[m:]) == 0
+    resid = torch.randn(m, n, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(n, device=DEV) * 0.1).to(torch.bfloat16)
+    r_ref = resid.cpu().clone()
+    exp_out = ref.add_rmsnorm(exp.cpu(), r_ref, w.cpu(), 1e-6, True)
+    out = ops.add_rmsnorm_acc(acc, resid, w, 1e-6, True)
+    assert _rel(out, exp_out) < 1e-2
+    assert _rel(resid, r_ref) < 1e-2
+    assert torch.count_nonzero(acc) == 0, "consumer must re-zero the accumulator"
+
+
+def test_silu_mul_acc():
+    acc = torch.randn(9, 2 * 448, device=DEV)
+    exp = ref.silu_mul_packed(acc.cpu())
+    out = ops.silu_mul_acc(acc, 7)
+    assert _rel(out, exp[:7]) < 1e-2
+    assert torch.count_nonzero(acc[:7]) == 0 and torch.count_nonzero(acc[7:]) > 0
+
+
+def test_embed_rmsnorm():
+    table = torch.randn(500, 1024, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(1024, device=DEV) * 0.1).to(torch.bfloat16)
+    ids = torch.randint(0, 500, (17,), device=DEV, dtype=torch.int32)
+    res, out = ops.embed_rmsnorm(ids, table, w, 1e-6, True)
+    assert torch.equal(res, table[ids.long()])
+    assert _rel(out, ref.rmsnorm(table[ids.long()].cpu(), w.cpu(), 1e-6, True)) < 1e-2
