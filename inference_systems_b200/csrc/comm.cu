@@ -1,0 +1,239 @@
+// Tensor-parallel communication over NVLink peer memory.
+//
+// Symmetric buffers: every rank cudaMalloc's one region, exports a CUDA IPC
+// handle, and maps every peer's region (``symm_alloc`` / ``symm_open``); kernels
+// then address peers with plain device pointers (P2P loads, stores and atomics
+// through NVSwitch).  Synchronisation between ranks uses monotone flag words in
+// the symmetric region: a producer RELEASES ``flags[rank] += 1`` on each peer at
+// system scope, a consumer ACQUIRES until every flag is >= 1 and, when all of its
+// blocks are done, takes the ones it consumed back.  Every wait is bounded by a
+// %globaltimer deadline; a timeout records an error word (read by
+// ``comm_error_word``) and later waits return at once, so a missing peer can
+// never hang a GPU.
+//
+//  * add_rmsnorm_acc_tp: consumer of the fused row-parallel GEMM all-reduce
+//    (gemm.cu ``tp_gemm_accum``): waits for all ranks' tiles, then
+//    residual += acc, out = RMSNorm(residual), acc <- 0.
+//  * xrank_argmax: cross-rank (score, token) argmax of the vocab-parallel LM
+//    head; each rank publishes 8 bytes per row to every peer instead of gathering logits.
+
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+
+namespace isb {
+
+__device__ unsigned int g_comm_err;
+
+namespace {
+
+ISB_DEVICE unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Wait until flags[0..n) are all >= 1 (bounded).  Returns false on timeout.
+ISB_DEVICE bool wait_flags(const unsigned int* flags, int n) {
+  if (*reinterpret_cast<volatile unsigned int*>(&g_comm_err) != 0u) return false;
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < n; ++r) {
+    uint32_t spins = 0;
+    while (ld_acquire_sys(flags + r) < 1u) {
+      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(&g_comm_err, 1u);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+struct Vec8 {
+  float v[8];
+};
+
+__device__ __forceinline__ Vec8 load8(const __nv_bfloat16* p) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  Vec8 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+
+__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// One warp per row (4 rows per block).  Block 0..n: wait, consume, count; the last block
+// returns the consumed flag units.
+__global__ void acc_norm_tp_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
+                                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
+                                   int H, float eps, bool zc, unsigned int* flags, int world, unsigned int* done) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = wait_flags(flags, world);
+  __syncthreads();
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row < rows) {
+    float* a = acc + size_t(row) * H;
+    __nv_bfloat16* res = residual + size_t(row) * H;
+    float ss = 0.f;
+    for (int c = lane * 8; c < H; c += 256) {
+      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
+      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
+      const Vec8 r = load8(res + c);
+      const float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
+                          x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / float(H) + eps);
+    for (int c = lane * 8; c < H; c += 256) {
+      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
+      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
+      const Vec8 r = load8(res + c);
+      float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
+                    x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
+      store8(res + c, v);
+      const Vec8 wv = load8(w + c);
+      float y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        y[i] = zc ? v[i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[i] * rs)) * wv.v[i];
+      store8(out + size_t(row) * H + c, y);
+      *reinterpret_cast<float4*>(a + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(a + c + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(done, 1u);
+    if (prev == gridDim.x - 1) {
+      *done = 0u;
+      if (ok)
+        for (int r = 0; r < world; ++r) atomicSub(flags + r, 1u);
+      __threadfence_system();
+    }
+  }
+}
+
+// Single CTA.  Publish this rank's (score, token) per row to every peer's exchange slot,
+// signal, wait for all ranks, reduce (ties -> smaller token id), write token ids.
+__global__ void xrank_argmax_kernel(const float* __restrict__ val, const int* __restrict__ idx, int B,
+                                    const unsigned long long* xbufs, const unsigned long long* peer_flags,
+                                    unsigned int* my_xbuf_flags, const float2* my_xbuf, int rank, int world,
+                                    int max_rows, int* __restrict__ out) {
+  __shared__ int ok;
+  for (int t = threadIdx.x; t < B; t += blockDim.x) {
+    const float2 e = make_float2(val[t], __int_as_float(idx[t]));
+    for (int r = 0; r < world; ++r)
+      reinterpret_cast<float2*>(xbufs[r])[size_t(rank) * max_rows + t] = e;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.sys;" ::: "memory");
+    for (int r = 0; r < world; ++r) {
+      unsigned int* flag = reinterpret_cast<unsigned int*>(peer_flags[r]) + rank;
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+    }
+    ok = wait_flags(my_xbuf_flags, world);
+  }
+  __syncthreads();
+  for (int t = threadIdx.x; t < B; t += blockDim.x) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int r = 0; r < world; ++r) {
+      const float2 e = __ldcg(my_xbuf + size_t(r) * max_rows + t);
+      const int i = __float_as_int(e.y);
+      if (e.x > best || (e.x == best && i < bi)) { best = e.x; bi = i; }
+    }
+    out[t] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && ok)
+    for (int r = 0; r < world; ++r) atomicSub(my_xbuf_flags + r, 1u);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------- host side
+// Allocate a zeroed device region and return (uint8 tensor view, IPC handle bytes).
+std::tuple<at::Tensor, at::Tensor> symm_alloc(int64_t nbytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, nbytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, nbytes) == cudaSuccess, "symm_alloc: memset failed");
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, p) == cudaSuccess, "symm_alloc: cudaIpcGetMemHandle failed");
+  int dev;
+  cudaGetDevice(&dev);
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, dev);
+  at::Tensor view = at::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+  at::Tensor handle = at::empty({int64_t(sizeof(h))}, at::TensorOptions().dtype(at::kByte));
+  std::memcpy(handle.data_ptr(), &h, sizeof(h));
+  return {view, handle};
+}
+
+int64_t symm_open(const at::Tensor& handle) {
+  TORCH_CHECK(handle.numel() == int64_t(sizeof(cudaIpcMemHandle_t)), "bad IPC handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "symm_open: cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+at::Tensor add_rmsnorm_acc_tp(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc,
+                              at::Tensor flags, at::Tensor done) {
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous(), "accumulator must be contiguous fp32");
+  TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16, "residual must be bf16");
+  TORCH_CHECK(flags.scalar_type() == at::kInt && done.scalar_type() == at::kInt, "int32 flag words");
+  const int H = residual.size(-1), rows = residual.numel() / H;
+  at::Tensor out = at::empty_like(residual);
+  const int blocks = std::max(1, (rows + 3) / 4);
+  acc_norm_tp_kernel<<<blocks, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+      acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows,
+      H, float(eps), zc, reinterpret_cast<unsigned int*>(flags.data_ptr<int>()), int(flags.numel()),
+      reinterpret_cast<unsigned int*>(done.data_ptr<int>()));
+  return out;
+}
+
+at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,
+                        const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
+                        int64_t max_rows) {
+  const int B = val.numel();
+  TORCH_CHECK(B <= max_rows, "xrank_argmax: more rows than the exchange buffer holds");
+  at::Tensor out = at::empty({B}, idx.options());
+  xrank_argmax_kernel<<<1, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+      val.data_ptr<float>(), idx.data_ptr<int>(), B, reinterpret_cast<const unsigned long long*>(xbufs.data_ptr<int64_t>()),
+      reinterpret_cast<const unsigned long long*>(peer_flags.data_ptr<int64_t>()),
+      reinterpret_cast<unsigned int*>(my_flags.data_ptr<int>()), reinterpret_cast<const float2*>(my_xbuf.data_ptr()),
+      int(rank), int(xbufs.numel()), int(max_rows), out.data_ptr<int>());
+  return out;
+}
+
+int64_t comm_error_word() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_comm_err, sizeof(v));
+  const unsigned int z = 0;
+  cudaMemcpyToSymbol(g_comm_err, &z, sizeof(z));
+  return v;
+}
+
+}  // namespace isb

@@ -64,6 +64,12 @@ struct GemmArgs {
   float* ws;                // split-K partials [tiles][splits][BM][BN] fp32
   float* acc;               // kRedAdd: fp32 accumulator [tokens][features], atomically added to
   unsigned int* counters;   // split-K arrival counters (self-resetting)
+  // kRedAdd across tensor-parallel ranks: the tile is added into every rank's accumulator
+  const unsigned long long* dsts;  // [ndst] accumulator base pointers (peer memory), or null
+  int ndst;
+  unsigned int* done_ctr;          // local CTA-completion counter (self-resetting)
+  const unsigned long long* peer_flags;  // [ndst] flag-array base of each rank; flag index = rank
+  int rank;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -76,6 +82,31 @@ __device__ unsigned int g_splitk_counters[kCounterSlots * kCountersPerSlot];
 ISB_DEVICE void red_add_v4(float* p, float a, float b, float c, float d) {
   asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
+}
+
+ISB_DEVICE void red_add_v4_sys(float* p, float a, float b, float c, float d) {
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Add 4 consecutive values at element offset ``off`` of the accumulator(s).
+ISB_DEVICE void acc_add4(const GemmArgs& args, size_t off, float a, float b, float c, float d) {
+  if (args.ndst == 0) {
+    red_add_v4(args.acc + off, a, b, c, d);
+    return;
+  }
+  for (int r = 0; r < args.ndst; ++r) {
+    const int dst = (args.rank + r) % args.ndst;  // stagger the peers
+    red_add_v4_sys(reinterpret_cast<float*>(args.dsts[dst]) + off, a, b, c, d);
+  }
+}
+
+ISB_DEVICE void acc_add1(const GemmArgs& args, size_t off, float a) {
+  if (args.ndst == 0) {
+    atomicAdd(args.acc + off, a);
+    return;
+  }
+  for (int r = 0; r < args.ndst; ++r) atomicAdd_system(reinterpret_cast<float*>(args.dsts[r]) + off, a);
 }
 
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
@@ -310,14 +341,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int t = p0 + row;
             const int col0 = q0 + c * CH;
             if (t < args.P_rows) {
-              float* dst = args.acc + size_t(t) * args.ldo + col0;
+              const size_t off = size_t(t) * args.ldo + col0;
               if (col0 + CH <= args.Q_rows && (args.ldo % 4) == 0) {
 #pragma unroll
-                for (int j = 0; j < CH / 4; ++j) red_add_v4(dst + 4 * j, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+                for (int j = 0; j < CH / 4; ++j) acc_add4(args, off + 4 * j, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
               } else {
 #pragma unroll
                 for (int j = 0; j < CH; ++j)
-                  if (col0 + j < args.Q_rows) atomicAdd(dst + j, v[j]);
+                  if (col0 + j < args.Q_rows) acc_add1(args, off + j, v[j]);
               }
             }
           }
@@ -394,12 +425,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int tok = q0 + t, f = p0 + f4;
           if (tok >= args.Q_rows || f >= args.P_rows) continue;
           const float4 w = *reinterpret_cast<const float4*>(fstage + t * BM + f4);
-          float* dst = args.acc + size_t(tok) * args.ldo + f;
+          const size_t off = size_t(tok) * args.ldo + f;
           if (vec_ok && f + 3 < args.P_rows) {
-            red_add_v4(dst, w.x, w.y, w.z, w.w);
+            acc_add4(args, off, w.x, w.y, w.z, w.w);
           } else {
             const float e[4] = {w.x, w.y, w.z, w.w};
-            for (int k = 0; k < 4 && f + k < args.P_rows; ++k) atomicAdd(dst + k, e[k]);
+            for (int k = 0; k < 4 && f + k < args.P_rows; ++k) acc_add1(args, off + k, e[k]);
           }
         }
       }
@@ -420,6 +451,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (dbg && threadIdx.x == 64) dbg[6] = globaltimer_ns();
+  if constexpr (EPI == kRedAdd) {
+    if (args.ndst > 0) {
+      // every rank's accumulator got this CTA's tile: count the CTA; the last one releases
+      // a flag on every rank (flag index = this rank) at system scope.
+      if (epi) asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+        unsigned int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(args.done_ctr) : "memory");
+        if (prev == total - 1) {
+          *args.done_ctr = 0u;
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          for (int r = 0; r < args.ndst; ++r) {
+            unsigned int* flag = reinterpret_cast<unsigned int*>(args.peer_flags[r]) + args.rank;
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+          }
+        }
+      }
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
@@ -676,6 +728,43 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   args.kb_per_split = p.kb_per;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+}
+
+// Tensor-parallel row-parallel GEMM fused with the all-reduce: every CTA adds its fp32 tile
+// into the accumulator of EVERY rank (peer memory, system-scope vector atomics over NVLink);
+// the grid's last CTA then releases flag[rank] on each rank.  ``dsts`` / ``flags`` are int64
+// device tensors of the ranks' accumulator / flag-array base addresses.
+void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& dsts, const at::Tensor& flags,
+                   at::Tensor done_ctr, int64_t rank, int64_t splits) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(dsts.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && dsts.numel() == flags.numel(),
+              "dsts / flags must be int64 device tables of equal length");
+  TORCH_CHECK(done_ctr.scalar_type() == at::kInt, "done counter must be int32");
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  Plan p = plan_gemm(a, b, false, 1);
+  int sp = splits > 0 ? int(splits) : 1;
+  if (splits <= 0) {
+    const int tiles = p.tiles_p * p.tiles_q;
+    while (sp < 16 && tiles * sp * 2 <= 2 * num_sms() && kb_total / (sp * 2) >= 2) sp *= 2;
+  }
+  p.kb_per = (kb_total + sp - 1) / sp;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  GemmArgs args = {};
+  args.K = a.size(1);
+  args.ldo = N;
+  args.kb_per_split = p.kb_per;
+  args.dsts = reinterpret_cast<const unsigned long long*>(dsts.data_ptr<int64_t>());
+  args.ndst = int(dsts.numel());
+  args.done_ctr = reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>());
+  args.peer_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
+  args.rank = int(rank);
+  if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (M == 0) return;
   if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }

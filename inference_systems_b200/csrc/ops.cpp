@@ -53,8 +53,19 @@ void dequantize_state_int8(const at::Tensor& q, const at::Tensor& scale, at::Ten
 void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_t n);
 
 int64_t attn_error_word();
+int64_t comm_error_word();
+void tp_gemm_accum(const at::Tensor& a, const at::Tensor& b, const at::Tensor& dsts, const at::Tensor& flags,
+                   at::Tensor done_ctr, int64_t rank, int64_t splits);
+std::tuple<at::Tensor, at::Tensor> symm_alloc(int64_t nbytes);
+int64_t symm_open(const at::Tensor& handle);
+void symm_close(int64_t ptr);
+at::Tensor add_rmsnorm_acc_tp(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc,
+                              at::Tensor flags, at::Tensor done);
+at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,
+                        const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
+                        int64_t max_rows);
 
-int64_t error_word() { return gemm_error_word() | (attn_error_word() << 8); }
+int64_t error_word() { return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16); }
 }  // namespace isb
 
 TORCH_LIBRARY(isb, m) {
@@ -98,6 +109,14 @@ TORCH_LIBRARY(isb, m) {
   m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
+  m.def("tp_gemm_accum(Tensor a, Tensor b, Tensor dsts, Tensor flags, Tensor(a!) done_ctr, int rank, int splits=0) -> ()");
+  m.def("symm_alloc(int nbytes) -> (Tensor, Tensor)");
+  m.def("symm_open(Tensor handle) -> int");
+  m.def("symm_close(int ptr) -> ()");
+  m.def("add_rmsnorm_acc_tp(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered, "
+        "Tensor(c!) flags, Tensor(d!) done) -> Tensor");
+  m.def("xrank_argmax(Tensor val, Tensor idx, Tensor xbufs, Tensor peer_flags, Tensor(a!) my_flags, Tensor my_xbuf, "
+        "int rank, int max_rows) -> Tensor");
 }
 
 TORCH_LIBRARY_IMPL(isb, CUDA, m) {
@@ -122,8 +141,16 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("gemm_accum", &isb::gemm_accum);
   m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);
   m.impl("silu_mul_acc", &isb::silu_mul_acc);
+  m.impl("tp_gemm_accum", &isb::tp_gemm_accum);
+  m.impl("add_rmsnorm_acc_tp", &isb::add_rmsnorm_acc_tp);
+  m.impl("xrank_argmax", &isb::xrank_argmax);
 }
 
-TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) { m.impl("error_word", &isb::error_word); }
+TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) {
+  m.impl("error_word", &isb::error_word);
+  m.impl("symm_alloc", &isb::symm_alloc);
+  m.impl("symm_open", &isb::symm_open);
+  m.impl("symm_close", &isb::symm_close);
+}
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "sm_100a kernels (torch.ops.isb)"; }

@@ -77,8 +77,10 @@ class ModelRunner:
             torch.cuda.set_device(self.device)
         if self.world_size > 1 and not dist.is_initialized():
             from datetime import timedelta
-            dist.init_process_group("nccl" if use_cuda else "gloo",
-                                    init_method=f"tcp://127.0.0.1:{config.dist_port}",
+            from inference_systems_b200.engine.llm_engine import externally_launched
+            # under torch.distributed.run the launcher owns the rendezvous store (env://)
+            init = "env://" if externally_launched(self.world_size) else f"tcp://127.0.0.1:{config.dist_port}"
+            dist.init_process_group("nccl" if use_cuda else "gloo", init_method=init,
                                     world_size=self.world_size, rank=rank,
                                     timeout=timedelta(seconds=config.dist_timeout_s))
         self.dtype = config.torch_dtype
