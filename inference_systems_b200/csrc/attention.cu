@@ -559,3 +559,148 @@ at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const 
 }
 
 }  // namespace isb
+
+// ------------------------------------------------------------ no-alloc entry
+// The C entry point declared in noalloc.h (no counterpart in the reference):
+// the same decode + combine kernels as attention_decode, with the split-KV
+// partials in a fixed device array instead of tensors from the allocator.
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace isb {
+namespace {
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[ISB_NOALLOC_SCRATCH_BYTES];
+
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+
+size_t part_o_bytes(int B, int Hq, int hd, int max_chunks) {
+  return (size_t(B) * Hq * max_chunks * hd * sizeof(float) + 255) / 256 * 256;
+}
+
+template <int HD, int G>
+int decode_smem() {
+  return 2 * DCHUNK * HD * 2 + (G * HD + G * DCHUNK) * 4;
+}
+
+template <int HD, int G>
+bool set_decode_attr() {
+  return cudaFuncSetAttribute(attn_decode_kernel<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                              decode_smem<HD, G>()) == cudaSuccess;
+}
+
+// Returns this device's scratch pointer, running the one-time set-up first.
+unsigned char* noalloc_scratch(int* code) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    *code = ISB_NOALLOC_ESETUP;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+      *code = ISB_NOALLOC_ESETUP;
+      return nullptr;
+    }
+    const bool ok = set_decode_attr<256, 1>() && set_decode_attr<256, 2>() && set_decode_attr<256, 3>() &&
+                    set_decode_attr<256, 4>() && set_decode_attr<256, 6>() && set_decode_attr<256, 8>() &&
+                    set_decode_attr<128, 1>() && set_decode_attr<128, 2>() && set_decode_attr<128, 4>();
+    if (!ok) {
+      *code = ISB_NOALLOC_ESETUP;
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *code = ISB_NOALLOC_OK;
+  return g_noalloc_ptr[dev];
+}
+
+template <int HD, int G>
+void launch_decode_noalloc(const __nv_bfloat16* q, const __nv_bfloat16* kc, const __nv_bfloat16* vc,
+                           const int* ctx_lens, const int* bt, int max_blocks, int B, int Hkv, float scale,
+                           float* part_o, float* part_ml, int max_chunks, cudaStream_t st) {
+  attn_decode_kernel<HD, G><<<dim3(Hkv, B, max_chunks), 256, decode_smem<HD, G>(), st>>>(
+      q, kc, vc, ctx_lens, bt, max_blocks, Hkv, scale, part_o, part_ml, max_chunks);
+}
+
+}  // namespace
+}  // namespace isb
+
+extern "C" {
+
+__attribute__((visibility("default"))) size_t isb_attention_decode_noalloc_scratch_bytes(int batch, int num_q_heads,
+                                                                                         int head_dim,
+                                                                                         int max_blocks) {
+  if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks <= 0) return 0;
+  const int max_chunks = max_blocks * (isb::PAGE / isb::DCHUNK);
+  return isb::part_o_bytes(batch, num_q_heads, head_dim, max_chunks) +
+         size_t(batch) * num_q_heads * max_chunks * 2 * sizeof(float);
+}
+
+__attribute__((visibility("default"))) int isb_noalloc_setup(void) {
+  int code = ISB_NOALLOC_OK;
+  isb::noalloc_scratch(&code);
+  return code;
+}
+
+__attribute__((visibility("default"))) int isb_attention_decode_noalloc(
+    const void* q, const void* gate, const void* k_cache, const void* v_cache, const int* ctx_lens,
+    const int* block_tables, int max_blocks, int batch, int num_q_heads, int num_kv_heads, int head_dim, float scale,
+    void* out, cudaStream_t stream) {
+  if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks <= 0)
+    return ISB_NOALLOC_EINVAL;
+  // Size check first: it never touches a pointer.
+  const size_t need = isb_attention_decode_noalloc_scratch_bytes(batch, num_q_heads, head_dim, max_blocks);
+  if (need > ISB_NOALLOC_SCRATCH_BYTES) return ISB_NOALLOC_ETOOBIG;
+  if (!q || !k_cache || !v_cache || !ctx_lens || !block_tables || !out) return ISB_NOALLOC_EINVAL;
+  if (num_q_heads % num_kv_heads != 0) return ISB_NOALLOC_EUNSUPPORTED;
+  const int G = num_q_heads / num_kv_heads;
+  const bool hd256 = head_dim == 256 && (G == 1 || G == 2 || G == 3 || G == 4 || G == 6 || G == 8);
+  const bool hd128 = head_dim == 128 && (G == 1 || G == 2 || G == 4);
+  if (!hd256 && !hd128) return ISB_NOALLOC_EUNSUPPORTED;
+
+  int code = ISB_NOALLOC_OK;
+  unsigned char* scratch = isb::noalloc_scratch(&code);
+  if (scratch == nullptr) return code;
+  const int max_chunks = max_blocks * (isb::PAGE / isb::DCHUNK);
+  float* part_o = reinterpret_cast<float*>(scratch);
+  float* part_ml = reinterpret_cast<float*>(scratch + isb::part_o_bytes(batch, num_q_heads, head_dim, max_chunks));
+
+  const auto* qb = static_cast<const __nv_bfloat16*>(q);
+  const auto* kb = static_cast<const __nv_bfloat16*>(k_cache);
+  const auto* vb = static_cast<const __nv_bfloat16*>(v_cache);
+#define ISB_NA_DEC(HD_, G_)                                                                                   \
+  if (head_dim == HD_ && G == G_)                                                                             \
+    isb::launch_decode_noalloc<HD_, G_>(qb, kb, vb, ctx_lens, block_tables, max_blocks, batch, num_kv_heads,   \
+                                        scale, part_o, part_ml, max_chunks, stream);
+  ISB_NA_DEC(256, 1) ISB_NA_DEC(256, 2) ISB_NA_DEC(256, 3) ISB_NA_DEC(256, 4) ISB_NA_DEC(256, 6) ISB_NA_DEC(256, 8)
+  ISB_NA_DEC(128, 1) ISB_NA_DEC(128, 2) ISB_NA_DEC(128, 4)
+#undef ISB_NA_DEC
+  const auto* gb = static_cast<const __nv_bfloat16*>(gate);
+  auto* ob = static_cast<__nv_bfloat16*>(out);
+  if (head_dim == 256)
+    isb::attn_combine_kernel<256><<<dim3(num_q_heads, batch), 256, 0, stream>>>(
+        part_o, part_ml, max_chunks, isb::DCHUNK, ctx_lens, gb, gb != nullptr, ob, num_q_heads);
+  else
+    isb::attn_combine_kernel<128><<<dim3(num_q_heads, batch), 128, 0, stream>>>(
+        part_o, part_ml, max_chunks, isb::DCHUNK, ctx_lens, gb, gb != nullptr, ob, num_q_heads);
+  return cudaGetLastError() == cudaSuccess ? ISB_NOALLOC_OK : ISB_NOALLOC_ELAUNCH;
+}
+
+__attribute__((visibility("default"))) const char* isb_noalloc_strerror(int code) {
+  switch (code) {
+    case ISB_NOALLOC_OK: return "ok";
+    case ISB_NOALLOC_ETOOBIG: return "split-KV partials exceed the fixed scratch array (ISB_NOALLOC_SCRATCH_BYTES)";
+    case ISB_NOALLOC_EUNSUPPORTED: return "unsupported (head_dim, q heads per kv head)";
+    case ISB_NOALLOC_EINVAL: return "null pointer or non-positive size";
+    case ISB_NOALLOC_ESETUP: return "per-device set-up failed (cudaGetSymbolAddress or kernel attribute)";
+    case ISB_NOALLOC_ELAUNCH: return "kernel launch failed";
+    default: return "unknown code";
+  }
+}
+
+}  // extern "C"
