@@ -202,9 +202,11 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
       }
       const int hrow = a.hist_row ? a.hist_row[t] : -1;
       if (hrow >= 0) {
-        float* HS = a.hist_rec + ((size_t(hrow) * a.Hv + h) * D) * D;
+        if (a.hist_rec) {  // conv-only history (MTP verify) skips the 64 KB state snapshot
+          float* HS = a.hist_rec + ((size_t(hrow) * a.Hv + h) * D) * D;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) *reinterpret_cast<float4*>(HS + (kr * 16 + i) * D + vc) = st[i];
+          for (int i = 0; i < 16; ++i) *reinterpret_cast<float4*>(HS + (kr * 16 + i) * D + vc) = st[i];
+        }
         __nv_bfloat16* hc = a.hist_conv + size_t(hrow) * a.C * (KW - 1);
         if (j == 0) {
           __nv_bfloat16* p = hc + size_t(qk_ch) * (KW - 1);
@@ -243,7 +245,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
 __global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int pool_slots, const int* slots,
                                                                  const float* keys, const float* deltas,
                                                                  const float* gs, const int* lens, int steps, int B,
-                                                                 int Hv) {
+                                                                 int Hv, int layer_rows) {
   const int h = blockIdx.x, b = blockIdx.y, l = blockIdx.z;
   const int tid = threadIdx.x, kr = tid >> 5, vc = (tid & 31) * 4;
   const int n = min(max(lens[b], 0), steps);
@@ -253,7 +255,7 @@ __global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int
 #pragma unroll
   for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
   for (int t = 0; t < n; ++t) {
-    const size_t row = (size_t(l) * B * steps + size_t(b) * steps + t) * Hv + h;
+    const size_t row = (size_t(l) * layer_rows + size_t(b) * steps + t) * Hv + h;
     const float e = expf(gs[row]);
     const float4 dl = *reinterpret_cast<const float4*>(deltas + row * D + vc);
 #pragma unroll
@@ -366,9 +368,9 @@ at::Tensor gdn_scan_history(const at::Tensor& proj, const at::Tensor& cu_seqlens
   a.cu_seqlens = cu_seqlens.data_ptr<int>();
   a.write_final = write_final;
   if (hist_row.has_value()) {
-    TORCH_CHECK(hist_rec.has_value() && hist_conv.has_value(), "history needs recurrent and conv buffers");
+    TORCH_CHECK(hist_conv.has_value(), "history needs a conv buffer (the recurrent one is optional)");
     a.hist_row = hist_row->data_ptr<int>();
-    a.hist_rec = hist_rec->data_ptr<float>();
+    a.hist_rec = hist_rec.has_value() ? hist_rec->data_ptr<float>() : nullptr;
     a.hist_conv = reinterpret_cast<__nv_bfloat16*>(hist_conv->data_ptr());
   }
   if (rec_k.has_value()) {
@@ -385,12 +387,16 @@ void gdn_replay_commit(at::Tensor rec, const at::Tensor& slots, const at::Tensor
   TORCH_CHECK(rec.dim() == 5 && rec.size(3) == D && rec.size(4) == D, "recurrent pool must be [L, S, Hv, 128, 128]");
   const int L = rec.size(0), B = slots.numel(), Hv = rec.size(2);
   if (B == 0) return;
+  // records are [L, rows, Hv, D] (rows >= B * steps; row b * steps + t of each layer is read)
+  TORCH_CHECK(keys.dim() == 4 && keys.size(0) == L && keys.size(1) >= int64_t(B) * steps && keys.size(2) == Hv,
+              "replay keys must be [L, rows >= B*steps, Hv, 128]");
+  TORCH_CHECK(deltas.sizes() == keys.sizes() && gs.dim() == 3 && gs.size(1) == keys.size(1), "replay record shapes");
   at::Tensor k = keys.to(at::kFloat).contiguous(), d = deltas.to(at::kFloat).contiguous(),
              g = gs.to(at::kFloat).contiguous();
   at::Tensor sl = slots.to(at::kInt).contiguous(), ln = lens.to(at::kInt).contiguous();
   replay_commit_kernel<<<dim3(Hv, B, L), kThreads, 0, at::cuda::getCurrentCUDAStream()>>>(
       rec.data_ptr<float>(), rec.size(1), sl.data_ptr<int>(), k.data_ptr<float>(), d.data_ptr<float>(),
-      g.data_ptr<float>(), ln.data_ptr<int>(), int(steps), B, Hv);
+      g.data_ptr<float>(), ln.data_ptr<int>(), int(steps), B, Hv, int(k.size(1)));
 }
 
 void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& slots, const at::Tensor& bounds,
@@ -398,6 +404,8 @@ void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& 
   TORCH_CHECK(conv.dim() == 4 && hist.dim() == 4, "conv pool [L,S,C,3], history [L,rows,C,3]");
   const int L = conv.size(0), B = slots.numel();
   if (B == 0) return;
+  TORCH_CHECK(hist.size(0) == L && hist.size(1) >= int64_t(B) * steps && hist.size(2) == conv.size(2),
+              "conv history must be [L, rows >= B*steps, C, 3]");
   at::Tensor sl = slots.to(at::kInt).contiguous(), bd = bounds.to(at::kInt).contiguous();
   at::Tensor h = hist.contiguous();
   conv_commit_kernel<<<dim3(B, L), 256, 0, at::cuda::getCurrentCUDAStream()>>>(

@@ -111,6 +111,13 @@ class LLMEngine:
     # --------------------------------------------------------------- requests
     def add_request(self, prompt: str | list[int], sampling_params: SamplingParams,
                     arrival_time_ns: int | None = None) -> int:
+        seq = self.make_request(prompt, sampling_params, arrival_time_ns)
+        self.scheduler.add(seq)
+        return seq.seq_id
+
+    def make_request(self, prompt: str | list[int], sampling_params: SamplingParams,
+                     arrival_time_ns: int | None = None) -> Sequence:
+        """Validate and tokenize a request without touching the scheduler (any thread may call it)."""
         if isinstance(prompt, str):
             if self.tokenizer is None:
                 raise ValueError("this model directory has no tokenizer; pass token ids")
@@ -119,9 +126,9 @@ class LLMEngine:
             raise ValueError("native MTP speculative decoding currently supports greedy sampling only")
         if len(prompt) > self.config.max_model_len:
             raise ValueError("prompt exceeds max_model_len")
-        seq = Sequence(prompt, sampling_params, arrival_time_ns=arrival_time_ns)
-        self.scheduler.add(seq)
-        return seq.seq_id
+        if not prompt:
+            raise ValueError("prompt must contain at least one token")
+        return Sequence(prompt, sampling_params, arrival_time_ns=arrival_time_ns)
 
     def abort_request(self, request_id: int) -> bool:
         return self.scheduler.abort(request_id)

@@ -136,7 +136,8 @@ class ModelRunner:
 
         # --------------------------------------------------------- KV cache
         self.allocate_kv_cache()
-        self.max_blocks_per_seq = (config.max_model_len + self.num_speculative_tokens + self.block_size) // self.block_size + 1
+        # speculative rounds touch positions up to pending + 2K - 1 (target verify + MTP drafts)
+        self.max_blocks_per_seq = (config.max_model_len + 2 * self.num_speculative_tokens + self.block_size) // self.block_size + 1
         self.sample_step = 0
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_bufs: dict[int, dict] = {}
@@ -351,6 +352,8 @@ class ModelRunner:
             dev = self._upload(flat)
             batch, rng, temps = self._batch_from(dev, layout, meta, is_prefill)
             toks = self._forward_sample(batch, rng, temps)
+            if is_prefill and self.mtp is not None:
+                self.mtp_driver.after_prefill(seqs, batch, self._last_hidden, toks, rng)
             if is_prefill and internal_boundaries:
                 self._capture_internal_states(seqs, internal_boundaries)
         self.sample_step += 1

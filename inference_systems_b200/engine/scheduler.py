@@ -671,6 +671,10 @@ class Scheduler:
                 self.stats["chunked_prefill_steps"] += 1
             used += seq.num_scheduled_tokens
             if seq.num_cached_tokens + seq.num_scheduled_tokens == seq.num_tokens:
+                # the MTP head drafts right after the last prefill chunk: pages for its cache rows
+                k = self.num_speculative_tokens
+                if k and self.block_manager.can_reserve_append(seq, k):
+                    self.block_manager.reserve_append(seq, k)
                 seq.status = SequenceStatus.RUNNING
                 self.waiting.popleft()
                 self.running.append(seq)
@@ -681,7 +685,8 @@ class Scheduler:
     def _schedule_decode(self, sequence_budget: int) -> list[Sequence]:
         t0 = perf_counter_ns()
         out: list[Sequence] = []
-        reserve = self.num_speculative_tokens + 1
+        # a speculative round writes target KV at pending..pending+K and MTP KV up to pending+2K-1
+        reserve = 2 * self.num_speculative_tokens
         while self.running and len(out) < sequence_budget:
             seq = self.running.popleft()
 

@@ -203,11 +203,15 @@ class GDNMixer(nn.Module):
             "out_proj": ([f"{p}.out_proj.weight"], lambda g: _rows(g(f"{p}.out_proj.weight"), tp.rank, tp.size, 1)),
         }
 
-    def forward(self, x: torch.Tensor, batch: ForwardBatch, pools: tuple[torch.Tensor, torch.Tensor]) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, batch: ForwardBatch, pools: tuple[torch.Tensor, torch.Tensor],
+                records: tuple | None = None) -> torch.Tensor:
         proj = self.scratch.project(x, self.in_proj) if self.scratch is not None else None
         if proj is None:
             proj = ops.linear(x, self.in_proj)
         rec_pool, conv_pool = pools
+        if records is not None:
+            return ops.gdn_verify(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool,
+                                  conv_pool, *records, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
         return ops.gdn(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool, conv_pool,
                        hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
 
@@ -391,7 +395,8 @@ class HybridCausalLM(nn.Module):
         attn_j = gdn_j = 0
         for i, layer in enumerate(layers):
             if layer.is_linear:
-                y = layer.mixer(x, batch, state_pools[gdn_j])
+                rec = batch.gdn_verify[gdn_j] if batch.gdn_verify is not None else None
+                y = layer.mixer(x, batch, state_pools[gdn_j], rec)
                 gdn_j += 1
             else:
                 y = layer.mixer(x, batch, kv_caches[attn_j], cos_sin)

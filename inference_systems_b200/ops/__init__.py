@@ -117,6 +117,40 @@ def gdn(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w,
                            rec_pool, conv_pool, hk=hk, hv=hv, dk=dk, dv=dv, eps=eps)
 
 
+def gdn_verify(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool,
+               rec_k: torch.Tensor, rec_delta: torch.Tensor, rec_g: torch.Tensor, conv_hist: torch.Tensor, *,
+               hk: int, hv: int, dk: int, dv: int, eps: float) -> torch.Tensor:
+    """GDN mixer over speculative rows without touching the slot pools.
+
+    Every token row ``t`` records its replay terms (``rec_k[t] = k_t``,
+    ``rec_delta[t] = delta_t``, ``rec_g[t] = log decay_t``) and the conv window
+    after it (``conv_hist[t]``), so the accepted prefix can later be folded into
+    the pool state (``gdn_replay_commit``) and its conv window copied
+    (``gdn_conv_commit``).  Parity: the reference's ReplaySSM verify
+    (``nanovllm/engine/model_runner.py:1520-1569``).
+    """
+    if proj.is_cuda:
+        rows = torch.arange(proj.shape[0], device=proj.device, dtype=torch.int32)
+        return cuda_ops().gdn_scan_history(proj, batch.cu_seqlens_q, batch.state_slots, conv_w, a_log, dt_bias,
+                                           norm_w, rec_pool, conv_pool, hk, hv, eps, False, rows, None, conv_hist,
+                                           rec_k, rec_delta, rec_g)
+    out = torch.empty(proj.shape[0], hv * dv, dtype=proj.dtype, device=proj.device)
+    cu = batch.cu_seqlens_host
+    for i, slot in enumerate(batch.slots_host):
+        s, e = cu[i], cu[i + 1]
+        if e == s:
+            continue
+        y, _, _, _, conv_h, (k, d, g) = ref.gdn_sequence(
+            proj[s:e], conv_w, a_log, dt_bias, norm_w, rec_pool[slot], conv_pool[slot], hk=hk, hv=hv, dk=dk,
+            dv=dv, eps=eps, history_at=list(range(e - s)), return_records=True)
+        out[s:e] = y
+        rec_k[s:e] = k
+        rec_delta[s:e] = d
+        rec_g[s:e] = g
+        conv_hist[s:e] = torch.stack(conv_h)
+    return out
+
+
 def lm_head_sample(hidden: torch.Tensor, weight: torch.Tensor, temperatures: torch.Tensor, rng: torch.Tensor,
                    vocab_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
     """LM-head GEMM fused with greedy / Gumbel-max selection over this rank's vocab slice.
@@ -185,9 +219,10 @@ def gdn_replay_commit(rec_states: torch.Tensor, slot_ids: torch.Tensor, keys: to
     b = slot_ids.numel()
     idx = slot_ids.long()
     state = rec_states.index_select(1, idx)
-    k = keys.view(keys.shape[0], b, num_steps, *keys.shape[2:]).float()
-    d = deltas.view(deltas.shape[0], b, num_steps, *deltas.shape[2:]).float()
-    g = log_decays.view(log_decays.shape[0], b, num_steps, *log_decays.shape[2:]).float()
+    rows = b * num_steps  # records are [L, rows >= b*steps, ...]; the first b*steps rows are read
+    k = keys[:, :rows].reshape(keys.shape[0], b, num_steps, *keys.shape[2:]).float()
+    d = deltas[:, :rows].reshape(deltas.shape[0], b, num_steps, *deltas.shape[2:]).float()
+    g = log_decays[:, :rows].reshape(log_decays.shape[0], b, num_steps, *log_decays.shape[2:]).float()
     lens = commit_lengths.long()
     for t in range(num_steps):
         upd = state * g[:, :, t].exp()[..., None, None] + torch.einsum("lbhd,lbhv->lbhdv", k[:, :, t], d[:, :, t])

@@ -33,6 +33,9 @@ class ForwardBatch:
     num_seqs: int = 0
     # GDN state capture for checkpoints / MTP verify: (seq, token offset) -> buffer row
     gdn_history: dict | None = None
+    # MTP verify: per GDN layer (rec_k, rec_delta, rec_g, conv_hist) record buffers; the
+    # slot pools are then left untouched (see ops.gdn_verify)
+    gdn_verify: list | None = None
 
     @property
     def num_tokens(self) -> int:
