@@ -26,7 +26,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -40,9 +39,10 @@ MODEL = "qwen3_5-0.8b"
 def parse():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=64)
+    p.add_argument("--steps", type=int, default=128)
     p.add_argument("--warmup", type=int, default=8)
     p.add_argument("--batch", type=int, default=128)
+    p.add_argument("--sweep", default=None, help="extra batch sizes, e.g. 1,8,32 (reported under 'sweep')")
     p.add_argument("--prompt-len", type=int, default=512)
     p.add_argument("--output-len", type=int, default=256)
     p.add_argument("--impl", default="isb", choices=["isb", "reference"])
@@ -76,148 +76,189 @@ def kernel_breakdown(replay, path: str, n: int = 3) -> None:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and clock-event reasons through NVML every ``period_s`` (read-only)."""
 
-    def __init__(self, gpu: int):
-        self.gpu = gpu
-        self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_gpu{gpu}.csv")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
+
+    def __init__(self, gpu: int, period_s: float = 0.01):
+        self.gpu, self.period = gpu, period_s
+        self.rows: list[tuple[float, float, int]] = []
+        self.max_mhz = None
+        self._stop = None
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        import threading
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
-                                         stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self._h = h
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001 - no NVML: report unsampled
+            self._nvml = None
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            n = self._nvml
+            while not self._stop.is_set():
+                try:
+                    self.rows.append((float(n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)),
+                                      n.nvmlDeviceGetPowerUsage(self._h) / 1000.0,
+                                      int(n.nvmlDeviceGetCurrentClocksEventReasons(self._h))))
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(self.period)
+
+        self._t = threading.Thread(target=loop, daemon=True)
+        self._t.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.fh.close()
+        if self._stop is not None:
+            self._stop.set()
+            self._t.join(timeout=2)
 
     def summary(self) -> dict:
-        if self.proc is None or not os.path.exists(self.path):
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        rows = []
-        for line in open(self.path):
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]) if parts[3] not in ("[N/A]", "N/A") else 0.0,
-                             parts[5:9]))
-            except ValueError:
-                continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        loaded = [r for r in rows if r[2] > 200.0] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "samples": 0}
+        loaded = [r for r in self.rows if r[1] > 200.0] or self.rows
+        n = self._nvml
+        reasons = sorted({name for name, attr in self.REASONS for r in loaded if r[2] & getattr(n, attr)})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(loaded), "power_w_median": round(statistics.median(r[1] for r in loaded), 1),
+                "source": "NVML every 10 ms during the timed regions"}
 
 
 # --------------------------------------------------------------- own engine
-def run_isb(args, rank: int, world: int) -> dict | None:
+def _p50(xs):
+    xs = sorted(x for x in xs if x is not None)
+    return round(xs[len(xs) // 2], 3) if xs else None
+
+
+def _serve_batch(llm, runner, cfg, b: int, args, clk) -> dict:
+    """B requests (512-token prompts) generated to completion through ``LLMEngine.step``.
+
+    Returns the end-to-end decode throughput over exactly ``steps`` decode
+    steps (after ``warmup`` decode steps), per-request TTFT/TPOT p50, and the
+    device-timed decode throughput of ``steps`` graph replays at this batch.
+    """
     import torch
 
     from inference_systems_b200 import SamplingParams
-    from inference_systems_b200.engine.llm_engine import LLMEngine, serve_worker
-    from inference_systems_b200.models.presets import preset
 
-    cfg = preset(args.model)
-    b = args.batch
-    total_steps = args.steps + args.warmup
-    kw = dict(load_format="dummy", device="cuda", tensor_parallel_size=world, max_num_seqs=b,
-              max_num_state_slots=b, max_model_len=args.prompt_len + args.output_len + total_steps + 32,
-              max_num_batched_tokens=16384, max_cudagraph_batch_size=b, enforce_eager=False,
-              dist_port=int(os.environ.get("MASTER_PORT", "29500")) + 17, gpu_memory_utilization=0.85)
-    if world > 1 and rank > 0:
-        serve_worker(cfg, **kw)
-        return None
-    llm = LLMEngine(cfg, **kw)
-    g = torch.Generator().manual_seed(0)
+    g = torch.Generator().manual_seed(b)
     prompts = torch.randint(0, cfg["vocab_size"], (b, args.prompt_len), generator=g).tolist()
-    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len + total_steps + 8, ignore_eos=True)
+    out_len = max(args.output_len, args.warmup + args.steps + 2)
+    sp = SamplingParams(temperature=0.0, max_tokens=out_len, ignore_eos=True)
+    llm.scheduler.reset_metrics()
     for p in prompts:
         llm.add_request(p, sp)
-    # prefill until every request produced its first token
     t0 = time.perf_counter()
     while llm.scheduler.waiting or any(s.num_completion_tokens == 0 for s in llm.scheduler.running):
         llm.step()
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
-    runner = llm.model_runner
     for _ in range(args.warmup):
         llm.step()
     torch.cuda.synchronize()
-
-    # ---------------- end-to-end: public engine API, K steps
     h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        torch.cuda.synchronize()
-        ev0.record()
-        wall0 = time.perf_counter()
-        decoded = 0
-        for _ in range(args.steps):
-            _, stats = llm.step()
-            decoded += stats.decode_tokens
-        ev1.record()
-        torch.cuda.synchronize()
-        wall_e2e = time.perf_counter() - wall0
-        e2e_ms = ev0.elapsed_time(ev1)
-        h2d = (runner.h2d_bytes - h2d0) / args.steps
-        d2h = (runner.d2h_bytes - d2h0) / args.steps
-        # ---------------- device-timed: K decode-graph replays, max over ranks
-        dev_ms = runner.call("bench_replay", b, args.warmup, args.steps)
-    clocks = clk.summary()
-    launches = runner.graph_kernel_count(b)
+    clk_on = clk.__enter__()
+    ev0.record()
+    wall0 = time.perf_counter()
+    decoded = 0
+    for _ in range(args.steps):
+        _, stats = llm.step()
+        decoded += stats.decode_tokens
+    ev1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - wall0
+    e2e_ms = ev0.elapsed_time(ev1)
+    h2d = (runner.h2d_bytes - h2d0) / args.steps
+    d2h = (runner.d2h_bytes - d2h0) / args.steps
+    while not llm.is_finished():  # finish the requests: TTFT / TPOT of complete requests
+        llm.step()
+    # device-timed: K decode-graph replays of this batch bucket, max over ranks
+    dev_ms = runner.call("bench_replay", b, args.warmup, args.steps)
+    clk_on.__exit__(None, None, None)
+    req = llm.get_request_metrics()[-b:]
+    return {
+        "batch": b,
+        "value": round(b * args.steps / (dev_ms / 1e3), 1),
+        "ms_per_step": round(dev_ms / args.steps, 4),
+        "e2e_value": round(decoded / (e2e_ms / 1e3), 1),
+        "e2e_wall_s": round(wall, 4),
+        "h2d_bytes_per_step": int(h2d),
+        "d2h_bytes_per_step": int(d2h),
+        "ttft_p50_ms": _p50(m.get("ttft_ms") for m in req),
+        "tpot_p50_ms": _p50(m.get("tpot_ms") for m in req),
+        "prefill_s": round(prefill_s, 3),
+        "output_len": out_len,
+    }
+
+
+def run_isb(args, rank: int, world: int) -> dict | None:
+    import torch
+
+    from inference_systems_b200.engine.llm_engine import LLMEngine, serve_worker
+    from inference_systems_b200.models.presets import preset
+
+    cfg = preset(args.model)
+    batches = sorted({args.batch, *([int(x) for x in args.sweep.split(",")] if args.sweep else [])})
+    bmax = max(batches)
+    out_len = max(args.output_len, args.warmup + args.steps + 2)
+    kw = dict(load_format="dummy", device="cuda", tensor_parallel_size=world, max_num_seqs=bmax,
+              max_num_state_slots=bmax, max_model_len=args.prompt_len + out_len + 32,
+              max_num_batched_tokens=16384, max_cudagraph_batch_size=bmax, enforce_eager=False,
+              dist_port=int(os.environ.get("MASTER_PORT", "29500")) + 17, gpu_memory_utilization=0.85)
+    if world > 1 and rank > 0:
+        serve_worker(cfg, **kw)
+        return None
+    llm = LLMEngine(cfg, **kw)
+    runner = llm.model_runner
+    clk = ClockSampler(torch.cuda.current_device())
+    results = {b: _serve_batch(llm, runner, cfg, b, args, clk) for b in batches}
+    head = results[args.batch]
+    launches = runner.graph_kernel_count(args.batch)
     if args.breakdown:
-        g = runner.graphs[runner._graph_bucket(b)]
-        kernel_breakdown(g.replay, os.path.join(ROOT, "gpurun_out", f"breakdown_tp{world}_b{b}.txt"))
-    req = [s.lifecycle_metrics() for s in llm.scheduler.running]
-    ttfts = sorted(m["ttft_ms"] for m in req if m["ttft_ms"] is not None)
-    tpots = sorted(m["tpot_ms"] for m in req if m["tpot_ms"] is not None)
-    value = b * args.steps / (dev_ms / 1e3)
+        g = runner.graphs[runner._graph_bucket(args.batch)]
+        kernel_breakdown(g.replay, os.path.join(ROOT, "gpurun_out", f"breakdown_tp{world}_b{args.batch}.txt"))
     out = {
         "metric": METRIC,
-        "value": round(value, 1),
+        "value": head["value"],
         "unit": "tokens/s",
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": round(dev_ms / args.steps, 4),
+        "ms_per_step": head["ms_per_step"],
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (uniform-random token ids; random-init N(0,0.02) weights of the 0.8B architecture)",
         "config": {"model": "Qwen3.5-0.8B-shape hybrid (24 layers, 18 GDN + 6 gated attention, hidden 1024, vocab 248320)",
-                   "global_batch": b, "seq_len": args.prompt_len, "parallelism": f"tp{world}",
+                   "global_batch": args.batch, "seq_len": args.prompt_len, "output_len": head["output_len"],
+                   "parallelism": f"tp{world}",
                    "l2": "inputs larger than L2 (weights 1.5 GB + GDN state per step exceed the 126 MB L2)",
                    "cuda_graph_decode": True},
-        "clocks": clocks,
-        "e2e": {"value": round(decoded / (e2e_ms / 1e3), 1), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
-                "d2h_bytes_per_step": int(d2h), "wall_s": round(wall_e2e, 4),
+        "clocks": clk.summary(),
+        "e2e": {"value": head["e2e_value"], "unit": "tokens/s", "h2d_bytes_per_step": head["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": head["d2h_bytes_per_step"], "wall_s": head["e2e_wall_s"],
                 "api": "LLMEngine.step() (scheduler + packed pinned H2D + CUDA-graph step + token D2H)"},
         "gpu_launches": launches * args.steps,
         "gpu_launches_per_step": launches,
-        "ttft_p50_ms": round(ttfts[len(ttfts) // 2], 2) if ttfts else None,
-        "tpot_p50_ms": round(tpots[len(tpots) // 2], 3) if tpots else None,
-        "prefill_s": round(prefill_s, 3),
+        "ttft_p50_ms": head["ttft_p50_ms"],
+        "tpot_p50_ms": head["tpot_p50_ms"],
+        "prefill_s": head["prefill_s"],
         "impl": "isb",
     }
+    if len(batches) > 1:
+        out["sweep"] = [results[b] for b in batches]
     llm.exit()
     return out
 

@@ -1,6 +1,6 @@
 """Per-kernel microbenchmarks of the sm_100a ops at Qwen3.5-0.8B decode shapes.
 
-    python bench_kernels.py [--batch 128] [--only gemm] [--json out.json]
+    python bench_kernels.py [--batch 128] [--only gemm] [--json out.json] [--once]
 
 Method: every case builds R independent argument sets whose large operands
 (weights, GDN state pool, KV cache) together exceed 2 x the 126 MB L2, captures
@@ -149,12 +149,20 @@ def main():
     ap.add_argument("--batch", type=int, default=128)
     ap.add_argument("--only", default=None)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--once", action="store_true",
+                    help="run each selected op twice (warm-up + one launch) with no graph: a small case for ncu -c 1")
     args = ap.parse_args()
     load_extension()
     hbm, tflops, src = peaks()
     rows = []
     for name, (fns, nbytes, flops) in cases(args.batch).items():
         if args.only and args.only not in name:
+            continue
+        if args.once:
+            fns[0]()
+            fns[-1]()
+            torch.cuda.synchronize()
+            print(json.dumps({"op": name, "batch": args.batch, "launched": 2}), flush=True)
             continue
         us = graph_time_us(fns)
         gbs = nbytes / (us * 1e-6) / 1e9

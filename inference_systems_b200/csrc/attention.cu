@@ -18,6 +18,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace isb {
 
@@ -58,6 +59,8 @@ __global__ void attn_prepare_kernel(TIn* __restrict__ qkv, int qkv_stride, __nv_
                                     __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                     __nv_bfloat16* __restrict__ q_out, int T, int Hq, int Hkv, float eps, bool gated,
                                     bool zc) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = HD / 32;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -161,6 +164,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
                                                           const int* __restrict__ block_tables, int max_blocks,
                                                           int Hkv, float scale, float* __restrict__ part_o,
                                                           float* __restrict__ part_ml, int max_chunks) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int ED = HD / 16;   // channels per lane in phase 1
   constexpr int DW = HD / 8;    // output channels per warp in phase 3
   extern __shared__ __align__(128) uint8_t dsm_raw[];
@@ -284,6 +289,8 @@ template <int HD>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_chunks,
                                     int chunk, const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ gate,
                                     bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
+  pdl_wait();
+  pdl_trigger();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = ctx_lens[b];
   const int chunks = (ctx + chunk - 1) / chunk;
@@ -311,6 +318,8 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
     const int* __restrict__ cu_q, const int* __restrict__ ctx_lens, const int* __restrict__ block_tables,
     int max_blocks, int Hkv, float scale, const __nv_bfloat16* __restrict__ gate, bool gated,
     __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int R = QT * G;        // query rows (query-major, head-minor)
   constexpr int KT = 32;           // keys per tile
   extern __shared__ float sm[];
@@ -447,7 +456,7 @@ std::tuple<at::Tensor, at::Tensor> attn_prepare(const at::Tensor& qkv, const at:
   const int blocks = (warps * 32 + threads - 1) / threads;
   auto st = at::cuda::getCurrentCUDAStream();
 #define ISB_PREP(HD_, T_)                                                                                         \
-  attn_prepare_kernel<HD_, T_><<<blocks, threads, 0, st>>>(                                                       \
+  launch_pdl(attn_prepare_kernel<HD_, T_>, dim3(blocks), dim3(threads), 0, st,                                                        \
       reinterpret_cast<T_*>(qkv.data_ptr()), qkv.size(1), reinterpret_cast<__nv_bfloat16*>(gate.data_ptr()),      \
       positions.data_ptr<int>(), slot_mapping.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(qn.data_ptr()), \
       reinterpret_cast<const __nv_bfloat16*>(kn.data_ptr()), cos_sin.data_ptr<float>(), rd,                       \
@@ -488,7 +497,7 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const a
       TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess);
       attr = true;
     }
-    kern<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+    launch_pdl(kern, dim3(grid), dim3(256), smem, st, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
                                   reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()),
                                   reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), ctx_lens.data_ptr<int>(),
                                   block_tables.data_ptr<int>(), max_blocks, Hkv, float(scale),
@@ -501,7 +510,7 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const a
 #undef ISB_DEC_G
   TORCH_CHECK(launched, "attention_decode: unsupported (head_dim, group) = (", hd, ", ", G, ")");
 #define ISB_COMB(HD_)                                                                                              \
-  attn_combine_kernel<HD_><<<dim3(Hq, B), HD_, 0, st>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),       \
+  launch_pdl(attn_combine_kernel<HD_>, dim3(dim3(Hq, B)), dim3(HD_), 0, st, part_o.data_ptr<float>(), part_ml.data_ptr<float>(),       \
                                                        max_chunks, DCHUNK, ctx_lens.data_ptr<int>(),                  \
                                                        reinterpret_cast<const __nv_bfloat16*>(gate.data_ptr()),      \
                                                        gated,                                                        \
@@ -537,7 +546,7 @@ at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const 
     auto kern = attn_prefill_kernel<HD_, G_, QT_>;                                                                 \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);                                \
     const dim3 grid((max_seqlen_q + QT_ - 1) / QT_, Hkv, B);                                                       \
-    kern<<<grid, 256, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),                           \
+    launch_pdl(kern, dim3(grid), dim3(256), smem, st, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),                           \
                                   reinterpret_cast<const __nv_bfloat16*>(kc.data_ptr()),                          \
                                   reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr()), cu_q.data_ptr<int>(),    \
                                   ctx_lens.data_ptr<int>(), block_tables.data_ptr<int>(), block_tables.size(1),    \

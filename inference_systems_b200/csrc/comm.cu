@@ -21,6 +21,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace isb {
 
@@ -80,6 +81,8 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
 __global__ void acc_norm_tp_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
                                    int H, float eps, bool zc, unsigned int* flags, int world, unsigned int* done) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int ok;
   if (threadIdx.x == 0) ok = wait_flags(flags, world);
   __syncthreads();
@@ -136,6 +139,8 @@ __global__ void xrank_argmax_kernel(const float* __restrict__ val, const int* __
                                     const unsigned long long* xbufs, const unsigned long long* peer_flags,
                                     unsigned int* my_xbuf_flags, const float2* my_xbuf, int rank, int world,
                                     int max_rows, int* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ int ok;
   for (int t = threadIdx.x; t < B; t += blockDim.x) {
     const float2 e = make_float2(val[t], __int_as_float(idx[t]));
@@ -206,7 +211,7 @@ at::Tensor add_rmsnorm_acc_tp(at::Tensor acc, at::Tensor residual, const at::Ten
   const int H = residual.size(-1), rows = residual.numel() / H;
   at::Tensor out = at::empty_like(residual);
   const int blocks = std::max(1, (rows + 3) / 4);
-  acc_norm_tp_kernel<<<blocks, 128, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(acc_norm_tp_kernel, dim3(blocks), dim3(128), 0, at::cuda::getCurrentCUDAStream(), 
       acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows,
       H, float(eps), zc, reinterpret_cast<unsigned int*>(flags.data_ptr<int>()), int(flags.numel()),
@@ -220,7 +225,7 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
   const int B = val.numel();
   TORCH_CHECK(B <= max_rows, "xrank_argmax: more rows than the exchange buffer holds");
   at::Tensor out = at::empty({B}, idx.options());
-  xrank_argmax_kernel<<<1, 512, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(xrank_argmax_kernel, dim3(1), dim3(512), 0, at::cuda::getCurrentCUDAStream(), 
       val.data_ptr<float>(), idx.data_ptr<int>(), B, reinterpret_cast<const unsigned long long*>(xbufs.data_ptr<int64_t>()),
       reinterpret_cast<const unsigned long long*>(peer_flags.data_ptr<int64_t>()),
       reinterpret_cast<unsigned int*>(my_flags.data_ptr<int>()), reinterpret_cast<const float2*>(my_xbuf.data_ptr()),

@@ -33,6 +33,11 @@ ISB_DEVICE void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
 }
 
+// Programmatic dependent launch: pdl_wait() blocks until the previous kernel in
+// the stream has completed and its writes are visible (a no-op when the kernel
+// was launched without PDL); pdl_trigger() lets the next kernel start launching.
+ISB_DEVICE void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+ISB_DEVICE void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 ISB_DEVICE void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 
 ISB_DEVICE void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {

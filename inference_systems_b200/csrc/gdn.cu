@@ -27,6 +27,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace isb {
 
@@ -123,6 +124,14 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     float4 st[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
+    if (j == 0) {
+      // Everything read so far (this layer's state/conv pools, weights, step
+      // metadata) is never written by the kernel launched right before the scan
+      // (its input projection), so those loads overlap it; the projection rows
+      // are read only after it has completed.
+      pdl_wait();
+      pdl_trigger();
+    }
 
     for (int t = t0; t < t1; ++t) {
       const TIn* x = static_cast<const TIn*>(a.proj) + size_t(t) * a.proj_stride;
@@ -320,8 +329,8 @@ ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Te
 
 void launch_scan(const ScanArgs& a, const at::Tensor& proj, int64_t hk, int B) {
   auto st = at::cuda::getCurrentCUDAStream();
-  if (proj.scalar_type() == at::kFloat) gdn_scan_kernel<float><<<dim3(hk, B), kThreads, 0, st>>>(a);
-  else gdn_scan_kernel<__nv_bfloat16><<<dim3(hk, B), kThreads, 0, st>>>(a);
+  if (proj.scalar_type() == at::kFloat) launch_pdl(gdn_scan_kernel<float>, dim3(hk, B), dim3(kThreads), 0, st, a);
+  else launch_pdl(gdn_scan_kernel<__nv_bfloat16>, dim3(hk, B), dim3(kThreads), 0, st, a);
 }
 
 }  // namespace

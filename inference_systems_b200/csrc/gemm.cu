@@ -24,6 +24,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace isb {
 
@@ -169,16 +170,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
+      // Weights (P under swap-AB, Q otherwise) are never written by a kernel: the
+      // first STAGES weight tiles are requested before waiting for the previous
+      // kernel (programmatic dependent launch), the activation tiles after it.
+      auto load_w = [&](uint8_t* sp, uint64_t* bar, int kx) {
+        if constexpr (SWAP) tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
+        else tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
+      };
+      auto load_x = [&](uint8_t* sp, uint64_t* bar, int kx) {
+        if constexpr (SWAP) tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
+        else tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
+      };
+      const int pre = min(nkb, Cfg::STAGES);
+      for (int i = 0; i < pre; ++i) {  // fresh stages: nothing to wait for
+        mbar_arrive_expect_tx(&full[i], Cfg::STAGE_BYTES);
+        load_w(smem + i * Cfg::STAGE_BYTES, &full[i], (kb_begin + i) * BK);
+      }
+      pdl_wait();
+      pdl_trigger();
       for (int i = 0; i < nkb; ++i) {
         if (dbg && i == 0) dbg[2] = globaltimer_ns();
         const int s = i % Cfg::STAGES;
         const uint32_t ph = (i / Cfg::STAGES) & 1;
-        if (!mbar_wait(&empty[s], ph ^ 1)) { atomicOr(&g_gemm_err, 1u); break; }
         uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
-        mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
         const int kx = (kb_begin + i) * BK;
-        tma_load_2d(sp, &tmP, &full[s], kx, tile_p * BM);
-        tma_load_2d(sp + Cfg::P_BYTES, &tmQ, &full[s], kx, tile_q * BN);
+        if (i >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1)) { atomicOr(&g_gemm_err, 1u); break; }
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          load_w(sp, &full[s], kx);
+        }
+        load_x(sp, &full[s], kx);
       }
     }
   } else if (warp == 1) {
@@ -220,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int s_last;
 
   if (epi) {
+    pdl_wait();  // outputs / accumulators / split-K scratch may still be in use by the previous kernel
     bool acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
     if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 4u);
     tc_fence_after();
@@ -481,6 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Second stage of the fused LM-head selection: best (score, index) over vocab tiles.
 __global__ void argmax_tiles_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int ntiles, int tokens,
                                     int vocab_offset, float* __restrict__ out_val, int* __restrict__ out_idx) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -556,7 +580,7 @@ static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, const CUte
     TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess);
     attr = true;
   }
-  kern<<<dim3(tiles_p, tiles_q, splits), kThreads, Cfg::SMEM, stream>>>(tp, tq, to, a);
+  launch_pdl(kern, dim3(tiles_p, tiles_q, splits), dim3(kThreads), Cfg::SMEM, stream, tp, tq, to, a);
   const cudaError_t e = cudaGetLastError();
   TORCH_CHECK(e == cudaSuccess, "gemm launch failed: ", cudaGetErrorString(e));
 }
@@ -849,7 +873,7 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const 
     args.P_rows = B; args.Q_rows = V;
     launch_gemm<256, false, kArgmax>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
   }
-  argmax_tiles_kernel<<<B, 256, 0, st>>>(pv.data_ptr<float>(), pi.data_ptr<int>(), vtiles, B, int(vocab_offset),
+  launch_pdl(argmax_tiles_kernel, dim3(B), dim3(256), 0, st, pv.data_ptr<float>(), pi.data_ptr<int>(), vtiles, B, int(vocab_offset),
                                          val.data_ptr<float>(), idx.data_ptr<int>());
   return {val, idx};
 }

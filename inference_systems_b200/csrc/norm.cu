@@ -11,6 +11,7 @@
 #include <torch/extension.h>
 
 #include "common.cuh"
+#include "launch.cuh"
 
 namespace isb {
 
@@ -60,6 +61,8 @@ __device__ __forceinline__ void norm_store8(__nv_bfloat16* o, const float* s, co
 __global__ void acc_norm_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows, int H,
                                 float eps, bool zc) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -94,6 +97,8 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
                             const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                             const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows, int H,
                             float eps, bool zc) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -128,6 +133,8 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
 
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int rows, int H, int vocab_start, int vocab_rows) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -156,8 +163,7 @@ at::Tensor rmsnorm(const at::Tensor& x_in, const at::Tensor& w, double eps, bool
   at::Tensor out = at::empty_like(x);
   const int H = x.size(-1), rows = x.numel() / H;
   if (rows == 0) return out;
-  norm_kernel<0><<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 32 * kRowsPerBlock, 0,
-                   at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(norm_kernel<0>, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(32 * kRowsPerBlock), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), nullptr, nullptr, nullptr,
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H,
       float(eps), zc);
@@ -172,8 +178,7 @@ at::Tensor add_rmsnorm(const at::Tensor& x_in, at::Tensor residual, const at::Te
   at::Tensor out = at::empty_like(x);
   const int H = x.size(-1), rows = x.numel() / H;
   if (rows == 0) return out;
-  norm_kernel<1><<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 32 * kRowsPerBlock, 0,
-                   at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(norm_kernel<1>, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(32 * kRowsPerBlock), 0, at::cuda::getCurrentCUDAStream(), 
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
       nullptr, nullptr, reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H, float(eps), zc);
@@ -182,6 +187,8 @@ at::Tensor add_rmsnorm(const at::Tensor& x_in, at::Tensor residual, const at::Te
 
 // out[t, g*64 + j] = SiLU(acc[t, g*128 + j]) * acc[t, g*128 + 64 + j]  (packed gate/up groups of 64), acc <- 0
 __global__ void silu_mul_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int rows, int inter) {
+  pdl_wait();
+  pdl_trigger();
   const int groups4 = inter / 4;  // output vectors of 4 per row
   const size_t n = size_t(rows) * groups4;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
@@ -209,7 +216,7 @@ at::Tensor silu_mul_acc(at::Tensor acc, int64_t rows) {
   if (rows == 0) return out;
   const size_t n = size_t(rows) * inter / 4;
   const int blocks = int(std::min<size_t>((n + 255) / 256, 148 * 8));
-  silu_mul_acc_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(silu_mul_acc_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(), 
       acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), int(rows), inter);
   return out;
 }
@@ -221,8 +228,7 @@ at::Tensor add_rmsnorm_acc(at::Tensor acc, at::Tensor residual, const at::Tensor
   TORCH_CHECK(acc.size(-1) == H && acc.numel() >= size_t(rows) * H, "accumulator shape mismatch");
   at::Tensor out = at::empty_like(residual);
   if (rows == 0) return out;
-  acc_norm_kernel<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 32 * kRowsPerBlock, 0,
-                    at::cuda::getCurrentCUDAStream()>>>(acc.data_ptr<float>(),
+  launch_pdl(acc_norm_kernel, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(32 * kRowsPerBlock), 0, at::cuda::getCurrentCUDAStream(), acc.data_ptr<float>(),
                                                         reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
                                                         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
                                                         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H,
@@ -238,8 +244,7 @@ std::tuple<at::Tensor, at::Tensor> embed_rmsnorm(const at::Tensor& ids, const at
   at::Tensor residual = at::empty({rows, H}, table.options());
   at::Tensor out = at::empty({rows, H}, table.options());
   if (rows == 0) return {residual, out};
-  norm_kernel<2><<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 32 * kRowsPerBlock, 0,
-                   at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(norm_kernel<2>, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(32 * kRowsPerBlock), 0, at::cuda::getCurrentCUDAStream(), 
       nullptr, reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), ids.data_ptr<int>(),
       reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
       reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H, float(eps), zc);
@@ -253,8 +258,7 @@ at::Tensor embed(const at::Tensor& ids, const at::Tensor& table, int64_t vocab_s
   const int rows = ids.numel(), H = table.size(1);
   at::Tensor out = at::empty({rows, H}, table.options());
   if (rows == 0) return out;
-  embed_kernel<<<(rows + kRowsPerBlock - 1) / kRowsPerBlock, 32 * kRowsPerBlock, 0,
-                 at::cuda::getCurrentCUDAStream()>>>(ids.data_ptr<int>(),
+  launch_pdl(embed_kernel, dim3((rows + kRowsPerBlock - 1) / kRowsPerBlock), dim3(32 * kRowsPerBlock), 0, at::cuda::getCurrentCUDAStream(), ids.data_ptr<int>(),
                                                      reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
                                                      reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H,
                                                      int(vocab_start), int(table.size(0)));
