@@ -73,26 +73,29 @@ def replicas(big_bytes: int) -> int:
     return max(2, math.ceil(2 * L2_BYTES / max(big_bytes, 1)))
 
 
-def cases(b: int):
+def cases(b: int) -> dict:
+    """name -> builder; a builder allocates its operands and returns (fns, algorithmic bytes, flops)."""
     dev, bf = "cuda", torch.bfloat16
     out = {}
 
     def gemm_case(name, n, k, mode):
-        wbytes = n * k * 2
-        r = replicas(wbytes)
-        a = torch.randn(b, k, device=dev).to(bf)
-        ws = [(torch.randn(n, k, device=dev) * 0.02).to(bf) for _ in range(r)]
-        acc = torch.zeros(b, n, device=dev)
-        if mode == "silu":
-            fns = [lambda w=w: ops.linear_silu_mul(a, w) for w in ws]
-            ob = b * n // 2 * 2
-        elif mode == "acc":
-            fns = [lambda w=w: ops.linear_accumulate(a, w, acc) for w in ws]
-            ob = b * n * 4 * 2
-        else:
-            fns = [lambda w=w: ops.linear(a, w) for w in ws]
-            ob = b * n * 2
-        out[name] = (fns, wbytes + b * k * 2 + ob, 2 * b * n * k)
+        def build():
+            wbytes = n * k * 2
+            r = replicas(wbytes)
+            a = torch.randn(b, k, device=dev).to(bf)
+            ws = [(torch.randn(n, k, device=dev) * 0.02).to(bf) for _ in range(r)]
+            acc = torch.zeros(b, n, device=dev)
+            if mode == "silu":
+                fns = [lambda w=w: ops.linear_silu_mul(a, w) for w in ws]
+                ob = b * n // 2 * 2
+            elif mode == "acc":
+                fns = [lambda w=w: ops.linear_accumulate(a, w, acc) for w in ws]
+                ob = b * n * 4 * 2
+            else:
+                fns = [lambda w=w: ops.linear(a, w) for w in ws]
+                ob = b * n * 2
+            return fns, wbytes + b * k * 2 + ob, 2 * b * n * k
+        out[name] = build
 
     gemm_case("gemm_gdn_in_proj", 8224 + 32, 1024, "store")
     gemm_case("gemm_attn_qkv", 5120, 1024, "store")
@@ -100,47 +103,59 @@ def cases(b: int):
     gemm_case("gemm_out_proj_accum", 1024, 2048, "acc")
     gemm_case("gemm_down_accum", 1024, 3584, "acc")
     gemm_case("gemm_out_proj_store", 1024, 2048, "store")
-    v = 248320
-    w = (torch.randn(v, 1024, device=dev) * 0.02).to(bf)  # 508 MB: already > 2 x L2
-    x = torch.randn(b, 1024, device=dev).to(bf)
-    temps = torch.zeros(b, device=dev)
-    rng = torch.zeros(2, dtype=torch.int32, device=dev)
-    out["lm_head_sample_greedy"] = ([lambda: ops.lm_head_sample(x, w, temps, rng, 0)], (w.numel() + x.numel()) * 2,
-                                    2 * b * w.numel())
-    # GDN decode (16 key == 16 value heads, Dk = Dv = 128)
-    hk = hv = 16
-    d = 128
-    c = 2 * hk * d + hv * d
-    p = c + hv * d + 2 * hv
-    state_bytes = b * hv * d * d * 4
-    r = replicas(state_bytes)
-    proj = torch.randn(b, p, device=dev).to(bf)
-    conv_w = (torch.randn(c, 4, device=dev) * 0.5).to(bf)
-    a_log, dt = torch.zeros(hv, device=dev), torch.ones(hv, device=dev)
-    nw = torch.ones(d, device=dev).to(bf)
-    slots = torch.arange(b, device=dev, dtype=torch.int32)
-    pools = [(torch.randn(b + 1, hv, d, d, device=dev) * 0.01, torch.zeros(b + 1, c, 3, device=dev).to(bf))
-             for _ in range(r)]
-    out["gdn_decode"] = ([lambda rc=rc, cv=cv: torch.ops.isb.gdn_decode(proj, slots, conv_w, a_log, dt, nw, rc, cv, hk,
-                                                                         hv, d, d, 1e-6) for rc, cv in pools],
-                         2 * state_bytes + proj.numel() * 2 + b * hv * d * 2, 0)
-    # attention decode: 8 q heads / 2 kv heads, hd 256, context 640
-    ctx = 640
-    kv_bytes = b * 2 * ctx * 256 * 2 * 2
-    r = replicas(kv_bytes)
-    q = torch.randn(b, 8, 256, device=dev).to(bf)
-    qkv = torch.randn(b, 5120, device=dev).to(bf)
-    bt = torch.arange(b * 3, device=dev, dtype=torch.int32).view(b, 3)
-    bt = torch.cat((bt, torch.full((b, 2), -1, device=dev, dtype=torch.int32)), 1)
-    cl = torch.full((b,), ctx, device=dev, dtype=torch.int32)
-    caches = [(torch.randn(b * 3, 2, 256, 256, device=dev).to(bf), torch.randn(b * 3, 2, 256, 256, device=dev).to(bf))
-              for _ in range(r)]
-    out["attention_decode"] = ([lambda kc=kc, vc=vc: torch.ops.isb.attention_decode(q, qkv, kc, vc, cl, bt, 0.0625, True)
-                                for kc, vc in caches], kv_bytes + q.numel() * 2 * 2, 4 * b * 8 * ctx * 256)
-    resid = torch.randn(b, 1024, device=dev).to(bf)
-    nwh = torch.zeros(1024, device=dev).to(bf)
-    acc = torch.zeros(b, 1024, device=dev)
-    out["add_rmsnorm_acc"] = ([lambda: ops.add_rmsnorm_acc(acc, resid, nwh, 1e-6, True)], b * 1024 * (8 + 4 + 2), 0)
+
+    def lm_head():
+        v = 248320
+        w = (torch.randn(v, 1024, device=dev) * 0.02).to(bf)  # 508 MB: already > 2 x L2
+        x = torch.randn(b, 1024, device=dev).to(bf)
+        temps = torch.zeros(b, device=dev)
+        rng = torch.zeros(2, dtype=torch.int32, device=dev)
+        return [lambda: ops.lm_head_sample(x, w, temps, rng, 0)], (w.numel() + x.numel()) * 2, 2 * b * w.numel()
+    out["lm_head_sample_greedy"] = lm_head
+
+    def gdn():
+        # GDN decode (16 key == 16 value heads, Dk = Dv = 128)
+        hk = hv = 16
+        d = 128
+        c = 2 * hk * d + hv * d
+        p = c + hv * d + 2 * hv
+        state_bytes = b * hv * d * d * 4
+        r = replicas(state_bytes)
+        proj = torch.randn(b, p, device=dev).to(bf)
+        conv_w = (torch.randn(c, 4, device=dev) * 0.5).to(bf)
+        a_log, dt = torch.zeros(hv, device=dev), torch.ones(hv, device=dev)
+        nw = torch.ones(d, device=dev).to(bf)
+        slots = torch.arange(b, device=dev, dtype=torch.int32)
+        pools = [(torch.randn(b + 1, hv, d, d, device=dev) * 0.01, torch.zeros(b + 1, c, 3, device=dev).to(bf))
+                 for _ in range(r)]
+        fns = [lambda rc=rc, cv=cv: torch.ops.isb.gdn_decode(proj, slots, conv_w, a_log, dt, nw, rc, cv, hk, hv, d,
+                                                             d, 1e-6) for rc, cv in pools]
+        return fns, 2 * state_bytes + proj.numel() * 2 + b * hv * d * 2, 0
+    out["gdn_decode"] = gdn
+
+    def attention():
+        # attention decode: 8 q heads / 2 kv heads, hd 256, context 640
+        ctx = 640
+        kv_bytes = b * 2 * ctx * 256 * 2 * 2
+        r = replicas(kv_bytes)
+        q = torch.randn(b, 8, 256, device=dev).to(bf)
+        gate = torch.randn(b, 8 * 256, device=dev).to(bf)
+        bt = torch.arange(b * 3, device=dev, dtype=torch.int32).view(b, 3)
+        bt = torch.cat((bt, torch.full((b, 2), -1, device=dev, dtype=torch.int32)), 1)
+        cl = torch.full((b,), ctx, device=dev, dtype=torch.int32)
+        caches = [(torch.randn(b * 3, 2, 256, 256, device=dev).to(bf), torch.randn(b * 3, 2, 256, 256, device=dev).to(bf))
+                  for _ in range(r)]
+        fns = [lambda kc=kc, vc=vc: torch.ops.isb.attention_decode(q, gate, kc, vc, cl, bt, 0.0625, True)
+               for kc, vc in caches]
+        return fns, kv_bytes + q.numel() * 2 * 2, 4 * b * 8 * ctx * 256
+    out["attention_decode"] = attention
+
+    def acc_norm():
+        resid = torch.randn(b, 1024, device=dev).to(bf)
+        nwh = torch.zeros(1024, device=dev).to(bf)
+        acc = torch.zeros(b, 1024, device=dev)
+        return [lambda: ops.add_rmsnorm_acc(acc, resid, nwh, 1e-6, True)], b * 1024 * (8 + 4 + 2), 0
+    out["add_rmsnorm_acc"] = acc_norm
     return out
 
 
@@ -155,9 +170,10 @@ def main():
     load_extension()
     hbm, tflops, src = peaks()
     rows = []
-    for name, (fns, nbytes, flops) in cases(args.batch).items():
+    for name, build in cases(args.batch).items():
         if args.only and args.only not in name:
             continue
+        fns, nbytes, flops = build()
         if args.once:
             fns[0]()
             fns[-1]()

@@ -59,8 +59,8 @@ __global__ void attn_prepare_kernel(TIn* __restrict__ qkv, int qkv_stride, __nv_
                                     __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ vc,
                                     __nv_bfloat16* __restrict__ q_out, int T, int Hq, int Hkv, float eps, bool gated,
                                     bool zc) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   constexpr int E = HD / 32;
   const int warp_global = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -164,8 +164,8 @@ __global__ void __launch_bounds__(256) attn_decode_kernel(const __nv_bfloat16* _
                                                           const int* __restrict__ block_tables, int max_blocks,
                                                           int Hkv, float scale, float* __restrict__ part_o,
                                                           float* __restrict__ part_ml, int max_chunks) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   constexpr int ED = HD / 16;   // channels per lane in phase 1
   constexpr int DW = HD / 8;    // output channels per warp in phase 3
   extern __shared__ __align__(128) uint8_t dsm_raw[];
@@ -289,8 +289,8 @@ template <int HD>
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int max_chunks,
                                     int chunk, const int* __restrict__ ctx_lens, const __nv_bfloat16* __restrict__ gate,
                                     bool gated, __nv_bfloat16* __restrict__ out, int Hq) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = ctx_lens[b];
   const int chunks = (ctx + chunk - 1) / chunk;
@@ -318,8 +318,8 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
     const int* __restrict__ cu_q, const int* __restrict__ ctx_lens, const int* __restrict__ block_tables,
     int max_blocks, int Hkv, float scale, const __nv_bfloat16* __restrict__ gate, bool gated,
     __nv_bfloat16* __restrict__ out) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   constexpr int R = QT * G;        // query rows (query-major, head-minor)
   constexpr int KT = 32;           // keys per tile
   extern __shared__ float sm[];

@@ -81,8 +81,8 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
 __global__ void acc_norm_tp_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
                                    const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
                                    int H, float eps, bool zc, unsigned int* flags, int world, unsigned int* done) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   __shared__ int ok;
   if (threadIdx.x == 0) ok = wait_flags(flags, world);
   __syncthreads();
@@ -139,8 +139,8 @@ __global__ void xrank_argmax_kernel(const float* __restrict__ val, const int* __
                                     const unsigned long long* xbufs, const unsigned long long* peer_flags,
                                     unsigned int* my_xbuf_flags, const float2* my_xbuf, int rank, int world,
                                     int max_rows, int* __restrict__ out) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   __shared__ int ok;
   for (int t = threadIdx.x; t < B; t += blockDim.x) {
     const float2 e = make_float2(val[t], __int_as_float(idx[t]));

@@ -86,6 +86,7 @@ __device__ __forceinline__ float take(const TIn* row, int idx, bool consume) {
 
 template <typename TIn>
 __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
+  pdl_trigger();
   __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
   __shared__ float red_k[8][D], red_q[8][D];
   __shared__ float scal[16];
@@ -126,11 +127,13 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
     if (j == 0) {
       // Everything read so far (this layer's state/conv pools, weights, step
-      // metadata) is never written by the kernel launched right before the scan
-      // (its input projection), so those loads overlap it; the projection rows
-      // are read only after it has completed.
+      // metadata) is written by no kernel of the same dependent-launch chain:
+      // the pools only by this layer's scan of an earlier step (an earlier
+      // graph launch or forward call) or by plainly launched commit / restore
+      // kernels, which start only after all earlier work has finished.  So these
+      // loads overlap the kernels still in flight; the projection rows are read
+      // only after the previous kernel has completed.
       pdl_wait();
-      pdl_trigger();
     }
 
     for (int t = t0; t < t1; ++t) {

@@ -140,6 +140,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* acc_full = empty + Cfg::STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 1);
 
+  pdl_trigger();  // the next kernel may start its own prologue now
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tile_p = blockIdx.x, tile_q = blockIdx.y;
   const int kb_total = (args.K + BK - 1) / BK;
@@ -187,7 +188,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_w(smem + i * Cfg::STAGE_BYTES, &full[i], (kb_begin + i) * BK);
       }
       pdl_wait();
-      pdl_trigger();
       for (int i = 0; i < nkb; ++i) {
         if (dbg && i == 0) dbg[2] = globaltimer_ns();
         const int s = i % Cfg::STAGES;
@@ -503,8 +503,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Second stage of the fused LM-head selection: best (score, index) over vocab tiles.
 __global__ void argmax_tiles_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int ntiles, int tokens,
                                     int vocab_offset, float* __restrict__ out_val, int* __restrict__ out_idx) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int t = blockIdx.x;
   float best = -INFINITY;
   int bi = 0x7fffffff;

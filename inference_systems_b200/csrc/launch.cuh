@@ -1,11 +1,17 @@
 // Host-side launch helper for programmatic dependent launch (PDL).
 //
 // A kernel launched with launch_pdl may begin (prologue, TMEM allocation,
-// prefetch of data no earlier kernel writes) while the previous kernel in the
-// stream is still running. Every such kernel calls pdl_wait() (common.cuh)
+// prefetch) while earlier kernels in the stream are still running. Every such
+// kernel calls pdl_trigger() (common.cuh) as it starts, so the next kernel can
+// be scheduled once all of this kernel's CTAs are resident, and pdl_wait()
 // before it reads anything an earlier kernel produced or writes anything an
-// earlier kernel reads, and pdl_trigger() only after that wait, so at most the
-// immediately preceding kernel is still running during its pre-wait prologue.
+// earlier kernel reads. pdl_wait() returns only after the previous kernel has
+// completed, and that kernel completed only after its own wait returned, so the
+// ordering is transitive. Because several kernels of a chain can be in flight
+// at once, code before pdl_wait() reads only data that no PDL-launched kernel
+// of the chain writes: weights, and a GDN layer's state pools (written by that
+// layer's scan in an earlier step, or by plainly launched kernels, which start
+// only after all earlier work has finished).
 // ISB_PDL=0 in the environment launches everything with plain stream order.
 #pragma once
 

@@ -61,8 +61,8 @@ __device__ __forceinline__ void norm_store8(__nv_bfloat16* o, const float* s, co
 __global__ void acc_norm_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows, int H,
                                 float eps, bool zc) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -97,8 +97,8 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
                             const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                             const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows, int H,
                             float eps, bool zc) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -133,8 +133,8 @@ __global__ void norm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* 
 
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table,
                              __nv_bfloat16* __restrict__ out, int rows, int H, int vocab_start, int vocab_rows) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -187,8 +187,8 @@ at::Tensor add_rmsnorm(const at::Tensor& x_in, at::Tensor residual, const at::Te
 
 // out[t, g*64 + j] = SiLU(acc[t, g*128 + j]) * acc[t, g*128 + 64 + j]  (packed gate/up groups of 64), acc <- 0
 __global__ void silu_mul_acc_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int rows, int inter) {
-  pdl_wait();
   pdl_trigger();
+  pdl_wait();
   const int groups4 = inter / 4;  // output vectors of 4 per row
   const size_t n = size_t(rows) * groups4;
   for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {

@@ -20,6 +20,7 @@ reference rejects that case, ``qwen3_5.py:33-34``).
 from __future__ import annotations
 
 import math
+import os
 from typing import Callable
 
 import torch
@@ -310,6 +311,7 @@ class HybridCausalLM(nn.Module):
         self.attn_layer_ids = [i for i, l in enumerate(self.layers) if not l.is_linear]
         self._cos_sin: torch.Tensor | None = None
         self.column_scratch = ColumnScratch()
+        self.column_scratch_tokens = 0
         self.comm = None  # set by the runner (parallel.comm.TPComm) when tp_size > 1
 
     # ------------------------------------------------------------ weights
@@ -363,10 +365,14 @@ class HybridCausalLM(nn.Module):
         re-zeroes the rows it read, so the buffer is zero between uses.
         """
         self.acc = torch.zeros(max_tokens, self.hidden_size, dtype=torch.float32, device=device)
-        if getattr(self, "use_column_scratch", False):
+        # Column-parallel projections of at most this many tokens split K across enough CTAs to
+        # cover every SM and add into an fp32 scratch consumed by the next kernel; above it the
+        # atomics cost more than the extra parallelism gains (measured), so they store bf16.
+        rows = min(max_tokens, int(os.environ.get("ISB_COLUMN_SCRATCH_TOKENS", str(self.column_scratch_tokens))))
+        if rows > 0:
             widths = [m.shape[0] for m in self.parameters() if m.dim() == 2 and m.shape[1] == self.hidden_size
                       and m.shape[0] != self.vocab_size and m.shape[0] != self.vocab_per_rank]
-            self.column_scratch.allocate(min(max_tokens, 256), max(widths), device)
+            self.column_scratch.allocate(rows, max(widths), device)
             for mod in self.modules():
                 if isinstance(mod, (AttentionMixer, GDNMixer, MLP)):
                     mod.scratch = self.column_scratch
