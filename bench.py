@@ -47,6 +47,9 @@ def parse():
     p.add_argument("--output-len", type=int, default=256)
     p.add_argument("--impl", default="isb", choices=["isb", "reference"])
     p.add_argument("--model", default=MODEL)
+    p.add_argument("--mtp", type=int, default=0,
+                   help="K > 0: MTP speculative decode with K drafts vs target-only (BASELINE config 3)")
+    p.add_argument("--mtp-accept", type=float, default=0.6, help="seeded draft/target agreement probability")
     p.add_argument("--breakdown", action="store_true",
                    help="after timing, profile 3 decode-graph replays with torch.profiler (kernel-time shares)")
     return p.parse_args()
@@ -263,6 +266,91 @@ def run_isb(args, rank: int, world: int) -> dict | None:
     return out
 
 
+# ------------------------------------------------------------ MTP (config 3)
+def _decode_run(llm, cfg, b: int, args) -> dict:
+    """B requests to completion; device-timed decode phase (after every first token)."""
+    import torch
+
+    from inference_systems_b200 import SamplingParams
+
+    g = torch.Generator().manual_seed(1000 + b)
+    prompts = torch.randint(0, cfg["vocab_size"], (b, args.prompt_len), generator=g).tolist()
+    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True)
+    llm.scheduler.reset_metrics()
+    for p in prompts:
+        llm.add_request(p, sp)
+    while llm.scheduler.waiting or any(s.num_completion_tokens == 0 for s in llm.scheduler.running):
+        llm.step()
+    first = sum(s.num_completion_tokens for s in llm.scheduler.running)
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    wall0 = time.perf_counter()
+    steps = 0
+    while not llm.is_finished():
+        llm.step()
+        steps += 1
+    ev1.record()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    req = llm.get_request_metrics()[-b:]
+    tokens = b * args.output_len - first
+    return {"batch": b, "decode_tokens_per_s": round(tokens / (ms / 1e3), 1), "decode_steps": steps,
+            "decode_ms": round(ms, 2), "wall_s": round(time.perf_counter() - wall0, 3),
+            "tpot_p50_ms": _p50(m.get("tpot_ms") for m in req), "ttft_p50_ms": _p50(m.get("ttft_ms") for m in req)}
+
+
+def run_mtp(args, rank: int, world: int) -> dict | None:
+    """MTP speculative decoding (K drafts, seeded agreement p) vs target-only decoding, same workload."""
+    import torch
+
+    from inference_systems_b200.engine.llm_engine import LLMEngine, serve_worker
+    from inference_systems_b200.models.presets import preset
+
+    cfg = preset(args.model)
+    batches = sorted({args.batch, *([int(x) for x in args.sweep.split(",")] if args.sweep else [])})
+    bmax = max(batches)
+    pages = (args.prompt_len + args.output_len + 2 * args.mtp + 255) // 256 + 1
+    res = {}
+    for mode in ("target", "mtp"):
+        kw = dict(load_format="dummy", device="cuda", tensor_parallel_size=world, max_num_seqs=bmax,
+                  max_num_state_slots=bmax, max_model_len=args.prompt_len + args.output_len + 32,
+                  max_num_batched_tokens=16384, max_cudagraph_batch_size=bmax, enforce_eager=False,
+                  num_kvcache_blocks=bmax * pages + 8,
+                  dist_port=int(os.environ.get("MASTER_PORT", "29500")) + 19 + (mode == "mtp"))
+        if mode == "mtp":
+            kw.update(num_speculative_tokens=args.mtp, mtp_synthetic_acceptance=args.mtp_accept)
+        if world > 1 and rank > 0:
+            serve_worker(cfg, **kw)
+            continue
+        llm = LLMEngine(cfg, **kw)
+        _decode_run(llm, cfg, min(batches), args)  # warm-up generation
+        res[mode] = {b: _decode_run(llm, cfg, b, args) for b in batches}
+        if mode == "mtp":
+            res["mtp_metrics"] = llm.get_runtime_metrics()["model_runner"].get("mtp", {})
+        llm.exit()
+    if rank > 0:
+        return None
+    rows = []
+    for b in batches:
+        t, m = res["target"][b], res["mtp"][b]
+        rows.append({"batch": b, "target_tok_s": t["decode_tokens_per_s"], "mtp_tok_s": m["decode_tokens_per_s"],
+                     "speedup": round(m["decode_tokens_per_s"] / t["decode_tokens_per_s"], 3),
+                     "target_tpot_p50_ms": t["tpot_p50_ms"], "mtp_tpot_p50_ms": m["tpot_p50_ms"]})
+    head = next(r for r in rows if r["batch"] == args.batch)
+    mm = res["mtp_metrics"]
+    return {"metric": f"MTP speculative decode tok/s (K={args.mtp}, agreement p={args.mtp_accept}) vs target-only",
+            "value": head["mtp_tok_s"], "unit": "tokens/s", "n_gpus": world, "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic prompts; random-init 0.8B-shape target + 1-layer MTP head",
+            "config": {"model": "Qwen3.5-0.8B-shape + MTP", "global_batch": args.batch, "seq_len": args.prompt_len,
+                       "output_len": args.output_len, "parallelism": f"tp{world}", "num_speculative_tokens": args.mtp,
+                       "synthetic_acceptance": args.mtp_accept, "cuda_graph": True},
+            "vs_target_only": head["speedup"], "sweep": rows,
+            "acceptance_rate": round(mm.get("acceptance_rate", 0.0), 4),
+            "mean_emitted_per_round": round(mm.get("mean_emitted_per_round", 0.0), 3),
+            "impl": "isb"}
+
+
 # --------------------------------------------------------------- reference
 def run_reference(args, rank: int, world: int) -> dict | None:
     from bench_reference import run as ref_run
@@ -277,6 +365,8 @@ def main():
         world = args.gpus
     if args.impl == "reference":
         out = run_reference(args, rank, world)
+    elif args.mtp > 0:
+        out = run_mtp(args, rank, world)
     else:
         out = run_isb(args, rank, world)
     if out is not None and rank == 0:

@@ -142,11 +142,15 @@ class ModelRunner:
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.graph_bufs: dict[int, dict] = {}
         self.graph_kernels: dict[int, int] = {}
-        if self.device.type == "cuda" and not self.enforce_eager:
-            self.capture_cudagraph()
         if self.mtp is not None:
             from inference_systems_b200.engine.mtp import MTPDriver
             self.mtp_driver = MTPDriver(self)
+        if self.device.type == "cuda" and not self.enforce_eager:
+            if self.mtp is not None:
+                # decode batches run as speculative rounds: capture those instead of target-only steps
+                self.mtp_driver.capture(_bucket_sizes(self._max_graph_batch()))
+            else:
+                self.capture_cudagraph()
 
         # ---------------------------------------------------------- RPC
         self.channel = None
@@ -180,6 +184,9 @@ class ModelRunner:
             torch.cuda.synchronize(self.device)
         self.graphs.clear()
         self.graph_bufs.clear()
+        if self.mtp is not None:
+            self.mtp_driver.graphs.clear()
+            self.mtp_driver.graph_bufs.clear()
         if self.comm is not None:
             self.comm.close()
         if self.world_size > 1:
@@ -378,11 +385,14 @@ class ModelRunner:
                 return s
         return None
 
+    def _max_graph_batch(self) -> int:
+        cfg = self.config
+        return min(cfg.max_num_seqs, cfg.max_cudagraph_batch_size,
+                   self.state_manager.max_num_seqs if self.state_manager else cfg.max_num_seqs)
+
     @torch.inference_mode()
     def capture_cudagraph(self) -> None:
-        cfg = self.config
-        max_bs = min(cfg.max_num_seqs, cfg.max_cudagraph_batch_size,
-                     self.state_manager.max_num_seqs if self.state_manager else cfg.max_num_seqs)
+        max_bs = self._max_graph_batch()
         pool = None
         dummy_seqs = []
         for bs_ in reversed(_bucket_sizes(max_bs)):

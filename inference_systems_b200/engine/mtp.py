@@ -109,6 +109,9 @@ class MTPDriver:
         n_attn = len(runner.model.attn_layer_ids)
         self.kv_index = n_attn  # the MTP layer is the last layer of the KV cache
         self.before_round = None  # test hook: callable(seqs, driver) run before each verify pass
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_bufs: dict[int, tuple[torch.Tensor, torch.Tensor]] = {}
+        self.graph_replays = 0
         self.reset_metrics()
 
     # ------------------------------------------------------------ helpers
@@ -138,6 +141,8 @@ class MTPDriver:
             "accepted_length_histogram": list(self.accept_hist),
             "prefill_catchups": self.prefill_catchups,
             "synthetic_acceptance": self.synthetic,
+            "cudagraph_buckets": sorted(self.graphs),
+            "cudagraph_replays": self.graph_replays,
         }
 
     def set_drafts(self, state_slot: int, tokens) -> None:
@@ -215,30 +220,44 @@ class MTPDriver:
         self.r.profiler.record_cpu("mtp.prefill_catchup", (perf_counter_ns() - t0) / 1e6)
 
     # -------------------------------------------------------------- round
-    @torch.inference_mode()
-    def run(self, seqs: list[Sequence]):
-        """One speculative round for a decode batch; returns emitted token lists (rank 0)."""
-        t0 = perf_counter_ns()
+    def _pack(self, seqs: list[Sequence], pad_to: int) -> np.ndarray:
+        """``[pending | position | state slot | page capacity | rng(2) | block tables]`` int32.
+
+        Rows past ``len(seqs)`` are padding: scratch state slot, no pages, zero
+        capacity (so every kernel sees an empty context for them).
+        """
+        r = self.r
+        b, mb = len(seqs), r.max_blocks_per_seq
+        scratch = r.state_manager.scratch_slot_id if r.state_manager is not None else 0
+        pend = np.zeros(pad_to, np.int32)
+        pos0 = np.zeros(pad_to, np.int32)
+        st = np.full(pad_to, scratch, np.int32)
+        caps = np.zeros(pad_to, np.int32)
+        bt = np.full((pad_to, mb), -1, dtype=np.int32)
+        for i, s in enumerate(seqs):
+            pend[i] = s.last_token
+            pos0[i] = len(s) - 1
+            st[i] = s.state_slot if s.state_slot is not None else scratch
+            caps[i] = len(s.block_table) * r.block_size
+            bt[i, :len(s.block_table)] = s.block_table
+        rng = np.asarray([r.config.seed & 0x7FFFFFFF, r.sample_step & 0x7FFFFFFF], np.int32)
+        return np.concatenate([pend, pos0, st, caps, rng, bt.reshape(-1)])
+
+    def _round_device(self, meta: torch.Tensor, b: int, slots_host: list[int] | None,
+                      max_k: int) -> torch.Tensor:
+        """Device work of one round over ``b`` (possibly padded) rows; returns ``[v (b*(K+1)) | a (b)]`` int32.
+
+        Host values are used only by the CPU reference path (``slots_host``,
+        ``max_k``), so the body can be captured in a CUDA graph per batch bucket.
+        """
         r = self.r
         k, bs = self.k, r.block_size
-        b = len(seqs)
-        if self.before_round is not None:
-            self.before_round(seqs, self)
         mb = r.max_blocks_per_seq
-        bt = np.full((b, mb), -1, dtype=np.int32)
-        for i, s in enumerate(seqs):
-            bt[i, :len(s.block_table)] = s.block_table
-        pend = np.asarray([s.last_token for s in seqs], np.int32)
-        pos0 = np.asarray([len(s) - 1 for s in seqs], np.int32)
-        st = np.asarray([s.state_slot if s.state_slot is not None else 0 for s in seqs], np.int32)
-        caps = np.asarray([len(s.block_table) * bs for s in seqs], np.int32)
-        rng = np.asarray([r.config.seed & 0x7FFFFFFF, r.sample_step & 0x7FFFFFFF], np.int32)
-        flat = np.concatenate([pend, pos0, st, caps, rng, bt.reshape(-1)])
-        dev_meta = r._upload(flat)
-        pend_d, pos_d, st_d, caps_d = (dev_meta[i * b:(i + 1) * b] for i in range(4))
-        rng_d = dev_meta[4 * b:4 * b + 2]
-        bt_d = dev_meta[4 * b + 2:].view(b, mb)
-        dev = dev_meta.device
+        pend_d, pos_d, st_d, caps_d = (meta[i * b:(i + 1) * b] for i in range(4))
+        rng_d = meta[4 * b:4 * b + 2]
+        bt_d = meta[4 * b + 2:4 * b + 2 + b * mb].view(b, mb)
+        dev = meta.device
+        valid = caps_d > 0
 
         # ---- verify: one target pass over [pending, drafts]
         ar = torch.arange(k + 1, dtype=torch.int32, device=dev)
@@ -248,14 +267,12 @@ class MTPDriver:
         sm = slot_of(bt_d, pos2, bs).reshape(-1)
         t = b * (k + 1)
         cu = torch.arange(b + 1, dtype=torch.int32, device=dev) * (k + 1)
-        ctx = (pos_d + k + 1).to(torch.int32)
-        slots_host = st.tolist()
+        ctx = torch.where(valid, pos_d + k + 1, torch.zeros_like(pos_d)).to(torch.int32)
         vbatch = ForwardBatch(
             is_prefill=True, input_ids=ids, positions=pos2.reshape(-1).to(torch.int32), cu_seqlens_q=cu,
             context_lens=ctx, block_tables=bt_d, slot_mapping=sm, state_slots=st_d, logits_indices=cu[1:] - 1,
-            max_seqlen_q=k + 1, max_seqlen_k=int(pos0.max()) + k + 1,
-            cu_seqlens_host=[i * (k + 1) for i in range(b + 1)], slots_host=slots_host, num_seqs=b,
-            gdn_verify=self._gdn_records(t))
+            max_seqlen_q=k + 1, max_seqlen_k=max_k, cu_seqlens_host=[i * (k + 1) for i in range(b + 1)],
+            slots_host=slots_host or [], num_seqs=b, gdn_verify=self._gdn_records(t))
         hidden = r.model(vbatch, r.kv_layers(), r.state_layers())
         v = self._sample(hidden, rng_d).view(b, k + 1)
         if self.synthetic > 0.0 and k > 0:
@@ -280,15 +297,74 @@ class MTPDriver:
             m_sel = m.index_select(0, rows)
             tok = self._sample(m_sel, rng_d)
             new = self._draft_steps(tok, m_sel, (pos_d + acc).to(torch.int32), bt_d, caps_d, st_d, rng_d,
-                                    slots_host, int(pos0.max()) + k + 1)
+                                    slots_host or [], max_k)
             self.drafts.index_copy_(0, st_d.long(), new)
+        return torch.cat((v.reshape(-1).to(torch.int32), acc))
 
-        # ---- one device->host copy of (v, a)
-        host = torch.cat((v.reshape(-1).to(torch.int32), acc)).to("cpu")
-        r.d2h_bytes += host.numel() * 4
+    # ---------------------------------------------------------- graphs
+    def _bucket(self, b: int) -> int | None:
+        for s in sorted(self.graphs):
+            if s >= b:
+                return s
+        return None
+
+    @torch.inference_mode()
+    def capture(self, sizes: list[int]) -> None:
+        """One CUDA graph per batch bucket for the whole round (verify, accept, commit, drafts)."""
+        r = self.r
+        pool = None
+        for b in sorted(sizes, reverse=True):
+            flat = self._pack([], b)
+            meta = torch.from_numpy(flat).to(r.device)
+            big = int(r.config.max_model_len) + 2 * self.k + 1
+            self._round_device(meta, b, None, big)  # warm-up outside the capture
+            torch.cuda.synchronize(r.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=pool):
+                out = self._round_device(meta, b, None, big)
+            if pool is None:
+                pool = g.pool()
+            self.graphs[b] = g
+            self.graph_bufs[b] = (meta, out)
+        torch.cuda.synchronize(r.device)
+        if r.state_manager is not None:
+            r.state_manager.reset_scratch()
+
+    @torch.inference_mode()
+    def run(self, seqs: list[Sequence]):
+        """One speculative round for a decode batch; returns emitted token lists (rank 0)."""
+        t0 = perf_counter_ns()
+        r = self.r
+        k = self.k
+        b = len(seqs)
+        if self.before_round is not None:
+            self.before_round(seqs, self)
+        bucket = self._bucket(b) if self.graphs else None
+        if bucket is not None:
+            flat = self._pack(seqs, bucket)
+            meta, out_dev = self.graph_bufs[bucket]
+            pinned = r._pinned(flat.shape[0])
+            pinned[: flat.shape[0]].copy_(torch.from_numpy(flat))
+            meta.copy_(pinned[: flat.shape[0]], non_blocking=True)
+            r.h2d_bytes += flat.nbytes
+            self.graphs[bucket].replay()
+            self.graph_replays += 1
+            tb = bucket * (k + 1)
+            host = out_dev.to("cpu")
+            vals = host[:tb].view(bucket, k + 1)[:b].tolist()
+            accs = host[tb:tb + b].tolist()
+            r.d2h_bytes += host.numel() * 4
+        else:
+            flat = self._pack(seqs, b)
+            meta = r._upload(flat)
+            slots_host = [s.state_slot if s.state_slot is not None else 0 for s in seqs]
+            max_k = max(len(s) for s in seqs) + k
+            host = self._round_device(meta, b, slots_host, max_k).to("cpu")
+            r.d2h_bytes += host.numel() * 4
+            t = b * (k + 1)
+            vals = host[:t].view(b, k + 1).tolist()
+            accs = host[t:].tolist()
         r.sample_step += 1
-        vals = host[:t].view(b, k + 1).tolist()
-        accs = host[t:].tolist()
         out = [row[: a + 1] for row, a in zip(vals, accs)]
         self.rounds += 1
         self.seq_rounds += b

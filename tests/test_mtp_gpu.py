@@ -32,11 +32,11 @@ def _prompts(n, length, vocab, seed=0):
     return [torch.randint(0, vocab, (length,), generator=g).tolist() for _ in range(n)]
 
 
-def _generate(d, prompts, n, hook=None, **kw):
+def _generate(d, prompts, n, hook=None, eager=True, **kw):
     from inference_systems_b200.llm import LLM
 
     llm = LLM(d, device="cuda", max_num_seqs=4, max_num_state_slots=4, max_model_len=1024, num_kvcache_blocks=32,
-              max_num_batched_tokens=128, enforce_eager=True, **kw)
+              max_num_batched_tokens=128, enforce_eager=eager, **kw)
     if hook is not None:
         llm.model_runner.mtp_driver.before_round = hook
     out = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=n,
@@ -55,8 +55,8 @@ def _prefix(a, b):
     return n
 
 
-@pytest.mark.parametrize("k", [1, 3])
-def test_mtp_oracle_drafts_match_target_only(ckpt, k):
+@pytest.mark.parametrize("k,eager", [(1, True), (3, True), (2, False)])
+def test_mtp_oracle_drafts_match_target_only(ckpt, k, eager):
     d, cfg = ckpt
     prompts = _prompts(3, 40, cfg["vocab_size"], seed=5)
     n = 12
@@ -75,18 +75,21 @@ def test_mtp_oracle_drafts_match_target_only(ckpt, k):
             driver.set_drafts(s.state_slot, drafts)
         rounds[0] += 1
 
-    got, m = _generate(d, prompts, n, hook=hook, num_speculative_tokens=k)
+    got, m = _generate(d, prompts, n, hook=hook, eager=eager, num_speculative_tokens=k)
     prefixes = [_prefix(g, w) for g, w in zip(got, want)]
     assert sum(p == n for p in prefixes) >= 2 and min(prefixes) >= 4, (got, want)
     mtp = m["model_runner"]["mtp"]
     assert mtp["rounds"] > 0 and mtp["accepted_tokens"] > 0
+    if not eager:
+        assert mtp["cudagraph_replays"] == mtp["rounds"]
     assert torch.ops.isb.error_word() == 0
 
 
-def test_mtp_synthetic_acceptance_runs_k_plus_one(ckpt):
+@pytest.mark.parametrize("eager", [True, False])
+def test_mtp_synthetic_acceptance_runs_k_plus_one(ckpt, eager):
     d, cfg = ckpt
     prompts = _prompts(2, 30, cfg["vocab_size"], seed=6)
-    got, m = _generate(d, prompts, 10, num_speculative_tokens=2, mtp_synthetic_acceptance=1.0)
+    got, m = _generate(d, prompts, 10, eager=eager, num_speculative_tokens=2, mtp_synthetic_acceptance=1.0)
     assert [len(g) for g in got] == [10, 10]
     mtp = m["model_runner"]["mtp"]
     assert mtp["acceptance_rate"] == 1.0
