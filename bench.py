@@ -328,6 +328,10 @@ def run_mtp(args, rank: int, world: int) -> dict | None:
         res[mode] = {b: _decode_run(llm, cfg, b, args) for b in batches}
         if mode == "mtp":
             res["mtp_metrics"] = llm.get_runtime_metrics()["model_runner"].get("mtp", {})
+            if args.breakdown:
+                drv = llm.model_runner.mtp_driver
+                kernel_breakdown(drv.graphs[drv._bucket(args.batch)].replay,
+                                 os.path.join(ROOT, "gpurun_out", f"breakdown_mtp{args.mtp}_b{args.batch}.txt"))
         llm.exit()
     if rank > 0:
         return None

@@ -268,11 +268,15 @@ class MTPDriver:
         t = b * (k + 1)
         cu = torch.arange(b + 1, dtype=torch.int32, device=dev) * (k + 1)
         ctx = torch.where(valid, pos_d + k + 1, torch.zeros_like(pos_d)).to(torch.int32)
+        # every verify row attends as its own decode query: row j of a sequence sees positions <= P + j
+        row_ctx = torch.where(valid[:, None], pos2 + 1, torch.zeros_like(pos2)).reshape(-1).to(torch.int32)
+        row_bt = bt_d.repeat_interleave(k + 1, dim=0)
         vbatch = ForwardBatch(
             is_prefill=True, input_ids=ids, positions=pos2.reshape(-1).to(torch.int32), cu_seqlens_q=cu,
             context_lens=ctx, block_tables=bt_d, slot_mapping=sm, state_slots=st_d, logits_indices=cu[1:] - 1,
             max_seqlen_q=k + 1, max_seqlen_k=max_k, cu_seqlens_host=[i * (k + 1) for i in range(b + 1)],
-            slots_host=slots_host or [], num_seqs=b, gdn_verify=self._gdn_records(t))
+            slots_host=slots_host or [], num_seqs=b, gdn_verify=self._gdn_records(t),
+            decode_rows=(row_ctx, row_bt))
         hidden = r.model(vbatch, r.kv_layers(), r.state_layers())
         v = self._sample(hidden, rng_d).view(b, k + 1)
         if self.synthetic > 0.0 and k > 0:

@@ -92,6 +92,9 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
         c = cuda_ops()
         q, gate = c.attn_prepare(qkv, batch.positions, batch.slot_mapping, q_norm, k_norm, cos_sin, k_cache,
                                  v_cache, num_heads, num_kv_heads, head_dim, eps, gated, zero_centered)
+        if batch.is_prefill and batch.decode_rows is not None:
+            row_ctx, row_bt = batch.decode_rows
+            return c.attention_decode(q, gate, k_cache, v_cache, row_ctx, row_bt, scale, gated)
         if batch.is_prefill:
             return c.attention_prefill(q, gate, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
                                        batch.block_tables, scale, gated, batch.max_seqlen_q)

@@ -36,6 +36,10 @@ class ForwardBatch:
     # MTP verify: per GDN layer (rec_k, rec_delta, rec_g, conv_hist) record buffers; the
     # slot pools are then left untouched (see ops.gdn_verify)
     gdn_verify: list | None = None
+    # Few query rows per sequence over a long cached context (MTP verify / catch-up): per-row
+    # (context length [T] int32, block-table row [T, max_blocks] int32) so attention runs every
+    # row as an independent split-KV decode query (causal by each row's own context length)
+    decode_rows: tuple | None = None
 
     @property
     def num_tokens(self) -> int:
