@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--mtp", type=int, default=0,
                    help="K > 0: MTP speculative decode with K drafts vs target-only (BASELINE config 3)")
     p.add_argument("--mtp-accept", type=float, default=0.6, help="seeded draft/target agreement probability")
+    p.add_argument("--prefill-breakdown", action="store_true",
+                   help="profile one prefill step of --batch prompts of --prompt-len tokens (kernel-time shares) and exit")
     p.add_argument("--breakdown", action="store_true",
                    help="after timing, profile 3 decode-graph replays with torch.profiler (kernel-time shares)")
     return p.parse_args()
@@ -203,6 +205,37 @@ def _serve_batch(llm, runner, cfg, b: int, args, clk) -> dict:
         "prefill_s": round(prefill_s, 3),
         "output_len": out_len,
     }
+
+
+def prefill_breakdown(args) -> None:
+    """Kernel-time table of the first prefill step (no JSON line; diagnostics only)."""
+    import torch
+
+    from inference_systems_b200 import SamplingParams
+    from inference_systems_b200.engine.llm_engine import LLMEngine
+    from inference_systems_b200.models.presets import preset
+
+    cfg = preset(args.model)
+    b = args.batch
+    llm = LLMEngine(cfg, load_format="dummy", device="cuda", max_num_seqs=b, max_num_state_slots=b,
+                    max_model_len=args.prompt_len + 64, max_num_batched_tokens=max(16384, args.prompt_len),
+                    enforce_eager=True, gpu_memory_utilization=0.85)
+    g = torch.Generator().manual_seed(0)
+    for _ in range(2):  # first pass warms up, second is profiled
+        for p in torch.randint(0, cfg["vocab_size"], (b, args.prompt_len), generator=g).tolist():
+            llm.add_request(p, SamplingParams(temperature=0.0, max_tokens=1, ignore_eos=True))
+        if _ == 0:
+            while not llm.is_finished():
+                llm.step()
+            continue
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        kernel_breakdown(lambda: llm.step(), os.path.join(ROOT, "gpurun_out", f"prefill_b{b}_len{args.prompt_len}.txt"), n=1)
+        print(json.dumps({"prefill_step_s": round(time.perf_counter() - t0, 4), "batch": b,
+                          "prompt_len": args.prompt_len}), flush=True)
+        while not llm.is_finished():
+            llm.step()
+    llm.exit()
 
 
 def run_isb(args, rank: int, world: int) -> dict | None:
@@ -369,6 +402,9 @@ def main():
         world = args.gpus
     if args.impl == "reference":
         out = run_reference(args, rank, world)
+    elif args.prefill_breakdown:
+        prefill_breakdown(args)
+        out = None
     elif args.mtp > 0:
         out = run_mtp(args, rank, world)
     else:

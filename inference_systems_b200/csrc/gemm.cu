@@ -71,6 +71,9 @@ struct GemmArgs {
   unsigned int* done_ctr;          // local CTA-completion counter (self-resetting)
   const unsigned long long* peer_flags;  // [ndst] flag-array base of each rank; flag index = rank
   int rank;
+  // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
+  // CTA and the accumulator is zero between uses, so plain stores replace the atomics
+  bool acc_plain;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -92,6 +95,10 @@ ISB_DEVICE void red_add_v4_sys(float* p, float a, float b, float c, float d) {
 
 // Add 4 consecutive values at element offset ``off`` of the accumulator(s).
 ISB_DEVICE void acc_add4(const GemmArgs& args, size_t off, float a, float b, float c, float d) {
+  if (args.acc_plain) {
+    *reinterpret_cast<float4*>(args.acc + off) = make_float4(a, b, c, d);
+    return;
+  }
   if (args.ndst == 0) {
     red_add_v4(args.acc + off, a, b, c, d);
     return;
@@ -103,6 +110,10 @@ ISB_DEVICE void acc_add4(const GemmArgs& args, size_t off, float a, float b, flo
 }
 
 ISB_DEVICE void acc_add1(const GemmArgs& args, size_t off, float a) {
+  if (args.acc_plain) {
+    args.acc[off] = a;
+    return;
+  }
   if (args.ndst == 0) {
     atomicAdd(args.acc + off, a);
     return;
@@ -750,6 +761,7 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   args.K = a.size(1);
   args.ldo = N;
   args.kb_per_split = p.kb_per;
+  args.acc_plain = p.splits == 1;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);

@@ -23,6 +23,10 @@ at::Tensor embed(const at::Tensor& ids, const at::Tensor& table, int64_t vocab_s
 at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
                       const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk,
                       int64_t hv, int64_t dk, int64_t dv, double eps);
+at::Tensor gdn_prefill_chunked(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
+                               const at::Tensor& chunk_info, int64_t nc, const at::Tensor& conv_w,
+                               const at::Tensor& A_log, const at::Tensor& dt_bias, const at::Tensor& norm_w,
+                               at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv, double eps);
 at::Tensor gdn_prefill(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
                        const at::Tensor& conv_w, const at::Tensor& A_log, const at::Tensor& dt_bias,
                        const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk, int64_t hv, int64_t dk,
@@ -79,6 +83,10 @@ TORCH_LIBRARY(isb, m) {
       "gdn_decode(Tensor(c!) proj, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, Tensor norm_w, "
       "Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps) -> Tensor");
   m.def(
+      "gdn_prefill_chunked(Tensor proj, Tensor cu_seqlens, Tensor slots, Tensor chunk_info, int nc, Tensor conv_w, "
+      "Tensor A_log, Tensor dt_bias, Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, float eps) "
+      "-> Tensor");
+  m.def(
       "gdn_prefill(Tensor(c!) proj, Tensor cu_seqlens, Tensor slots, Tensor conv_w, Tensor A_log, Tensor dt_bias, "
       "Tensor norm_w, Tensor(a!) rec, Tensor(b!) conv, int hk, int hv, int dk, int dv, float eps, int max_seqlen) "
       "-> Tensor");
@@ -128,6 +136,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("embed", &isb::embed);
   m.impl("gdn_decode", &isb::gdn_decode);
   m.impl("gdn_prefill", &isb::gdn_prefill);
+  m.impl("gdn_prefill_chunked", &isb::gdn_prefill_chunked);
   m.impl("gdn_scan_history", &isb::gdn_scan_history);
   m.impl("gdn_replay_commit", &isb::gdn_replay_commit);
   m.impl("gdn_conv_commit", &isb::gdn_conv_commit);

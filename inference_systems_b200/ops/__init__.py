@@ -8,6 +8,8 @@ error, never a silent fallback.  CPU tensors run the plain-PyTorch contracts in
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from inference_systems_b200.ops import reference as ref
@@ -106,11 +108,68 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
                                scale, gate)
 
 
+_GDN_CHUNKED = os.environ.get("ISB_GDN_CHUNKED", "1") != "0"
+GDN_CHUNK = 64
+
+
+def gdn_chunk_table(batch: ForwardBatch) -> tuple[torch.Tensor, int]:
+    """Device table ``[chunk_seq | chunk_t0 | chunk_n | cu_chunks]`` (int32) of 64-token chunks.
+
+    Built once per forward from the host copy of ``cu_seqlens`` and shared by
+    every GDN layer of that forward.
+    """
+    cached = getattr(batch, "_gdn_chunks", None)
+    if cached is not None:
+        return cached
+    cu = batch.cu_seqlens_host
+    seq, t0, n, cuc = [], [], [], [0]
+    for i in range(len(cu) - 1):
+        for s in range(cu[i], cu[i + 1], GDN_CHUNK):
+            seq.append(i)
+            t0.append(s)
+            n.append(min(GDN_CHUNK, cu[i + 1] - s))
+        cuc.append(len(seq))
+    info = torch.tensor(seq + t0 + n + cuc, dtype=torch.int32).to(batch.cu_seqlens_q.device, non_blocking=True)
+    batch._gdn_chunks = (info, len(seq))
+    return batch._gdn_chunks
+
+
+_SMS: int | None = None
+
+
+def _chunked_is_faster(batch: ForwardBatch, hv: int) -> bool:
+    """Pick the chunked prefill or the token scan for this batch from a cost model fitted on B200.
+
+    Token scan: one CTA per (value head, sequence), two per SM, about 2.9 us per
+    token step, so waves x longest length.  Chunked: the chunk-parallel prep
+    kernel (one CTA per chunk and head, ~100 us, one per SM) plus the state
+    kernel (4 CTAs per head and sequence, ~21 us per chunk, one per SM).
+    """
+    global _SMS
+    if _SMS is None:
+        _SMS = torch.cuda.get_device_properties(batch.cu_seqlens_q.device).multi_processor_count
+    cu = batch.cu_seqlens_host
+    b = len(cu) - 1
+    lens = [cu[i + 1] - cu[i] for i in range(b)]
+    lmax = max(lens, default=0)
+    if lmax < 2:
+        return False
+    nc = sum((n + GDN_CHUNK - 1) // GDN_CHUNK for n in lens)
+    ceil = lambda x, y: -(-x // y)  # noqa: E731
+    scan = ceil(b * hv, 2 * _SMS) * lmax * 2.9
+    chunked = ceil(nc * hv, _SMS) * 100.0 + ceil(4 * hv * b, _SMS) * ceil(lmax, GDN_CHUNK) * 21.0
+    return chunked < scan
+
+
 def gdn(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool, *,
         hk: int, hv: int, dk: int, dv: int, eps: float) -> torch.Tensor:
     """Gated DeltaNet mixer core (conv, norms, delta rule, gated norm); states updated in the pools."""
     if proj.is_cuda:
         c = cuda_ops()
+        if batch.is_prefill and proj.dtype == torch.bfloat16 and _GDN_CHUNKED and _chunked_is_faster(batch, hv):
+            info, nc = gdn_chunk_table(batch)
+            return c.gdn_prefill_chunked(proj, batch.cu_seqlens_q, batch.state_slots, info, nc, conv_w, a_log,
+                                         dt_bias, norm_w, rec_pool, conv_pool, hk, hv, eps)
         if batch.is_prefill:
             return c.gdn_prefill(proj, batch.cu_seqlens_q, batch.state_slots, conv_w, a_log, dt_bias, norm_w,
                                  rec_pool, conv_pool, hk, hv, dk, dv, eps, batch.max_seqlen_q)

@@ -156,6 +156,43 @@ def test_gdn_prefill(lens, hk, hv):
     assert torch.equal(conv_g.cpu(), conv_c)
 
 
+@pytest.mark.parametrize("lens,hk,hv", [([5, 1, 33], 16, 16), ([64, 65, 17], 2, 6), ([300, 128], 4, 4),
+                                         ([1000], 2, 4)])
+def test_gdn_prefill_chunked_matches_scan_and_oracle(lens, hk, hv):
+    from inference_systems_b200.ops import GDN_CHUNK
+
+    b, t = len(lens), sum(lens)
+    proj, conv_w, a_log, dt_bias, norm_w, rec, conv, slots = _gdn_inputs(b, hk, hv, t, t=t)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    rec_c, conv_c = rec.clone(), conv.clone()
+    exp = ref.gdn_forward(proj, cu, slots.tolist(), conv_w, a_log, dt_bias, norm_w, rec_c, conv_c,
+                          hk=hk, hv=hv, dk=128, dv=128, eps=1e-6)
+    seq, t0, nn, cuc = [], [], [], [0]
+    for i in range(b):
+        for st in range(cu[i], cu[i + 1], GDN_CHUNK):
+            seq.append(i)
+            t0.append(st)
+            nn.append(min(GDN_CHUNK, cu[i + 1] - st))
+        cuc.append(len(seq))
+    info = torch.tensor(seq + t0 + nn + cuc, dtype=torch.int32, device=DEV)
+    args = (conv_w.to(DEV), a_log.to(DEV), dt_bias.to(DEV), norm_w.to(DEV))
+    cu_d = torch.tensor(cu, dtype=torch.int32, device=DEV)
+    rec_k, conv_k = rec.to(DEV), conv.to(DEV)
+    out_k = torch.ops.isb.gdn_prefill_chunked(proj.to(DEV), cu_d, slots.to(DEV), info, len(seq), *args, rec_k, conv_k,
+                                              hk, hv, 1e-6)
+    rec_s, conv_s = rec.to(DEV), conv.to(DEV)
+    out_s = torch.ops.isb.gdn_prefill(proj.to(DEV), cu_d, slots.to(DEV), *args, rec_s, conv_s, hk, hv, 128, 128,
+                                      1e-6, max(lens))
+    torch.cuda.synchronize()
+    assert _rel(out_k.cpu(), exp) < 2e-2
+    assert _rel(out_k.float(), out_s.float()) < 2e-2
+    assert _rel(rec_k.cpu(), rec_c) < 1e-3
+    assert _rel(rec_k, rec_s) < 1e-3
+    assert torch.equal(conv_k.cpu(), conv_c)
+
+
 def gate_ref(qkv, hq, hd):
     t = qkv.shape[0]
     return qkv[:, : hq * hd * 2].reshape(t, hq, 2 * hd)[..., hd:].reshape(t, hq * hd)
