@@ -52,6 +52,10 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const a
 at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                              double scale, bool gated, int64_t max_seqlen_q);
+at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
+                                const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
+                                double scale, bool gated, int64_t max_seqlen_q);
+int64_t attn_tc_error_word();
 void quantize_state_int8(const at::Tensor& state, at::Tensor q, at::Tensor scale);
 void dequantize_state_int8(const at::Tensor& q, const at::Tensor& scale, at::Tensor out);
 void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_t n);
@@ -69,7 +73,9 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
                         const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
                         int64_t max_rows);
 
-int64_t error_word() { return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16); }
+int64_t error_word() {
+  return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24);
+}
 }  // namespace isb
 
 TORCH_LIBRARY(isb, m) {
@@ -107,6 +113,9 @@ TORCH_LIBRARY(isb, m) {
       "attention_decode(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
   m.def(
+      "attention_prefill_tc(Tensor q, Tensor gate, Tensor kc, Tensor vc, Tensor cu_q, Tensor ctx_lens, "
+      "Tensor block_tables, float scale, bool gated, int max_seqlen_q) -> Tensor");
+  m.def(
       "attention_prefill(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor cu_seqlens_q, "
       "Tensor context_lens, Tensor block_tables, float scale, bool gated, int max_seqlen_q) -> Tensor");
   m.def("quantize_state_int8(Tensor state, Tensor(a!) q, Tensor(b!) scale) -> ()");
@@ -137,6 +146,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("gdn_decode", &isb::gdn_decode);
   m.impl("gdn_prefill", &isb::gdn_prefill);
   m.impl("gdn_prefill_chunked", &isb::gdn_prefill_chunked);
+  m.impl("attention_prefill_tc", &isb::attention_prefill_tc);
   m.impl("gdn_scan_history", &isb::gdn_scan_history);
   m.impl("gdn_replay_commit", &isb::gdn_replay_commit);
   m.impl("gdn_conv_commit", &isb::gdn_conv_commit);

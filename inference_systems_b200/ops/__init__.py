@@ -97,6 +97,9 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
         if batch.is_prefill and batch.decode_rows is not None:
             row_ctx, row_bt = batch.decode_rows
             return c.attention_decode(q, gate, k_cache, v_cache, row_ctx, row_bt, scale, gated)
+        if batch.is_prefill and _ATTN_TC and head_dim == 256 and num_heads // num_kv_heads in (1, 2, 4, 8):
+            return c.attention_prefill_tc(q, gate, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
+                                          batch.block_tables, scale, gated, batch.max_seqlen_q)
         if batch.is_prefill:
             return c.attention_prefill(q, gate, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
                                        batch.block_tables, scale, gated, batch.max_seqlen_q)
@@ -109,6 +112,7 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
 
 
 _GDN_CHUNKED = os.environ.get("ISB_GDN_CHUNKED", "1") != "0"
+_ATTN_TC = os.environ.get("ISB_ATTN_TC", "1") != "0"
 GDN_CHUNK = 64
 
 

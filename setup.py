@@ -14,7 +14,7 @@ from setuptools import setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 CSRC = Path("inference_systems_b200") / "csrc"
-SOURCES = ["ops.cpp", "gemm.cu", "norm.cu", "gdn.cu", "gdn_chunk.cu", "attention.cu", "state.cu", "comm.cu"]
+SOURCES = ["ops.cpp", "gemm.cu", "norm.cu", "gdn.cu", "gdn_chunk.cu", "attention.cu", "attention_tc.cu", "state.cu", "comm.cu"]
 
 NVCC_FLAGS = [
     "-O3",

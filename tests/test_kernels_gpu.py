@@ -255,6 +255,28 @@ def test_attention_prefill(hq, hkv, new, past):
     assert _rel(out.cpu(), exp) < 2e-2
 
 
+@pytest.mark.parametrize("hq,hkv,new,past", [(8, 2, [7, 1, 40], [0, 5, 300]), (8, 2, [300, 65], [0, 200]),
+                                              (4, 1, [257], [0]), (2, 1, [130], [100]), (16, 2, [20, 9], [64, 0])])
+def test_attention_prefill_tensor_core(hq, hkv, new, past):
+    hd = 256
+    qkv, qn, kn, cos_sin, kc, vc, m = _attn_case(7 * hq + sum(new), hq, hkv, hd, new, past)
+    q, gate, k, v = ref.attn_qkv_prepare(qkv, m["positions"], qn, kn, cos_sin, hq, hkv, hd, 1e-6, True, True)
+    kc_r, vc_r = kc.clone(), vc.clone()
+    ref.store_kv(k, v, kc_r, vc_r, m["slot_mapping"])
+    exp = ref.paged_attention(q, kc_r, vc_r, m["cu"], m["ctx"], m["bt"], hd ** -0.5, gate)
+    kc_g, vc_g = kc.to(DEV), vc.to(DEV)
+    qg, gate_g = torch.ops.isb.attn_prepare(qkv.to(DEV), m["positions"].to(DEV), m["slot_mapping"].to(DEV),
+                                            qn.to(DEV), kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6,
+                                            True, True)
+    args = (qg, gate_g, kc_g, vc_g, m["cu"].to(DEV), m["ctx"].to(DEV), m["bt"].to(DEV), hd ** -0.5, True, max(new))
+    out_tc = torch.ops.isb.attention_prefill_tc(*args)
+    out_simt = torch.ops.isb.attention_prefill(*args)
+    torch.cuda.synchronize()
+    assert torch.ops.isb.error_word() == 0
+    assert _rel(out_tc.cpu(), exp) < 2e-2
+    assert _rel(out_tc.float(), out_simt.float()) < 2e-2
+
+
 @pytest.mark.parametrize("hq,hkv,past", [(8, 2, [0, 5, 300, 1000]), (4, 1, [255]), (24, 4, [2000, 1]),
                                          (3, 1, [700])])
 def test_attention_decode(hq, hkv, past):
