@@ -2,18 +2,21 @@
 //
 // Symmetric buffers: every rank cudaMalloc's one region, exports a CUDA IPC
 // handle, and maps every peer's region (``symm_alloc`` / ``symm_open``); kernels
-// then address peers with plain device pointers (P2P loads, stores and atomics
-// through NVSwitch).  Synchronisation between ranks uses monotone flag words in
-// the symmetric region: a producer RELEASES ``flags[rank] += 1`` on each peer at
-// system scope, a consumer ACQUIRES until every flag is >= 1 and, when all of its
-// blocks are done, takes the ones it consumed back.  Every wait is bounded by a
-// %globaltimer deadline; a timeout records an error word (read by
-// ``comm_error_word``) and later waits return at once, so a missing peer can
-// never hang a GPU.
+// then address peers with plain device pointers (P2P loads and stores through
+// NVSwitch).  Synchronisation between ranks uses monotone counters in the
+// symmetric region, released at system scope by their owner and acquired by
+// peers.  Every wait is bounded by a %globaltimer deadline; a timeout records an
+// error word (read by ``comm_error_word``) and later waits return at once, so a
+// missing peer can never hang a GPU.
 //
-//  * add_rmsnorm_acc_tp: consumer of the fused row-parallel GEMM all-reduce
-//    (gemm.cu ``tp_gemm_accum``): waits for all ranks' tiles, then
-//    residual += acc, out = RMSNorm(residual), acc <- 0.
+//  * add_rmsnorm_acc_tp: second half of the fused row-parallel GEMM all-reduce.
+//    Each rank's GEMM (gemm.cu ``tp_gemm_accum``) reduced its partial product
+//    into its own fp32 accumulator and bumped its own counter; this kernel waits
+//    until every peer's counter has reached this rank's, sums all ranks'
+//    accumulators with P2P loads, adds the residual and applies the next
+//    RMSNorm.  Accumulators alternate between two parities per call, and the
+//    buffer of the previous call is re-zeroed here: every peer finished reading
+//    it, because each peer's current GEMM started after its previous consumer.
 //  * xrank_argmax: cross-rank (score, token) argmax of the vocab-parallel LM
 //    head; each rank publishes 8 bytes per row to every peer instead of gathering logits.
 
@@ -76,61 +79,90 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = raw;
 }
 
-// One warp per row (4 rows per block).  Block 0..n: wait, consume, count; the last block
-// returns the consumed flag units.
-__global__ void acc_norm_tp_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
-                                   const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows,
-                                   int H, float eps, bool zc, unsigned int* flags, int world, unsigned int* done) {
+// Wait until every counter flags[r] (peer memory) has reached ``target`` (bounded).
+ISB_DEVICE bool wait_counters(const unsigned long long* flags, int n, unsigned int target) {
+  if (*reinterpret_cast<volatile unsigned int*>(&g_comm_err) != 0u) return false;
+  const uint64_t t0 = globaltimer_ns();
+  for (int r = 0; r < n; ++r) {
+    const unsigned int* f = reinterpret_cast<const unsigned int*>(flags[r]);
+    uint32_t spins = 0;
+    while (int(ld_acquire_sys(f) - target) < 0) {
+      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(&g_comm_err, 1u);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// One block of 128 threads per row (8 columns per thread per step).
+__global__ void __launch_bounds__(128) acc_norm_tp_kernel(const unsigned long long* __restrict__ accs,
+                                                          float* __restrict__ my_other,
+                                                          __nv_bfloat16* __restrict__ residual,
+                                                          const __nv_bfloat16* __restrict__ w,
+                                                          __nv_bfloat16* __restrict__ out, int rows, int H, float eps,
+                                                          bool zc, const unsigned long long* flags,
+                                                          const unsigned int* my_flag, int world,
+                                                          unsigned int* rows_used, int parity) {
   pdl_trigger();
   pdl_wait();
   __shared__ int ok;
-  if (threadIdx.x == 0) ok = wait_flags(flags, world);
+  __shared__ float red[4];
+  const int tid = threadIdx.x, row = blockIdx.x;
+  if (tid == 0) {
+    const unsigned int target = ld_acquire_sys(my_flag);  // this rank's GEMM of this call has completed
+    ok = wait_counters(flags, world, target);
+  }
   __syncthreads();
-  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  // re-zero the accumulator rows of the previous call (other parity); peers are done with them
+  const int prev_rows = int(rows_used[parity ^ 1]);
+  for (int r = row; r < prev_rows; r += gridDim.x)
+    for (int c = tid * 4; c < H; c += 512) *reinterpret_cast<float4*>(my_other + size_t(r) * H + c) = make_float4(0.f, 0.f, 0.f, 0.f);
   if (row < rows) {
-    float* a = acc + size_t(row) * H;
     __nv_bfloat16* res = residual + size_t(row) * H;
     float ss = 0.f;
-    for (int c = lane * 8; c < H; c += 256) {
-      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
-      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
-      const Vec8 r = load8(res + c);
-      const float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
-                          x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
+    constexpr int kMaxChunks = 8;  // H <= 8 * 1024
+    float v[kMaxChunks][8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = tid * 8 + k * 1024;
+      if (c >= H) break;
+      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        for (int r = 0; r < world; ++r) {
+          const float* a = reinterpret_cast<const float*>(accs[r]) + size_t(row) * H + c;
+          const float4 x0 = __ldcv(reinterpret_cast<const float4*>(a));
+          const float4 x1 = __ldcv(reinterpret_cast<const float4*>(a + 4));
+          x[0] += x0.x; x[1] += x0.y; x[2] += x0.z; x[3] += x0.w;
+          x[4] += x1.x; x[5] += x1.y; x[6] += x1.z; x[7] += x1.w;
+        }
+      }
+      const Vec8 rr = load8(res + c);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        v[k][i] = x[i] + rr.v[i];
+        ss += v[k][i] * v[k][i];
+      }
     }
     ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / float(H) + eps);
-    for (int c = lane * 8; c < H; c += 256) {
-      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
-      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
-      const Vec8 r = load8(res + c);
-      float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
-                    x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
-      store8(res + c, v);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    const float rs = rsqrtf((red[0] + red[1] + red[2] + red[3]) / float(H) + eps);
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = tid * 8 + k * 1024;
+      if (c >= H) break;
+      store8(res + c, v[k]);
       const Vec8 wv = load8(w + c);
       float y[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        y[i] = zc ? v[i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[i] * rs)) * wv.v[i];
+        y[i] = zc ? v[k][i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[k][i] * rs)) * wv.v[i];
       store8(out + size_t(row) * H + c, y);
-      *reinterpret_cast<float4*>(a + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<float4*>(a + c + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
   }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    const unsigned int prev = atomicAdd(done, 1u);
-    if (prev == gridDim.x - 1) {
-      *done = 0u;
-      if (ok)
-        for (int r = 0; r < world; ++r) atomicSub(flags + r, 1u);
-      __threadfence_system();
-    }
-  }
+  if (row == 0 && tid == 0) rows_used[parity] = unsigned(rows);
 }
 
 // Single CTA.  Publish this rank's (score, token) per row to every peer's exchange slot,
@@ -203,19 +235,25 @@ int64_t symm_open(const at::Tensor& handle) {
 
 void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
 
-at::Tensor add_rmsnorm_acc_tp(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc,
-                              at::Tensor flags, at::Tensor done) {
-  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous(), "accumulator must be contiguous fp32");
+at::Tensor add_rmsnorm_acc_tp(const at::Tensor& accs, at::Tensor my_acc_other, at::Tensor residual,
+                              const at::Tensor& w, double eps, bool zc, const at::Tensor& flags,
+                              const at::Tensor& my_flag, at::Tensor rows_used, int64_t parity) {
+  TORCH_CHECK(accs.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && accs.numel() == flags.numel(),
+              "accs / flags must be int64 device tables of equal length");
+  TORCH_CHECK(my_acc_other.scalar_type() == at::kFloat && my_acc_other.is_contiguous(), "fp32 accumulator");
   TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16, "residual must be bf16");
-  TORCH_CHECK(flags.scalar_type() == at::kInt && done.scalar_type() == at::kInt, "int32 flag words");
+  TORCH_CHECK(my_flag.scalar_type() == at::kInt && rows_used.scalar_type() == at::kInt && rows_used.numel() == 2,
+              "int32 flag / row-count words");
   const int H = residual.size(-1), rows = residual.numel() / H;
+  TORCH_CHECK(H % 8 == 0 && H <= 8192, "hidden size must be a multiple of 8 and at most 8192");
   at::Tensor out = at::empty_like(residual);
-  const int blocks = std::max(1, (rows + 3) / 4);
-  launch_pdl(acc_norm_tp_kernel, dim3(blocks), dim3(128), 0, at::cuda::getCurrentCUDAStream(), 
-      acc.data_ptr<float>(), reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows,
-      H, float(eps), zc, reinterpret_cast<unsigned int*>(flags.data_ptr<int>()), int(flags.numel()),
-      reinterpret_cast<unsigned int*>(done.data_ptr<int>()));
+  launch_pdl(acc_norm_tp_kernel, dim3(std::max(rows, 1)), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()), my_acc_other.data_ptr<float>(),
+             reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H, float(eps), zc,
+             reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned int*>(my_flag.data_ptr<int>()), int(flags.numel()),
+             reinterpret_cast<unsigned int*>(rows_used.data_ptr<int>()), int(parity));
   return out;
 }
 

@@ -74,6 +74,9 @@ struct GemmArgs {
   // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
   // CTA and the accumulator is zero between uses, so plain stores replace the atomics
   bool acc_plain;
+  // when set, the grid's last CTA releases ``*signal += 1`` at system scope after every CTA's tile
+  // is in ``acc`` (tensor-parallel peers poll it before reading this rank's accumulator)
+  unsigned int* signal;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -485,7 +488,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if (dbg && threadIdx.x == 64) dbg[6] = globaltimer_ns();
   if constexpr (EPI == kRedAdd) {
-    if (args.ndst > 0) {
+    if (args.signal != nullptr) {
+      if (epi) asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+        unsigned int prev;
+        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(args.done_ctr) : "memory");
+        if (prev == total - 1) {
+          *args.done_ctr = 0u;
+          asm volatile("fence.acq_rel.sys;" ::: "memory");
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(args.signal) : "memory");
+        }
+      }
+    } else if (args.ndst > 0) {
       // every rank's accumulator got this CTA's tile: count the CTA; the last one releases
       // a flag on every rank (flag index = this rank) at system scope.
       if (epi) asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -768,18 +784,20 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }
 
-// Tensor-parallel row-parallel GEMM fused with the all-reduce: every CTA adds its fp32 tile
-// into the accumulator of EVERY rank (peer memory, system-scope vector atomics over NVLink);
-// the grid's last CTA then releases flag[rank] on each rank.  ``dsts`` / ``flags`` are int64
-// device tensors of the ranks' accumulator / flag-array base addresses.
-void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& dsts, const at::Tensor& flags,
-                   at::Tensor done_ctr, int64_t rank, int64_t splits) {
+// Tensor-parallel row-parallel GEMM, first half of the fused all-reduce: the rank-local
+// partial product is reduced into this rank's accumulator exactly as in ``gemm_accum``
+// (split-K CTAs add their fp32 tiles) and the grid's last CTA then releases ``flag += 1``
+// at system scope, so peers know the accumulator is complete and can read it over NVLink
+// (``add_rmsnorm_acc_tp`` sums every rank's accumulator).
+void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, at::Tensor flag,
+                   at::Tensor done_ctr, int64_t splits) {
   at::Tensor a = a_in.contiguous();
   check_operands(a, b);
   const int M = a.size(0), N = b.size(0);
-  TORCH_CHECK(dsts.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && dsts.numel() == flags.numel(),
-              "dsts / flags must be int64 device tables of equal length");
-  TORCH_CHECK(done_ctr.scalar_type() == at::kInt, "done counter must be int32");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) >= M && acc.size(1) == N,
+              "accumulator must be contiguous fp32 [>= M, N]");
+  TORCH_CHECK(flag.scalar_type() == at::kInt && done_ctr.scalar_type() == at::kInt, "int32 flag / counter words");
+  if (M == 0) return;
   const int kb_total = (int(a.size(1)) + BK - 1) / BK;
   Plan p = plan_gemm(a, b, false, 1);
   int sp = splits > 0 ? int(splits) : 1;
@@ -790,17 +808,15 @@ void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
   p.kb_per = (kb_total + sp - 1) / sp;
   p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
   GemmArgs args = {};
+  args.acc = acc.data_ptr<float>();
   args.K = a.size(1);
   args.ldo = N;
   args.kb_per_split = p.kb_per;
-  args.dsts = reinterpret_cast<const unsigned long long*>(dsts.data_ptr<int64_t>());
-  args.ndst = int(dsts.numel());
+  args.acc_plain = p.splits == 1;
+  args.signal = reinterpret_cast<unsigned int*>(flag.data_ptr<int>());
   args.done_ctr = reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>());
-  args.peer_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
-  args.rank = int(rank);
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (M == 0) return;
   if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }

@@ -62,13 +62,14 @@ void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_
 
 int64_t attn_error_word();
 int64_t comm_error_word();
-void tp_gemm_accum(const at::Tensor& a, const at::Tensor& b, const at::Tensor& dsts, const at::Tensor& flags,
-                   at::Tensor done_ctr, int64_t rank, int64_t splits);
+void tp_gemm_accum(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, at::Tensor flag, at::Tensor done_ctr,
+                   int64_t splits);
 std::tuple<at::Tensor, at::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const at::Tensor& handle);
 void symm_close(int64_t ptr);
-at::Tensor add_rmsnorm_acc_tp(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc,
-                              at::Tensor flags, at::Tensor done);
+at::Tensor add_rmsnorm_acc_tp(const at::Tensor& accs, at::Tensor my_acc_other, at::Tensor residual,
+                              const at::Tensor& w, double eps, bool zc, const at::Tensor& flags,
+                              const at::Tensor& my_flag, at::Tensor rows_used, int64_t parity);
 at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,
                         const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
                         int64_t max_rows);
@@ -126,12 +127,12 @@ TORCH_LIBRARY(isb, m) {
   m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
-  m.def("tp_gemm_accum(Tensor a, Tensor b, Tensor dsts, Tensor flags, Tensor(a!) done_ctr, int rank, int splits=0) -> ()");
+  m.def("tp_gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, Tensor(b!) flag, Tensor(c!) done_ctr, int splits=0) -> ()");
   m.def("symm_alloc(int nbytes) -> (Tensor, Tensor)");
   m.def("symm_open(Tensor handle) -> int");
   m.def("symm_close(int ptr) -> ()");
-  m.def("add_rmsnorm_acc_tp(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered, "
-        "Tensor(c!) flags, Tensor(d!) done) -> Tensor");
+  m.def("add_rmsnorm_acc_tp(Tensor accs, Tensor(a!) my_acc_other, Tensor(b!) residual, Tensor w, float eps, "
+        "bool zero_centered, Tensor flags, Tensor my_flag, Tensor(c!) rows_used, int parity) -> Tensor");
   m.def("xrank_argmax(Tensor val, Tensor idx, Tensor xbufs, Tensor peer_flags, Tensor(a!) my_flags, Tensor my_xbuf, "
         "int rank, int max_rows) -> Tensor");
 }

@@ -8,13 +8,14 @@ then broadcasts sampled tokens (``nanovllm/engine/model_runner.py:668-702``).
 
 Here, on GPUs:
 
-* ``row_parallel_residual_norm`` = ONE GEMM kernel whose CTAs add their fp32
-  tiles into every rank's accumulator over NVLink peer memory
-  (``tp_gemm_accum``) + ONE consumer kernel that waits for all ranks' release
-  flags, adds the residual and applies the next RMSNorm
-  (``add_rmsnorm_acc_tp``).  The accumulators are double-buffered by call
-  parity so a rank that runs one layer ahead never writes into a buffer a
-  peer is still reading.
+* ``row_parallel_residual_norm`` = ONE GEMM kernel that reduces this rank's
+  partial product into its own fp32 accumulator (split-K tiles added locally)
+  and whose last CTA bumps this rank's completion counter
+  (``tp_gemm_accum``) + ONE consumer kernel that waits until every peer's
+  counter has caught up, sums all ranks' accumulators with NVLink P2P loads,
+  adds the residual and applies the next RMSNorm (``add_rmsnorm_acc_tp``).
+  Accumulators alternate between two parities per call; the consumer re-zeroes
+  the previous call's buffer, which every peer has finished reading by then.
 * ``lm_head_sample`` = the LM-head GEMM with its fused greedy/Gumbel-max
   selection on this rank's vocab slice + ``xrank_argmax``, which exchanges 8
   bytes per row with every peer; every rank ends with the same token ids.
@@ -90,6 +91,7 @@ class TPComm:
         self.acc_local = [local("acc0", torch.float32, self.max_rows * h).view(self.max_rows, h),
                           local("acc1", torch.float32, self.max_rows * h).view(self.max_rows, h)]
         self.accflag_local = [local("accflag0", torch.int32, w), local("accflag1", torch.int32, w)]
+        self.rows_used = torch.zeros(2, dtype=torch.int32, device=self.device)
         self.gdone = [local("gdone0", torch.int32, 1), local("gdone1", torch.int32, 1)]
         self.ndone = [local("ndone0", torch.int32, 1), local("ndone1", torch.int32, 1)]
         self.xbuf_ptrs = table("xbuf")
@@ -116,9 +118,10 @@ class TPComm:
             c = ops.cuda_ops()
             s = self.set
             self.set ^= 1
-            c.tp_gemm_accum(x, w, self.acc_ptrs[s], self.accflag_ptrs[s], self.gdone[s], self.rank, 0)
-            return c.add_rmsnorm_acc_tp(self.acc_local[s][:t], residual, norm_w, eps, zero_centered,
-                                        self.accflag_local[s], self.ndone[s])
+            c.tp_gemm_accum(x, w, self.acc_local[s], self.accflag_local[s][:1], self.gdone[s], 0)
+            return c.add_rmsnorm_acc_tp(self.acc_ptrs[s], self.acc_local[s ^ 1], residual, norm_w, eps,
+                                        zero_centered, self.accflag_ptrs[s], self.accflag_local[s][:1],
+                                        self.rows_used, s)
         y = ops.linear(x, w)
         dist.all_reduce(y, group=self.group)
         return ops.add_rmsnorm(y, residual, norm_w, eps, zero_centered)
