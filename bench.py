@@ -140,6 +140,20 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- own engine
+def model_desc(name: str) -> tuple[str, str]:
+    """(config.model text, data text) for a preset, from its dimensions."""
+    from inference_systems_b200.models.presets import preset
+
+    c = preset(name)
+    types = c.get("layer_types") or []
+    n_lin = sum(t == "linear_attention" for t in types)
+    size = {"qwen3_5-0.8b": "0.8B", "qwen3_5-9b": "9B", "qwen3_5-27b": "27B"}.get(name, name)
+    model = (f"Qwen3.5-{size}-shape hybrid ({c['num_hidden_layers']} layers, {n_lin} GDN + "
+             f"{len(types) - n_lin} gated attention, hidden {c['hidden_size']}, vocab {c['vocab_size']})")
+    data = f"synthetic (uniform-random token ids; random-init N(0,0.02) weights of the {size} architecture)"
+    return model, data
+
+
 def _p50(xs):
     xs = sorted(x for x in xs if x is not None)
     return round(xs[len(xs) // 2], 3) if xs else None
@@ -276,11 +290,11 @@ def run_isb(args, rank: int, world: int) -> dict | None:
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
-        "data": "synthetic (uniform-random token ids; random-init N(0,0.02) weights of the 0.8B architecture)",
-        "config": {"model": "Qwen3.5-0.8B-shape hybrid (24 layers, 18 GDN + 6 gated attention, hidden 1024, vocab 248320)",
+        "data": model_desc(args.model)[1],
+        "config": {"model": model_desc(args.model)[0],
                    "global_batch": args.batch, "seq_len": args.prompt_len, "output_len": head["output_len"],
                    "parallelism": f"tp{world}",
-                   "l2": "inputs larger than L2 (weights 1.5 GB + GDN state per step exceed the 126 MB L2)",
+                   "l2": "inputs larger than L2 (weights and GDN state read per step exceed the 126 MB L2)",
                    "cuda_graph_decode": True},
         "clocks": clk.summary(),
         "e2e": {"value": head["e2e_value"], "unit": "tokens/s", "h2d_bytes_per_step": head["h2d_bytes_per_step"],

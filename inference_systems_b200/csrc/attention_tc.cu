@@ -60,7 +60,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 template <int G>
 __global__ void __launch_bounds__(256, 1)
     attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, TcArgs a) {
-  constexpr int QT = MR / G;
+  constexpr int QT = MR / G;          // tokens per tile; G * QT <= 128 rows are used
+  constexpr int QROWS = G * QT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = smem;
@@ -115,7 +116,7 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0) {
     // ---------------------------------------------------- TMA: Q once, K blocks
     if (lane == 0) {
-      mbar_arrive_expect_tx(qfull, Q_BYTES);
+      mbar_arrive_expect_tx(qfull, QROWS * HD * 2);  // rows past QROWS stay unused
       for (int c = 0; c < 4; ++c) tma_load_3d(q_s + c * (Q_BYTES / 4), &tmQ, qfull, c * 64, kvh * G, q_start + q0);
       for (int j = 0; j < nkb; ++j) {
         const int s = j & 1;
@@ -202,7 +203,7 @@ __global__ void __launch_bounds__(256, 1)
     const int r = threadIdx.x - 128;                       // query row == TMEM lane
     const uint32_t lane_base = uint32_t((warp & 3) * 32) << 16;
     const int q_local = q0 + r / G;
-    const bool row_ok = q_local < nq;
+    const bool row_ok = r < QROWS && q_local < nq;
     const int qpos = past + q_local;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
@@ -351,7 +352,7 @@ void launch_tc(const at::Tensor& q, const at::Tensor& kc, const TcArgs& a, int B
 bool attention_prefill_tc_supported(int64_t hd, int64_t hq, int64_t hkv) {
   if (hd != HD || hq % hkv) return false;
   const int64_t g = hq / hkv;
-  return g == 1 || g == 2 || g == 4 || g == 8;
+  return g == 1 || g == 2 || g == 3 || g == 4 || g == 6 || g == 8;
 }
 
 at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
@@ -379,7 +380,9 @@ at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, con
   switch (Hq / Hkv) {
     case 1: launch_tc<1>(q, kc, a, B, int(max_seqlen_q), st); break;
     case 2: launch_tc<2>(q, kc, a, B, int(max_seqlen_q), st); break;
+    case 3: launch_tc<3>(q, kc, a, B, int(max_seqlen_q), st); break;
     case 4: launch_tc<4>(q, kc, a, B, int(max_seqlen_q), st); break;
+    case 6: launch_tc<6>(q, kc, a, B, int(max_seqlen_q), st); break;
     case 8: launch_tc<8>(q, kc, a, B, int(max_seqlen_q), st); break;
     default: TORCH_CHECK(false, "unsupported GQA group");
   }

@@ -97,7 +97,7 @@ def attention_block(qkv: torch.Tensor, batch: ForwardBatch, q_norm: torch.Tensor
         if batch.is_prefill and batch.decode_rows is not None:
             row_ctx, row_bt = batch.decode_rows
             return c.attention_decode(q, gate, k_cache, v_cache, row_ctx, row_bt, scale, gated)
-        if batch.is_prefill and _ATTN_TC and head_dim == 256 and num_heads // num_kv_heads in (1, 2, 4, 8):
+        if batch.is_prefill and _ATTN_TC and head_dim == 256 and num_heads // num_kv_heads in (1, 2, 3, 4, 6, 8):
             return c.attention_prefill_tc(q, gate, k_cache, v_cache, batch.cu_seqlens_q, batch.context_lens,
                                           batch.block_tables, scale, gated, batch.max_seqlen_q)
         if batch.is_prefill:

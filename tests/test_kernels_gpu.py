@@ -256,7 +256,8 @@ def test_attention_prefill(hq, hkv, new, past):
 
 
 @pytest.mark.parametrize("hq,hkv,new,past", [(8, 2, [7, 1, 40], [0, 5, 300]), (8, 2, [300, 65], [0, 200]),
-                                              (4, 1, [257], [0]), (2, 1, [130], [100]), (16, 2, [20, 9], [64, 0])])
+                                              (4, 1, [257], [0]), (2, 1, [130], [100]), (16, 2, [20, 9], [64, 0]),
+                                              (6, 1, [100, 43], [0, 300]), (12, 4, [50], [10]), (3, 1, [90], [0])])
 def test_attention_prefill_tensor_core(hq, hkv, new, past):
     hd = 256
     qkv, qn, kn, cos_sin, kc, vc, m = _attn_case(7 * hq + sum(new), hq, hkv, hd, new, past)
