@@ -110,9 +110,11 @@ __global__ void __launch_bounds__(128) acc_norm_tp_kernel(const unsigned long lo
   __shared__ int ok;
   __shared__ float red[4];
   const int tid = threadIdx.x, row = blockIdx.x;
-  if (tid == 0) {
+  if (tid == 0) ok = 1;
+  __syncthreads();
+  if (tid < world) {  // every peer's counter is polled by its own thread: one NVLink round trip, not world
     const unsigned int target = ld_acquire_sys(my_flag);  // this rank's GEMM of this call has completed
-    ok = wait_counters(flags, world, target);
+    if (!wait_counters(flags + tid, 1, target)) ok = 0;
   }
   __syncthreads();
   // re-zero the accumulator rows of the previous call (other parity); peers are done with them
