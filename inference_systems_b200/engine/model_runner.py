@@ -358,11 +358,12 @@ class ModelRunner:
             flat, layout, meta = self._pack(seqs, is_prefill)
             dev = self._upload(flat)
             batch, rng, temps = self._batch_from(dev, layout, meta, is_prefill)
+            marks = self._internal_history(seqs, batch, meta, internal_boundaries) if is_prefill else None
             toks = self._forward_sample(batch, rng, temps)
             if is_prefill and self.mtp is not None:
                 self.mtp_driver.after_prefill(seqs, batch, self._last_hidden, toks, rng)
-            if is_prefill and internal_boundaries:
-                self._capture_internal_states(seqs, internal_boundaries)
+            if marks:
+                self._capture_internal_states(batch, marks)
         self.sample_step += 1
         out = self._tokens_to_host(toks, b)
         self.forward_calls += 1
@@ -373,8 +374,38 @@ class ModelRunner:
         self.profiler.record_cpu("target_only.run", (perf_counter_ns() - t0) / 1e6)
         return out if self.rank == 0 else None
 
-    def _capture_internal_states(self, seqs, boundaries) -> None:
-        raise NotImplementedError("internal hybrid checkpoints are captured by the prefill history path")
+    def _internal_history(self, seqs, batch: ForwardBatch, meta, boundaries) -> list | None:
+        """Attach GDN history buffers for checkpoint boundaries strictly inside this prefill chunk."""
+        if not boundaries or self.state_manager is None:
+            return None
+        sm = self.state_manager
+        cu = meta["cu_host"]
+        rows = [-1] * batch.num_tokens
+        marks = []  # (state slot, boundary tokens, history row)
+        for i, s in enumerate(seqs):
+            for b in boundaries.get(s.seq_id, ()):
+                t = cu[i] + (b - 1 - s.num_cached_tokens)
+                if cu[i] <= t < cu[i + 1]:
+                    rows[t] = len(marks)
+                    marks.append((s.state_slot, b, t))
+        if not marks:
+            return None
+        r = len(marks)
+        rs, cs = sm.recurrent_states.shape, sm.conv_states.shape
+        batch.gdn_history = {
+            "rows": torch.tensor(rows, dtype=torch.int32).to(self.device),
+            "rec": [torch.empty(r, *rs[2:], dtype=torch.float32, device=self.device) for _ in range(rs[0])],
+            "conv": [torch.empty(r, *cs[2:], dtype=sm.conv_states.dtype, device=self.device) for _ in range(cs[0])],
+        }
+        return marks
+
+    def _capture_internal_states(self, batch: ForwardBatch, marks) -> None:
+        """Keep the recorded (recurrent, conv) states until the engine publishes the checkpoints."""
+        h = batch.gdn_history
+        for k, (slot, boundary, _) in enumerate(marks):
+            rec = torch.stack([layer[k] for layer in h["rec"]])
+            conv = torch.stack([layer[k] for layer in h["conv"]])
+            self.internal_prefix_states[(slot, boundary)] = (rec, conv)
 
     # ======================================================= CUDA graphs
     def _graph_bucket(self, b: int) -> int | None:

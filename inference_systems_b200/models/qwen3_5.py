@@ -205,11 +205,15 @@ class GDNMixer(nn.Module):
         }
 
     def forward(self, x: torch.Tensor, batch: ForwardBatch, pools: tuple[torch.Tensor, torch.Tensor],
-                records: tuple | None = None) -> torch.Tensor:
+                records: tuple | None = None, history: tuple | None = None) -> torch.Tensor:
         proj = self.scratch.project(x, self.in_proj) if self.scratch is not None else None
         if proj is None:
             proj = ops.linear(x, self.in_proj)
         rec_pool, conv_pool = pools
+        if history is not None:
+            return ops.gdn_with_history(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool,
+                                        conv_pool, *history, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv,
+                                        eps=self.eps)
         if records is not None:
             return ops.gdn_verify(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool,
                                   conv_pool, *records, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
@@ -402,7 +406,11 @@ class HybridCausalLM(nn.Module):
         for i, layer in enumerate(layers):
             if layer.is_linear:
                 rec = batch.gdn_verify[gdn_j] if batch.gdn_verify is not None else None
-                y = layer.mixer(x, batch, state_pools[gdn_j], rec)
+                hist = None
+                if batch.gdn_history is not None:
+                    h = batch.gdn_history
+                    hist = (h["rows"], h["rec"][gdn_j], h["conv"][gdn_j])
+                y = layer.mixer(x, batch, state_pools[gdn_j], rec, hist)
                 gdn_j += 1
             else:
                 y = layer.mixer(x, batch, kv_caches[attn_j], cos_sin)

@@ -217,6 +217,41 @@ def gdn_verify(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, 
     return out
 
 
+def gdn_with_history(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool,
+                     rows: torch.Tensor, hist_rec: torch.Tensor, hist_conv: torch.Tensor, *, hk: int, hv: int, dk: int,
+                     dv: int, eps: float) -> torch.Tensor:
+    """GDN mixer that also records the state after selected tokens (token-recurrent scan).
+
+    ``rows[t] >= 0`` marks token row ``t``: the recurrent / conv state right after
+    it goes to ``hist_rec[rows[t]]`` / ``hist_conv[rows[t]]``; the final states are
+    written back to the pools as usual.  Used for hybrid prefix checkpoints taken
+    inside a prefill chunk (reference: ``capture_tensors`` of internal
+    checkpoints, ``nanovllm/engine/state_manager.py:328-546``).
+    """
+    if proj.is_cuda:
+        return cuda_ops().gdn_scan_history(proj, batch.cu_seqlens_q, batch.state_slots, conv_w, a_log, dt_bias,
+                                           norm_w, rec_pool, conv_pool, hk, hv, eps, True, rows, hist_rec,
+                                           hist_conv, None, None, None)
+    out = torch.empty(proj.shape[0], hv * dv, dtype=proj.dtype, device=proj.device)
+    cu = batch.cu_seqlens_host
+    rows_h = rows.tolist()
+    for i, slot in enumerate(batch.slots_host):
+        s, e = cu[i], cu[i + 1]
+        if e == s:
+            continue
+        marks = [t - s for t in range(s, e) if rows_h[t] >= 0]
+        y, rec, conv, rh, ch, _ = ref.gdn_sequence(proj[s:e], conv_w, a_log, dt_bias, norm_w, rec_pool[slot],
+                                                   conv_pool[slot], hk=hk, hv=hv, dk=dk, dv=dv, eps=eps,
+                                                   history_at=marks)
+        out[s:e] = y
+        rec_pool[slot] = rec
+        conv_pool[slot] = conv
+        for local, r_state, c_state in zip(marks, rh, ch):
+            hist_rec[rows_h[s + local]] = r_state
+            hist_conv[rows_h[s + local]] = c_state
+    return out
+
+
 def lm_head_sample(hidden: torch.Tensor, weight: torch.Tensor, temperatures: torch.Tensor, rng: torch.Tensor,
                    vocab_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
     """LM-head GEMM fused with greedy / Gumbel-max selection over this rank's vocab slice.

@@ -31,7 +31,8 @@ class ForwardBatch:
     cu_seqlens_host: list[int] = field(default_factory=list)
     slots_host: list[int] = field(default_factory=list)
     num_seqs: int = 0
-    # GDN state capture for checkpoints / MTP verify: (seq, token offset) -> buffer row
+    # GDN states after selected tokens (hybrid prefix checkpoints inside a prefill chunk):
+    # {"rows": [T] int32 (-1 = none), "rec": per-layer [R, Hv, Dk, Dv] fp32, "conv": per-layer [R, C, K-1]}
     gdn_history: dict | None = None
     # MTP verify: per GDN layer (rec_k, rec_delta, rec_g, conv_hist) record buffers; the
     # slot pools are then left untouched (see ops.gdn_verify)
