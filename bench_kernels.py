@@ -150,6 +150,45 @@ def cases(b: int) -> dict:
         return fns, kv_bytes + q.numel() * 2 * 2, 4 * b * 8 * ctx * 256
     out["attention_decode"] = attention
 
+    def attention_prefill():
+        # tensor-core causal prefill: 4 sequences x 2048 new tokens, 8 q / 2 kv heads, hd 256
+        nseq, n = 4, 2048
+        t = nseq * n
+        q = (torch.randn(t, 8, 256, device=dev) * 0.5).to(bf)
+        gate = torch.randn(t, 8 * 256, device=dev).to(bf)
+        pages = n // 256
+        kc = torch.randn(nseq * pages, 2, 256, 256, device=dev).to(bf)
+        vc = torch.randn(nseq * pages, 2, 256, 256, device=dev).to(bf)
+        bt = torch.arange(nseq * pages, device=dev, dtype=torch.int32).view(nseq, pages)
+        cu = torch.arange(nseq + 1, device=dev, dtype=torch.int32) * n
+        cl = torch.full((nseq,), n, device=dev, dtype=torch.int32)
+        flops = 4 * nseq * 8 * 256 * (n * (n + 1) // 2)
+        fn = lambda: torch.ops.isb.attention_prefill_tc(q, gate, kc, vc, cu, cl, bt, 0.0625, True, n)  # noqa: E731
+        return [fn], (q.numel() * 2 * 3 + kc.numel() * 4), flops
+    out["attention_prefill_tc"] = attention_prefill
+
+    def gdn_chunked():
+        # chunked GDN prefill: one 8192-token sequence, 16 key / 16 value heads
+        hk = hv = 16
+        d = 128
+        n = 8192
+        c = 2 * hk * d + hv * d
+        p = c + hv * d + 2 * hv
+        proj = torch.randn(n, p, device=dev).to(bf)
+        conv_w = (torch.randn(c, 4, device=dev) * 0.5).to(bf)
+        a_log, dt = torch.zeros(hv, device=dev), torch.ones(hv, device=dev)
+        nw = torch.ones(d, device=dev).to(bf)
+        slots = torch.zeros(1, device=dev, dtype=torch.int32)
+        rec = torch.zeros(2, hv, d, d, device=dev)
+        conv = torch.zeros(2, c, 3, device=dev).to(bf)
+        nc = n // 64
+        info = torch.tensor([0] * nc + list(range(0, n, 64)) + [64] * nc + [0, nc], dtype=torch.int32, device=dev)
+        cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        fn = lambda: torch.ops.isb.gdn_prefill_chunked(proj, cu, slots, info, nc, conv_w, a_log, dt, nw, rec,  # noqa
+                                                       conv, hk, hv, 1e-6)
+        return [fn], proj.numel() * 2 + n * hv * d * 2, 0
+    out["gdn_prefill_chunked"] = gdn_chunked
+
     def acc_norm():
         resid = torch.randn(b, 1024, device=dev).to(bf)
         nwh = torch.zeros(1024, device=dev).to(bf)

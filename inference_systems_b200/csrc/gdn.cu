@@ -87,6 +87,10 @@ __device__ __forceinline__ float take(const TIn* row, int idx, bool consume) {
 template <typename TIn>
 __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
   pdl_trigger();
+  // Nothing is read before the wait: the state pools are also written by plainly launched
+  // kernels (slot zeroing on allocation, checkpoint restore, MTP commit), and a dependent
+  // launch may start before such a kernel's writes are visible.
+  pdl_wait();
   __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
   __shared__ float red_k[8][D], red_q[8][D];
   __shared__ float scal[16];
@@ -125,16 +129,6 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     float4 st[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
-    if (j == 0) {
-      // Everything read so far (this layer's state/conv pools, weights, step
-      // metadata) is written by no kernel of the same dependent-launch chain:
-      // the pools only by this layer's scan of an earlier step (an earlier
-      // graph launch or forward call) or by plainly launched commit / restore
-      // kernels, which start only after all earlier work has finished.  So these
-      // loads overlap the kernels still in flight; the projection rows are read
-      // only after the previous kernel has completed.
-      pdl_wait();
-    }
 
     for (int t = t0; t < t1; ++t) {
       const TIn* x = static_cast<const TIn*>(a.proj) + size_t(t) * a.proj_stride;

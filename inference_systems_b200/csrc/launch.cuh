@@ -7,11 +7,10 @@
 // before it reads anything an earlier kernel produced or writes anything an
 // earlier kernel reads. pdl_wait() returns only after the previous kernel has
 // completed, and that kernel completed only after its own wait returned, so the
-// ordering is transitive. Because several kernels of a chain can be in flight
-// at once, code before pdl_wait() reads only data that no PDL-launched kernel
-// of the chain writes: weights, and a GDN layer's state pools (written by that
-// layer's scan in an earlier step, or by plainly launched kernels, which start
-// only after all earlier work has finished).
+// ordering is transitive. Several kernels of a chain can be in flight at once,
+// and a dependent may also start before a plainly launched predecessor's writes
+// are visible, so code before pdl_wait() reads only data no kernel ever writes
+// (the weights).
 // ISB_PDL=0 in the environment launches everything with plain stream order.
 #pragma once
 

@@ -1,5 +1,9 @@
 """Hybrid prefix cache on the sm_100a path: checkpoint capture (including internal
-checkpoints recorded by the scan kernel's history mode) and restore."""
+checkpoints recorded by the scan kernel's history mode) and restore.
+
+Run back to back, these also catch a kernel that reads a reallocated state slot
+before the slot's zeroing is visible (the cache-less reference run would then
+depend on timing)."""
 
 import os
 
@@ -16,7 +20,9 @@ pytestmark = pytest.mark.gpu
 @pytest.fixture(scope="module")
 def ckpt(tmp_path_factory):
     cfg = preset("tiny_hd")
-    sd = random_state_dict(cfg, seed=0, std=0.05)
+    # std 0.25: logit margins large enough that bf16 rounding differences between chunkings
+    # (cached prefix + short prefill vs one long prefill) do not flip greedy tokens
+    sd = random_state_dict(cfg, seed=0, std=0.25)
     d = str(tmp_path_factory.mktemp("tiny_hd_hpc"))
     write_config(d, cfg)
     save_file({k: v.contiguous() for k, v in sd.items()}, os.path.join(d, "model.safetensors"))

@@ -193,6 +193,42 @@ def test_gdn_prefill_chunked_matches_scan_and_oracle(lens, hk, hv):
     assert torch.equal(conv_k.cpu(), conv_c)
 
 
+@pytest.mark.parametrize("lens,hk,hv,marks", [([300, 40], 16, 16, [[99, 255], [9]]), ([130], 2, 4, [[0, 64, 129]])])
+def test_gdn_scan_history_states_match_oracle(lens, hk, hv, marks):
+    b, t = len(lens), sum(lens)
+    proj, conv_w, a_log, dt_bias, norm_w, rec, conv, slots = _gdn_inputs(b, hk, hv, 7 * t, t=t)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    rows = [-1] * t
+    k = 0
+    for i, ms in enumerate(marks):
+        for m in ms:
+            rows[cu[i] + m] = k
+            k += 1
+    hist_rec_r, hist_conv_r = [None] * k, [None] * k
+    rec_c, conv_c = rec.clone(), conv.clone()
+    for i in range(b):
+        _, r_fin, c_fin, rh, ch, _ = ref.gdn_sequence(proj[cu[i]:cu[i + 1]], conv_w, a_log, dt_bias, norm_w,
+                                                      rec_c[slots[i]], conv_c[slots[i]], hk=hk, hv=hv, dk=128, dv=128,
+                                                      eps=1e-6, history_at=marks[i])
+        for m, rs_, cs_ in zip(marks[i], rh, ch):
+            hist_rec_r[rows[cu[i] + m]] = rs_
+            hist_conv_r[rows[cu[i] + m]] = cs_
+    c = 2 * hk * 128 + hv * 128
+    hist_rec = torch.zeros(k, hv, 128, 128, device=DEV)
+    hist_conv = torch.zeros(k, c, 3, device=DEV, dtype=torch.bfloat16)
+    rec_g, conv_g = rec.to(DEV), conv.to(DEV)
+    torch.ops.isb.gdn_scan_history(proj.to(DEV), torch.tensor(cu, dtype=torch.int32, device=DEV), slots.to(DEV),
+                                   conv_w.to(DEV), a_log.to(DEV), dt_bias.to(DEV), norm_w.to(DEV), rec_g, conv_g,
+                                   hk, hv, 1e-6, True, torch.tensor(rows, dtype=torch.int32, device=DEV), hist_rec,
+                                   hist_conv, None, None, None)
+    torch.cuda.synchronize()
+    for j in range(k):
+        assert _rel(hist_rec[j].cpu(), hist_rec_r[j]) < 1e-3, j
+        assert torch.equal(hist_conv[j].cpu(), hist_conv_r[j].to(torch.bfloat16)), j
+
+
 def gate_ref(qkv, hq, hd):
     t = qkv.shape[0]
     return qkv[:, : hq * hd * 2].reshape(t, hq, 2 * hd)[..., hd:].reshape(t, hq * hd)
