@@ -1,6 +1,7 @@
 """Per-kernel microbenchmarks of the sm_100a ops at Qwen3.5-0.8B decode shapes.
 
     python bench_kernels.py [--batch 128] [--only gemm] [--json out.json] [--once]
+    python -m torch.distributed.run --nproc-per-node N ... bench_kernels.py --tp   (fused TP paths)
 
 Method: every case builds R independent argument sets whose large operands
 (weights, GDN state pool, KV cache) together exceed 2 x the 126 MB L2, captures
@@ -198,7 +199,99 @@ def cases(b: int) -> dict:
     return out
 
 
+def tp_bench(batches=(1, 8, 128)) -> None:
+    """Fused tensor-parallel paths vs the NCCL baseline; run under torch.distributed.run.
+
+    Row-parallel down projection (hidden 1024, intermediate 3584 / TP) fused with the
+    all-reduce, residual add and RMSNorm; vocab-parallel LM head fused with the
+    cross-rank argmax.  Device time per call inside a CUDA graph (20 calls per graph,
+    5 replays), max over ranks.  Roofline = max(FLOPs / measured bf16 peak, bytes
+    this rank must pull over NVLink / 770 GB/s, bytes read from HBM / measured HBM).
+    """
+    import torch.distributed as dist
+
+    from inference_systems_b200.parallel.comm import TPComm
+
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", init_method="env://")
+    hbm, tflops, src = peaks()
+    nvlink = 770.0
+    h, inter, vocab = 1024, 3584 // world, 248320 // world
+    comm = TPComm(dev, rank, world, h, None, max_rows=256)
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(rank)
+    w = (torch.randn(h, inter, device=dev, generator=g) * 0.02).to(bf)
+    nw = torch.zeros(h, device=dev).to(bf)
+    lm = (torch.randn(vocab, h, device=dev, generator=g) * 0.02).to(bf)
+    rows = []
+
+    def timed(fn, calls=20):
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(calls):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for _ in range(calls):
+                fn()
+        gr.replay()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(5):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) * 1e3 / (5 * calls)], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del gr
+        return float(t.item())
+
+    for b in batches:
+        x = (torch.randn(b, inter, device=dev, generator=g)).to(bf)
+        res = torch.randn(b, h, device=dev, generator=g).to(bf)
+        fused = timed(lambda: comm.row_parallel_residual_norm(x, w, res, nw, 1e-6, True))
+
+        def nccl_path():
+            y = ops.linear(x, w)
+            dist.all_reduce(y)
+            return ops.add_rmsnorm(y, res, nw, 1e-6, True)
+
+        base = timed(nccl_path)
+        flops = 2 * b * inter * h
+        link = (world - 1) * b * h * 4 / (nvlink * 1e9) * 1e6
+        roof = max(flops / (tflops * 1e12) * 1e6, link, (h * inter * 2) / (hbm * 1e9) * 1e6)
+        rows.append({"path": "row-parallel GEMM -> all-reduce -> residual + RMSNorm", "tp": world, "batch": b,
+                     "fused_us": round(fused, 2), "nccl_baseline_us": round(base, 2),
+                     "roofline_us": round(roof, 2), "fraction_of_roofline": round(roof / fused, 3)})
+        hid = torch.randn(b, h, device=dev, generator=g).to(bf)
+        temps = torch.zeros(b, device=dev)
+        rng = torch.zeros(2, dtype=torch.int32, device=dev)
+        fused = timed(lambda: comm.lm_head_sample(hid, lm, temps, rng, rank * vocab), calls=4)
+        roof = max(2 * b * vocab * h / (tflops * 1e12) * 1e6, vocab * h * 2 / (hbm * 1e9) * 1e6,
+                   (world - 1) * b * 8 / (nvlink * 1e9) * 1e6)
+        rows.append({"path": "vocab-parallel LM head -> cross-rank argmax", "tp": world, "batch": b,
+                     "fused_us": round(fused, 2), "roofline_us": round(roof, 2),
+                     "fraction_of_roofline": round(roof / fused, 3)})
+    if rank == 0:
+        for r in rows:
+            print(json.dumps(r), flush=True)
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main():
+    if "--tp" in sys.argv:
+        load_extension()
+        tp_bench()
+        return
     ap = argparse.ArgumentParser()
     ap.add_argument("--batch", type=int, default=128)
     ap.add_argument("--only", default=None)
