@@ -527,6 +527,222 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (dbg && threadIdx.x == 0) dbg[7] = globaltimer_ns();
 }
 
+// Persistent LM head (swap-AB: vocabulary rows are the 128-row MMA side, the <= 128 tokens the
+// N side): one CTA per SM walks vocabulary tiles with a stride of gridDim.x.  Two TMEM
+// accumulators alternate, so while the epilogue warps reduce tile i to per-token
+// (max, argmax) through shared memory, the producer and MMA warps already stream and multiply
+// tile i+1.  The per-tile results go to the same [tiles][tokens] partials as the one-tile-per-CTA
+// path and the same second-stage kernel finishes the selection.
+ISB_DEVICE void named_bar_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+static int num_sms();
+
+template <int BN>
+struct LmCfg {
+  static constexpr int CH = BN < 32 ? 16 : 32;  // score columns staged and scanned at a time
+  static constexpr int P_BYTES = BM * BK * 2;
+  static constexpr int Q_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = P_BYTES + Q_BYTES;
+  static constexpr int SC_BYTES = 2 * BM * (CH + 1) * 4;  // one staging slice per epilogue warpgroup
+  static constexpr int STAGES = (220 * 1024 - SC_BYTES - BN * 4) / STAGE_BYTES < 8
+                                    ? (220 * 1024 - SC_BYTES - BN * 4) / STAGE_BYTES : 8;
+  static constexpr int ACC_COLS = BN < 32 ? 32 : BN;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS < 64 ? 64 : 2 * ACC_COLS;
+  static constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + SC_BYTES + BN * 4 + 256;
+};
+
+constexpr int kLmThreads = 320;  // producer warp, MMA warp, two epilogue warpgroups
+
+template <int BN>
+__global__ void __launch_bounds__(kLmThreads, 1)
+    lm_head_persistent_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
+                              GemmArgs args, int ntiles) {
+  using Cfg = LmCfg<BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* sc_all = reinterpret_cast<float*>(smem + Cfg::STAGES * Cfg::STAGE_BYTES);  // [2][BM][CH + 1]
+  float* temp_s = sc_all + 2 * BM * (Cfg::CH + 1);                                 // [BN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(temp_s + BN);
+  uint64_t* empty = full + Cfg::STAGES;
+  uint64_t* acc_full = empty + Cfg::STAGES;   // [2]
+  uint64_t* acc_empty = acc_full + 2;         // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb_total = (args.K + BK - 1) / BK;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < Cfg::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 256);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmP);
+    prefetch_tmap(&tmQ);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;
+      for (int lt = 0; lt < my_tiles; ++lt) {
+        const int tile = blockIdx.x + lt * gridDim.x;
+        for (int kb = 0; kb < kb_total; ++kb, ++i) {
+          const int s = i % Cfg::STAGES;
+          if (i >= Cfg::STAGES && !mbar_wait(&empty[s], ((i / Cfg::STAGES) & 1) ^ 1)) {
+            atomicOr(&g_gemm_err, 16u);
+            lt = my_tiles;
+            break;
+          }
+          uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          tma_load_2d(sp, &tmP, &full[s], kb * BK, tile * BM);
+          tma_load_2d(sp + Cfg::P_BYTES, &tmQ, &full[s], kb * BK, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+      int i = 0;
+      bool ok = true;
+      for (int lt = 0; ok && lt < my_tiles; ++lt) {
+        const int buf = lt & 1;
+        if (lt >= 2 && !mbar_wait(&acc_empty[buf], ((lt >> 1) - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * Cfg::ACC_COLS;
+        for (int kb = 0; kb < kb_total; ++kb, ++i) {
+          const int s = i % Cfg::STAGES;
+          if (!mbar_wait(&full[s], (i / Cfg::STAGES) & 1)) { ok = false; break; }
+          tc_fence_after();
+          uint8_t* sp = smem + s * Cfg::STAGE_BYTES;
+          const uint64_t pd = smem_desc_sw128(sp), qd = smem_desc_sw128(sp + Cfg::P_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) mma_bf16(acc, pd + 2 * k, qd + 2 * k, idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit(&empty[s]);
+        }
+        mma_commit(&acc_full[buf]);
+      }
+      if (!ok) atomicOr(&g_gemm_err, 32u);
+    }
+  } else {
+    // ---- epilogue: warpgroups of warps 2..5 and 6..9; TMEM lane quarter = warp % 4; warpgroup eh
+    // owns the column chunks c with c % 2 == eh
+    const int eh = (warp - 2) >> 2;
+    const int et = (threadIdx.x - 64) & 127;  // thread index inside the warpgroup
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;      // vocabulary row within the tile == TMEM lane
+    const uint32_t lane_addr = uint32_t(quarter * 32) << 16;
+    constexpr int CH = Cfg::CH;
+    constexpr int NCH = BN / CH;
+    float* sc_s = sc_all + eh * BM * (CH + 1);
+    const int seed = args.rng[0], step = args.rng[1];
+    for (int j = threadIdx.x - 64; j < BN; j += 256) temp_s[j] = j < args.Q_rows ? args.temps[j] : 0.f;
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+    bool ok = true;
+    for (int lt = 0; lt < my_tiles; ++lt) {
+      const int tile = blockIdx.x + lt * gridDim.x;
+      const int buf = lt & 1;
+      if (!mbar_wait(&acc_full[buf], (lt >> 1) & 1)) ok = false;
+      tc_fence_after();
+      const int vrow = tile * BM + row;
+      const bool valid = ok && vrow < args.P_rows;
+      const int my_last = NCH - 1 - ((NCH - 1 - eh) & 1);  // last chunk of this warpgroup (may be < 0)
+      if (my_last < 0) {
+        tc_fence_before();
+        mbar_arrive(&acc_empty[buf]);
+      }
+#pragma unroll 1
+      for (int c = eh; c < NCH; c += 2) {
+        float v[CH];
+        const uint32_t taddr = tmem + buf * Cfg::ACC_COLS + lane_addr + c * CH;
+        if constexpr (CH == 16) tmem_ld16(taddr, v); else tmem_ld32(taddr, v);
+        if (c == my_last) {
+          tc_fence_before();
+          mbar_arrive(&acc_empty[buf]);  // this warpgroup has read all its columns of the accumulator
+        }
+#pragma unroll
+        for (int x = 0; x < CH; ++x) {
+          const int col = c * CH + x;
+          float sc = valid ? v[x] : -INFINITY;
+          const float temp = temp_s[col];
+          if (valid && temp > 1e-10f) sc = sc / temp + gumbel_noise(seed, step, col, args.vocab_offset + vrow);
+          sc_s[row * (CH + 1) + x] = sc;
+        }
+        named_bar_sync(2 + eh, 128);
+        // CH columns, 128 / CH threads per column, each scanning a slice of the rows
+        constexpr int TPC = 128 / CH, RPT = BM / TPC;
+        const int x = et % CH, part = et / CH;
+        float best = -INFINITY;
+        int bi = 0;
+        for (int r = part * RPT; r < (part + 1) * RPT; ++r) {
+          const float y = sc_s[r * (CH + 1) + x];
+          if (y > best) { best = y; bi = r; }
+        }
+#pragma unroll
+        for (int o = CH; o < 32; o <<= 1) {  // combine the row slices held by lanes CH, 2CH, .. apart
+          const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+          const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+          if (ob > best || (ob == best && oi < bi)) { best = ob; bi = oi; }
+        }
+        float* red_v = reinterpret_cast<float*>(sc_s);  // reuse after the scan: [4 warps][CH]
+        named_bar_sync(2 + eh, 128);
+        if ((et & 31) < CH) {
+          red_v[(et >> 5) * CH + x] = best;
+          reinterpret_cast<int*>(red_v + 4 * CH)[(et >> 5) * CH + x] = bi;
+        }
+        named_bar_sync(2 + eh, 128);
+        if (et < CH) {
+          float b2 = red_v[x];
+          int i2 = reinterpret_cast<int*>(red_v + 4 * CH)[x];
+          for (int w = 1; w < 4; ++w) {
+            const float ob = red_v[w * CH + x];
+            const int oi = reinterpret_cast<int*>(red_v + 4 * CH)[w * CH + x];
+            if (ob > b2 || (ob == b2 && oi < i2)) { b2 = ob; i2 = oi; }
+          }
+          const int col = c * CH + x;
+          if (col < args.Q_rows) {
+            args.part_val[size_t(tile) * args.Q_rows + col] = b2;
+            args.part_idx[size_t(tile) * args.Q_rows + col] = tile * BM + i2;
+          }
+        }
+        named_bar_sync(2 + eh, 128);  // sc_s is rewritten by the next chunk / tile
+      }
+    }
+    if (!ok) atomicOr(&g_gemm_err, 64u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, Cfg::TMEM_COLS);
+}
+
+template <int BN>
+static void launch_lm_persistent(const CUtensorMap& tp, const CUtensorMap& tq, const GemmArgs& a, int tiles,
+                                 cudaStream_t st) {
+  using Cfg = LmCfg<BN>;
+  auto kern = lm_head_persistent_kernel<BN>;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess,
+                "persistent LM head smem attribute");
+    attr = true;
+  }
+  const int grid = std::min(tiles, num_sms());
+  launch_pdl(kern, dim3(grid), dim3(kLmThreads), Cfg::SMEM, st, tp, tq, a, tiles);
+}
+
 // Second stage of the fused LM-head selection: best (score, index) over vocab tiles.
 __global__ void argmax_tiles_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int ntiles, int tokens,
                                     int vocab_offset, float* __restrict__ out_val, int* __restrict__ out_idx) {
@@ -872,6 +1088,14 @@ at::Tensor gemm_timeline(const at::Tensor& a_in, const at::Tensor& b, int64_t sp
   return ts;
 }
 
+static bool lm_persistent_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ISB_LM_PERSISTENT");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const at::Tensor& w, const at::Tensor& temps,
                                                   const at::Tensor& rng, int64_t vocab_offset) {
   at::Tensor h = h_in.contiguous();
@@ -894,7 +1118,15 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h_in, const 
   args.part_idx = pi.data_ptr<int>();
   args.vocab_offset = int(vocab_offset);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (p.swap) {
+  if (p.swap && p.tiles_q == 1 && lm_persistent_enabled()) {
+    args.P_rows = V; args.Q_rows = B;
+    switch (p.bn) {
+      case 16: launch_lm_persistent<16>(p.tp, p.tq, args, p.tiles_p, st); break;
+      case 32: launch_lm_persistent<32>(p.tp, p.tq, args, p.tiles_p, st); break;
+      case 64: launch_lm_persistent<64>(p.tp, p.tq, args, p.tiles_p, st); break;
+      default: launch_lm_persistent<128>(p.tp, p.tq, args, p.tiles_p, st); break;
+    }
+  } else if (p.swap) {
     args.P_rows = V; args.Q_rows = B;
     dispatch_bn<kArgmax, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
   } else {
