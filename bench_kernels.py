@@ -79,14 +79,20 @@ def cases(b: int) -> dict:
     dev, bf = "cuda", torch.bfloat16
     out = {}
 
-    def gemm_case(name, n, k, mode):
+    def gemm_case(name, n, k, mode, splits=0):
         def build():
             wbytes = n * k * 2
             r = replicas(wbytes)
             a = torch.randn(b, k, device=dev).to(bf)
             ws = [(torch.randn(n, k, device=dev) * 0.02).to(bf) for _ in range(r)]
             acc = torch.zeros(b, n, device=dev)
-            if mode == "silu":
+            if mode == "silu" and splits:
+                fns = [lambda w=w: torch.ops.isb.gemm(a, w, 1, splits) for w in ws]
+                ob = b * n // 2 * 2
+            elif mode == "store" and splits:
+                fns = [lambda w=w: torch.ops.isb.gemm(a, w, 0, splits) for w in ws]
+                ob = b * n * 2
+            elif mode == "silu":
                 fns = [lambda w=w: ops.linear_silu_mul(a, w) for w in ws]
                 ob = b * n // 2 * 2
             elif mode == "acc":
@@ -104,6 +110,9 @@ def cases(b: int) -> dict:
     gemm_case("gemm_out_proj_accum", 1024, 2048, "acc")
     gemm_case("gemm_down_accum", 1024, 3584, "acc")
     gemm_case("gemm_out_proj_store", 1024, 2048, "store")
+    for sp in (2, 4):  # split-K variants of the column-parallel GEMMs (workspace reduction)
+        gemm_case(f"gemm_gdn_in_proj_split{sp}", 8224 + 32, 1024, "store", sp)
+        gemm_case(f"gemm_gate_up_silu_split{sp}", 7168, 1024, "silu", sp)
 
     def lm_head():
         v = 248320

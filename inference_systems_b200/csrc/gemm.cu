@@ -142,7 +142,7 @@ ISB_DEVICE float gumbel_noise(int seed, int step, int row, int col) {
   return -logf(-logf(u));
 }
 
-template <int BN, bool SWAP, int EPI>
+template <int BN, bool SWAP, int EPI, bool CL = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmP, const __grid_constant__ CUtensorMap tmQ,
                    const __grid_constant__ CUtensorMap tmO, GemmArgs args) {
@@ -254,7 +254,81 @@ __global__ void __launch_bounds__(kThreads, 1)
   __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(smem + XBUF_BYTES);  // [BN][128] bf16
   __shared__ int s_last;
 
-  if (epi) {
+  if constexpr (CL) {
+    // ---- split-K pair in a 2-CTA cluster (swap-AB store / SiLU*mul): each CTA of the pair
+    // multiplied half of K; both park their fp32 partial rows in their own shared memory, then
+    // CTA r sums its own and its peer's partials (DSMEM loads) for token columns
+    // [r*BN/2, (r+1)*BN/2) and runs the epilogue for that half.  The peer's partials stay
+    // alive until the second cluster barrier.
+    static_assert(SWAP && (EPI == kStore || EPI == kSiluMul), "cluster split-K serves swap-AB store / SiLU*mul");
+    constexpr int PSTR = BN + 4;
+    constexpr int HALF = BN / 2;
+    constexpr int OST_BYTES = ((BN * BM * 2) + 1023) / 1024 * 1024;
+    float* pbuf = reinterpret_cast<float*>(smem + XBUF_BYTES + OST_BYTES);  // [BM][PSTR]
+    static_assert(XBUF_BYTES + OST_BYTES + BM * PSTR * 4 <= Cfg::STAGES * Cfg::STAGE_BYTES,
+                  "cluster split-K staging must fit in the stage buffers");
+    if (epi) {
+      pdl_wait();
+      const bool acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
+      if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 8u);
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BN / CH; ++c) {
+        float v[CH];
+        if (acc_ok) {
+          if constexpr (CH == 16) tmem_ld16(lane_addr + c * CH, v); else tmem_ld32(lane_addr + c * CH, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < CH; j += 4)
+          *reinterpret_cast<float4*>(pbuf + row * PSTR + c * CH + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      }
+    }
+    cluster_sync();
+    if (epi) {
+      const uint32_t me = cluster_ctarank();
+      const int cbase = int(me) * HALF;
+      const uint32_t peer_row = mapa_shared(smem_u32(pbuf + row * PSTR + cbase), me ^ 1u);
+#pragma unroll 4
+      for (int j = 0; j < HALF; j += 4) {
+        const float4 a4 = *reinterpret_cast<const float4*>(pbuf + row * PSTR + cbase + j);
+        const float4 b4 = ld_dsmem_f4(peer_row + j * 4);
+        const float sum[4] = {a4.x + b4.x, a4.y + b4.y, a4.z + b4.z, a4.w + b4.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          if constexpr (EPI == kStore) {
+            ostage[(j + e) * BM + row] = __float2bfloat16(sum[e]);
+          } else {
+            if (row >= 64) xbuf[(row - 64) * Cfg::RED_STRIDE + j + e] = sum[e];
+            else pbuf[row * PSTR + cbase + j + e] = sum[e];  // keep the gate sum in place
+          }
+        }
+      }
+      if constexpr (EPI == kSiluMul) {
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (row < 64) {
+          for (int j = 0; j < HALF; ++j)
+            ostage[j * 64 + row] =
+                __float2bfloat16(silu(pbuf[row * PSTR + cbase + j]) * xbuf[row * Cfg::RED_STRIDE + j]);
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const int x0 = EPI == kSiluMul ? tile_p * 64 : tile_p * BM;
+        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                         reinterpret_cast<uint64_t>(&tmO)),
+                     "r"(x0), "r"(tile_q * BN + cbase), "r"(smem_u32(ostage))
+                     : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+        asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      }
+    }
+    cluster_sync();  // the peer has finished reading this CTA's partials
+  }
+  if (epi && !CL) {
     pdl_wait();  // outputs / accumulators / split-K scratch may still be in use by the previous kernel
     bool acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
     if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 4u);
@@ -813,6 +887,30 @@ CUtensorMap make_kmajor_map(const void* ptr, int64_t rows, int64_t K, int box_ro
   return m;
 }
 
+// Cluster split-K pair (swap-AB store / SiLU*mul): grid (tiles_p, tiles_q, 2), cluster (1, 1, 2).
+template <int BN, int EPI>
+static void launch_gemm_pair(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& to, GemmArgs a,
+                             int tiles_p, int tiles_q, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, true, EPI, true>;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess);
+    attr = true;
+  }
+  launch_pdl_cluster(kern, dim3(tiles_p, tiles_q, 2), dim3(kThreads), Cfg::SMEM, stream, dim3(1, 1, 2), tp, tq, to, a);
+  const cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, "gemm (cluster pair) launch failed: ", cudaGetErrorString(e));
+}
+
+static bool gemm_pair_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ISB_GEMM_PAIR");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
 template <int BN, bool SWAP, int EPI>
 static void launch_gemm(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& to, GemmArgs a, int tiles_p,
                         int tiles_q, int splits, cudaStream_t stream) {
@@ -940,6 +1038,16 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
   const int M = a.size(0), N = b.size(0);
   const int out_cols = out.size(1);
   Plan p = plan_gemm(a, b, false, force_splits);
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  // two CTAs per weight tile (split K over a cluster pair) when the doubled grid still fits in a
+  // wave and the token tile is narrow (measured: a win up to 32 tokens, a loss at 128, where
+  // exchanging the 64 KB partial tile costs more than halving each CTA's weight stream saves)
+  const bool pair = p.swap && force_splits == 0 && gemm_pair_enabled() && kb_total >= 4 && p.bn <= 32 &&
+                    p.tiles_p * p.tiles_q * 2 <= num_sms();
+  if (pair) {
+    p.kb_per = (kb_total + 1) / 2;
+    p.splits = 2;
+  }
   GemmArgs args = {};
   args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   args.K = a.size(1);
@@ -948,7 +1056,7 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
   args.dbg = dbg;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   at::Tensor ws;
-  if (p.splits > 1) {
+  if (p.splits > 1 && !pair) {
     ws = at::empty({int64_t(p.tiles_p) * p.tiles_q * p.splits * BM * p.bn}, a.options().dtype(at::kFloat));
     args.ws = ws.data_ptr<float>();
     args.counters = counter_slot();
@@ -956,9 +1064,21 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
   CUtensorMap to = p.tp;
   if (p.swap) {
     TORCH_CHECK(out_cols % 8 == 0, "swap-AB GEMM output width must be a multiple of 8 (16-byte rows)");
-    to = make_store_map(out.data_ptr(), M, out_cols, epilogue == kSiluMul ? 64 : BM, p.bn);
+    to = make_store_map(out.data_ptr(), M, out_cols, epilogue == kSiluMul ? 64 : BM, pair ? p.bn / 2 : p.bn);
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (pair) {
+    if (epilogue == kSiluMul) TORCH_CHECK(N % 128 == 0, "packed gate/up rows must be a multiple of 128");
+#define ISB_PAIR(BN_)                                                                                   \
+  if (p.bn == BN_) {                                                                                    \
+    if (epilogue == kStore) launch_gemm_pair<BN_, kStore>(p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, st); \
+    else launch_gemm_pair<BN_, kSiluMul>(p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, st);                   \
+    return;                                                                                             \
+  }
+    ISB_PAIR(16) ISB_PAIR(32) ISB_PAIR(64) ISB_PAIR(128)
+#undef ISB_PAIR
+    TORCH_CHECK(false, "unsupported tile width");
+  }
   if (epilogue == kStore) {
     if (p.swap) dispatch_bn<kStore, true>(p.bn, p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
     else launch_gemm<256, false, kStore>(p.tp, p.tq, to, args, p.tiles_p, p.tiles_q, p.splits, st);
