@@ -470,6 +470,41 @@ std::tuple<at::Tensor, at::Tensor> attn_prepare(const at::Tensor& qkv, const at:
   return {q, gate};
 }
 
+bool attention_decode_tc_supported(int64_t hd, int64_t hq, int64_t hkv);
+void attention_decode_tc_partials(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc,
+                                  const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale,
+                                  at::Tensor& part_o, at::Tensor& part_ml, int max_chunks);
+
+// ISB_ATTN_DECODE_TC: 0 = split-KV SIMT kernel only, 1 = tensor-core kernel whenever the head
+// layout allows, unset = tensor cores from 16 (sequence, KV head) pairs up.
+int attn_decode_tc_mode() {
+  static const int mode = [] {
+    const char* e = std::getenv("ISB_ATTN_DECODE_TC");
+    return e ? std::atoi(e) : 2;
+  }();
+  return mode;
+}
+
+// Tensor-core split-KV decode (128-key chunks) followed by the combine kernel.
+at::Tensor attention_decode_tc(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
+                               const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated) {
+  const int B = q.size(0), Hq = q.size(1), hd = q.size(2);
+  check_cache(kc, vc, hd);
+  TORCH_CHECK(ctx_lens.scalar_type() == at::kInt && block_tables.scalar_type() == at::kInt, "int32 metadata");
+  at::Tensor out = at::empty({B, Hq * hd}, q.options());
+  if (B == 0) return out;
+  constexpr int TCHUNK = 128;
+  const int max_chunks = block_tables.size(1) * (PAGE / TCHUNK);
+  at::Tensor part_o = at::empty({B, Hq, max_chunks, hd}, q.options().dtype(at::kFloat));
+  at::Tensor part_ml = at::empty({B, Hq, max_chunks, 2}, q.options().dtype(at::kFloat));
+  attention_decode_tc_partials(q, kc, vc, ctx_lens, block_tables, scale, part_o, part_ml, max_chunks);
+  launch_pdl(attn_combine_kernel<256>, dim3(Hq, B), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             part_o.data_ptr<float>(), part_ml.data_ptr<float>(), max_chunks, TCHUNK, ctx_lens.data_ptr<int>(),
+             reinterpret_cast<const __nv_bfloat16*>(gate.data_ptr()), gated,
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), Hq);
+  return out;
+}
+
 at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                             const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated) {
   const int B = q.size(0), Hq = q.size(1), hd = q.size(2);
@@ -479,6 +514,9 @@ at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const a
   const int Hkv = kc.size(1);
   const int G = Hq / Hkv;
   const int max_blocks = block_tables.size(1);
+  const int tc_mode = attn_decode_tc_mode();
+  if (tc_mode != 0 && attention_decode_tc_supported(hd, Hq, Hkv) && (tc_mode == 1 || B * Hkv >= 16))
+    return attention_decode_tc(q, gate, kc, vc, ctx_lens, block_tables, scale, gated);
   at::Tensor out = at::empty({B, Hq * hd}, q.options());
   if (B == 0) return out;
   const int max_chunks = max_blocks * (PAGE / DCHUNK);

@@ -297,6 +297,302 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+// ------------------------------------------------------------------ decode
+// Persistent split-KV decode: one CTA per SM walks work items (key chunk of 128 tokens,
+// sequence, KV head), chunk-major so the round-robin assignment spreads the non-empty
+// items evenly.  Per item, with the G query heads of the KV head as the N = 16 (zero-padded)
+// dimension:
+//   S^T = K Q^T        tcgen05.mma M=128 keys, N=16, K=256        -> TMEM (double-buffered)
+//   softmax            warps 2-5, one key per thread; per-head max / sum across the 4 warps
+//   O^T = V^T P^T      2 x tcgen05.mma M=128 dims, N=16, K=128 keys -> TMEM (double-buffered)
+// V is the A operand in MN-major form, read straight from its TMA tile (a 128-byte-swizzled
+// [keys][64 dims] box is exactly the canonical MN-major layout: dim blocks of 64 one box
+// (16 KB) apart, key groups of 8 one 1024-byte atom apart), so no transpose is needed.
+// K and V tiles (64 KB each) stream through a 3-slot TMA ring that runs across items.
+// The kernel writes unnormalised partials (o, max, sum) per (sequence, head, chunk); the
+// split-KV combine kernel merges them and applies the output gate.  Key rows past the
+// context inside the last tile are masked in the softmax, and their V rows are zeroed in
+// shared memory before the P V product (stale cache rows may hold any bit pattern).
+constexpr int DT = 128;                       // keys per tile (two tiles per page)
+constexpr int KV_TILE = DT * HD * 2;          // 64 KB: 4 boxes of [128 rows x 128 B]
+constexpr int NSLOT = 3;
+constexpr int QD_BYTES = 16 * HD * 2;         // 4 blocks of [16 rows x 128 B]
+constexpr int PD_BYTES = 16 * DT * 2;         // 2 blocks of [16 rows x 128 B]
+constexpr int DEC_BAR_BYTES = 512;
+constexpr int DEC_SMEM = NSLOT * KV_TILE + 2 * QD_BYTES + 2 * PD_BYTES + DEC_BAR_BYTES + 1024;
+constexpr uint32_t DEC_TMEM_COLS = 128;       // S [0,32) (2 x 16), O [32,96) (2 x 2 x 16)
+
+struct DecArgs {
+  const int* ctx_lens;
+  const int* block_tables;
+  int max_blocks;
+  int B, Hq, Hkv;
+  float scale_log2;
+  float* part_o;    // [B, Hq, max_chunks, HD]
+  float* part_ml;   // [B, Hq, max_chunks, 2]
+  int max_chunks;
+  int nitems;       // max_chunks * B * Hkv
+};
+
+// MN-major operand, 128-byte swizzle: 64-element blocks along M/N are ``lbo`` bytes apart,
+// groups of 8 rows along K are 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(const void* tile, uint32_t lbo) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= (1024ull >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+__device__ __forceinline__ void bar_sync_consumers() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int G>
+__global__ void __launch_bounds__(192, 1)
+    attn_decode_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, DecArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kv_s = smem;
+  uint8_t* q_s = kv_s + NSLOT * KV_TILE;
+  uint8_t* p_s = q_s + 2 * QD_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + 2 * PD_BYTES);
+  uint64_t* full = bars;        // [3] tile landed
+  uint64_t* slotfree = bars + 3;  // [3] tile consumed by its MMA
+  uint64_t* qfull = bars + 6;   // [2]
+  uint64_t* qfree = bars + 8;   // [2]
+  uint64_t* sfull = bars + 10;  // [2]
+  uint64_t* sfree = bars + 12;  // [2]
+  uint64_t* pfull = bars + 14;  // [2]
+  uint64_t* pfree = bars + 16;  // [2]
+  uint64_t* ofull = bars + 18;  // [2]
+  uint64_t* ofree = bars + 20;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 24);
+  float* red = reinterpret_cast<float*>(bars + 32);  // [2][4 warps][8 heads]
+
+  pdl_trigger();
+  pdl_wait();  // q and the new K/V rows come from the kernel right before
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Q and P rows >= G stay zero: TMA and the softmax write rows < G only
+  for (int i = threadIdx.x; i < (2 * QD_BYTES + 2 * PD_BYTES) / 16; i += blockDim.x)
+    reinterpret_cast<uint4*>(q_s)[i] = make_uint4(0u, 0u, 0u, 0u);
+  fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&slotfree[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&qfull[s], 1);
+      mbar_init(&qfree[s], 1);
+      mbar_init(&sfull[s], 1);
+      mbar_init(&sfree[s], 128);
+      mbar_init(&pfull[s], 128);
+      mbar_init(&pfree[s], 1);
+      mbar_init(&ofull[s], 1);
+      mbar_init(&ofree[s], 128);
+    }
+    fence_mbar_init();
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, DEC_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int BH = a.B * a.Hkv;
+  // item -> (sequence, KV head, chunk); false when the chunk starts past the context
+  auto item = [&](int it, int& b, int& kvh, int& chunk, int& n) -> bool {
+    chunk = it / BH;
+    const int rem = it - chunk * BH;
+    b = rem / a.Hkv;
+    kvh = rem - b * a.Hkv;
+    n = min(DT, a.ctx_lens[b] - chunk * DT);
+    return n > 0;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int L = 0, j = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; ok && it < a.nitems; it += gridDim.x) {
+        int b, kvh, chunk, n;
+        if (!item(it, b, kvh, chunk, n)) continue;
+        const int qb = j & 1;
+        if (j >= 2 && !mbar_wait(&qfree[qb], ((j >> 1) - 1) & 1)) { ok = false; break; }
+        mbar_arrive_expect_tx(&qfull[qb], G * HD * 2);
+        for (int c = 0; c < 4; ++c)
+          tma_load_2d(q_s + qb * QD_BYTES + c * 2048, &tmQ, &qfull[qb], c * 64, b * a.Hq + kvh * G);
+        const int key0 = chunk * DT;
+        const int row = (a.block_tables[size_t(b) * a.max_blocks + key0 / PAGE] * a.Hkv + kvh) * PAGE + key0 % PAGE;
+        for (int kv = 0; kv < 2; ++kv, ++L) {
+          const int s = L % NSLOT, u = L / NSLOT;
+          if (u >= 1 && !mbar_wait(&slotfree[s], (u - 1) & 1)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], KV_TILE);
+          const CUtensorMap* tm = kv ? &tmV : &tmK;
+          for (int c = 0; c < 4; ++c) tma_load_2d(kv_s + s * KV_TILE + c * (KV_TILE / 4), tm, &full[s], c * 64, row);
+        }
+        ++j;
+      }
+      if (!ok) atomicOr(&g_attn_tc_err, 0x10u);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_bf16_f32(128, 16);
+      constexpr uint32_t idO = idesc_bf16_f32(128, 16) | (1u << 15);  // A = V^T, MN-major
+      auto issue_s = [&](int j, int L) -> bool {
+        const int b2 = j & 1, s = L % NSLOT;
+        if (!mbar_wait(&qfull[b2], (j >> 1) & 1)) return false;
+        if (!mbar_wait(&full[s], (L / NSLOT) & 1)) return false;
+        if (j >= 2 && !mbar_wait(&sfree[b2], ((j >> 1) - 1) & 1)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int k = 0; k < HD / 16; ++k) {
+          const uint64_t ad = smem_desc_sw128(kv_s + s * KV_TILE + (k >> 2) * (KV_TILE / 4)) + 2 * (k & 3);
+          const uint64_t bd = smem_desc_sw128(q_s + b2 * QD_BYTES + (k >> 2) * 2048) + 2 * (k & 3);
+          mma_bf16(tmem + b2 * 16, ad, bd, idS, k > 0 ? 1u : 0u);
+        }
+        mma_commit(&sfull[b2]);
+        mma_commit(&slotfree[s]);
+        mma_commit(&qfree[b2]);
+        return true;
+      };
+      auto issue_pv = [&](int j, int L) -> bool {
+        const int b2 = j & 1, s = L % NSLOT;
+        if (!mbar_wait(&pfull[b2], (j >> 1) & 1)) return false;
+        if (!mbar_wait(&full[s], (L / NSLOT) & 1)) return false;
+        if (j >= 2 && !mbar_wait(&ofree[b2], ((j >> 1) - 1) & 1)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int ks = 0; ks < DT / 16; ++ks) {
+            const uint64_t ad = smem_desc_mn_sw128(kv_s + s * KV_TILE + 2 * h * (KV_TILE / 4) + ks * 2048, KV_TILE / 4);
+            const uint64_t bd = smem_desc_sw128(p_s + b2 * PD_BYTES + (ks >> 2) * 2048) + 2 * (ks & 3);
+            mma_bf16(tmem + 32 + b2 * 32 + h * 16, ad, bd, idO, ks > 0 ? 1u : 0u);
+          }
+        mma_commit(&ofull[b2]);
+        mma_commit(&slotfree[s]);
+        mma_commit(&pfree[b2]);
+        return true;
+      };
+      int L = 0, j = 0;
+      bool ok = true;
+      for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
+        int b, kvh, chunk, n;
+        if (!item(it, b, kvh, chunk, n)) continue;
+        if (!issue_s(j, L)) { ok = false; break; }               // S of this item ...
+        if (j > 0 && !issue_pv(j - 1, L - 1)) { ok = false; break; }  // ... then P V of the previous
+        L += 2;
+        ++j;
+      }
+      if (ok && j > 0 && !issue_pv(j - 1, L - 1)) ok = false;
+      if (!ok) atomicOr(&g_attn_tc_err, 0x20u);
+    }
+  } else {
+    // ------------------------------------------------------------ softmax + partials (warps 2..5)
+    const int quad = warp & 3;             // TMEM lane quadrant of this warp
+    const int r = quad * 32 + lane;        // key row of S^T, dim row of O^T
+    const uint32_t lane_base = uint32_t(quad * 32) << 16;
+    int L = 0, j = 0;
+    bool ok = true;
+    int pb_ = 0, pkvh = 0, pchunk = 0;
+    float pm[G], pl[G];
+    // A failed wait clears ``ok`` and later waits are skipped, but every thread keeps the same
+    // sequence of named barriers and warp-collective TMEM loads, so nothing waits forever.
+    auto wait = [&](uint64_t* bar, uint32_t parity) { ok = ok && mbar_wait(bar, parity); };
+    auto emit = [&](int jj) {              // partials of the item before
+      const int b2 = jj & 1;
+      wait(&ofull[b2], (jj >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+      float o0[16], o1[16];
+      tmem_ld16(tmem + 32 + b2 * 32 + lane_base, o0);
+      tmem_ld16(tmem + 32 + b2 * 32 + 16 + lane_base, o1);
+      tc_fence_before();
+      mbar_arrive(&ofree[b2]);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const size_t base = (size_t(pb_) * a.Hq + pkvh * G + g) * a.max_chunks + pchunk;
+        a.part_o[base * HD + r] = o0[g];
+        a.part_o[base * HD + 128 + r] = o1[g];
+        if (r == g) {
+          a.part_ml[base * 2 + 0] = pm[g] * 0.6931471805599453f;  // back to natural-log units
+          a.part_ml[base * 2 + 1] = pl[g];
+        }
+      }
+    };
+    for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
+      int b, kvh, chunk, n;
+      if (!item(it, b, kvh, chunk, n)) continue;
+      const int b2 = j & 1;
+      wait(&sfull[b2], (j >> 1) & 1);
+      __syncwarp();
+      tc_fence_after();
+      float sv[16];
+      tmem_ld16(tmem + b2 * 16 + lane_base, sv);
+      tc_fence_before();
+      mbar_arrive(&sfree[b2]);
+      const bool valid = r < n;
+      float x[G], m[G], l[G];
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        x[g] = valid ? sv[g] * a.scale_log2 : -INFINITY;
+        const float mx = warp_max(x[g]);
+        if (lane == 0) red[quad * 8 + g] = mx;
+      }
+      bar_sync_consumers();
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        m[g] = fmaxf(fmaxf(red[g], red[8 + g]), fmaxf(red[16 + g], red[24 + g]));  // finite: key 0 is valid
+        x[g] = valid ? exp2f(x[g] - m[g]) : 0.f;
+        const float sm = warp_sum(x[g]);
+        if (lane == 0) red[32 + quad * 8 + g] = sm;
+      }
+      if (j >= 2) wait(&pfree[b2], ((j >> 1) - 1) & 1);
+      uint8_t* prow = p_s + b2 * PD_BYTES + (r >> 6) * 2048;
+      const int pc = (r & 63) >> 3;
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+        *reinterpret_cast<__nv_bfloat16*>(prow + g * 128 + ((pc ^ g) * 16) + (r & 7) * 2) = __float2bfloat16(x[g]);
+      if (n < DT) {
+        // last tile of the sequence: zero the V rows past the context before P V reads them
+        const int vs = (L + 1) % NSLOT;
+        wait(&full[vs], ((L + 1) / NSLOT) & 1);
+        if (r >= n) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              *reinterpret_cast<uint4*>(kv_s + vs * KV_TILE + c * (KV_TILE / 4) + r * 128 + i * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&pfull[b2]);
+      bar_sync_consumers();
+#pragma unroll
+      for (int g = 0; g < G; ++g) l[g] = (red[32 + g] + red[40 + g]) + (red[48 + g] + red[56 + g]);
+      if (j > 0) emit(j - 1);
+      pb_ = b; pkvh = kvh; pchunk = chunk;
+#pragma unroll
+      for (int g = 0; g < G; ++g) { pm[g] = m[g]; pl[g] = l[g]; }
+      L += 2;
+      ++j;
+    }
+    if (j > 0) emit(j - 1);
+    if (!ok) atomicOr(&g_attn_tc_err, 0x40u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, DEC_TMEM_COLS);
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn_tc() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -347,7 +643,90 @@ void launch_tc(const at::Tensor& q, const at::Tensor& kc, const TcArgs& a, int B
   launch_pdl(kern, grid, dim3(256), SMEM_BYTES, st, tq, tk, a);
 }
 
+template <int G>
+void launch_dec_tc(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const DecArgs& a,
+                   cudaStream_t st) {
+  CUtensorMap tq, tk, tv;
+  {
+    cuuint64_t dims[2] = {cuuint64_t(HD), cuuint64_t(q.size(0)) * cuuint64_t(a.Hq)};
+    cuuint64_t strides[1] = {cuuint64_t(HD) * 2};
+    cuuint32_t box[2] = {64, cuuint32_t(G)};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = encode_fn_tc()(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, q.data_ptr(), dims, strides, box, es,
+                                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (decode q) failed: ", int(r));
+  }
+  const int64_t rows = kc.size(0) * kc.size(1) * kc.size(2);
+  for (int w = 0; w < 2; ++w) {
+    cuuint64_t dims[2] = {cuuint64_t(HD), cuuint64_t(rows)};
+    cuuint64_t strides[1] = {cuuint64_t(HD) * 2};
+    cuuint32_t box[2] = {64, DT};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = encode_fn_tc()(w ? &tv : &tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (w ? vc : kc).data_ptr(), dims,
+                                strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (decode kv) failed: ", int(r));
+  }
+  auto kern = attn_decode_tc_kernel<G>;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, DEC_SMEM) == cudaSuccess,
+                "tc decode attention smem attribute");
+    attr = true;
+  }
+  static int sms = 0;
+  if (!sms) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int grid = std::max(1, std::min(sms, a.nitems));
+  launch_pdl(kern, dim3(grid), dim3(192), DEC_SMEM, st, tq, tk, tv, a);
+}
+
 }  // namespace
+
+bool attention_decode_tc_supported(int64_t hd, int64_t hq, int64_t hkv) {
+  return hd == HD && hq % hkv == 0 && hq / hkv >= 1 && hq / hkv <= 8 && hq / hkv != 5 && hq / hkv != 7;
+}
+
+// Split-KV partials for 128-key chunks (chunk c of sequence b covers keys [128c, 128c+128));
+// ``part_o`` [B, Hq, max_chunks, 256] and ``part_ml`` [B, Hq, max_chunks, 2] fp32, merged by
+// the split-KV combine kernel.
+void attention_decode_tc_partials(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc,
+                                  const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale,
+                                  at::Tensor& part_o, at::Tensor& part_ml, int max_chunks) {
+  TORCH_CHECK(q.dim() == 3 && q.is_contiguous() && q.scalar_type() == at::kBFloat16, "q must be [B, Hq, 256] bf16");
+  TORCH_CHECK(kc.dim() == 4 && kc.size(2) == PAGE && kc.size(3) == HD && kc.is_contiguous() && vc.is_contiguous(),
+              "KV cache must be [blocks, Hkv, 256, 256]");
+  const int B = q.size(0), Hq = q.size(1), Hkv = kc.size(1);
+  TORCH_CHECK(attention_decode_tc_supported(q.size(2), Hq, Hkv), "unsupported head layout for tensor-core decode");
+  TORCH_CHECK(max_chunks == block_tables.size(1) * (PAGE / DT), "max_chunks must cover the block table");
+  DecArgs a = {};
+  a.ctx_lens = ctx_lens.data_ptr<int>();
+  a.block_tables = block_tables.data_ptr<int>();
+  a.max_blocks = block_tables.size(1);
+  a.B = B;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.scale_log2 = float(scale) * 1.4426950408889634f;
+  a.part_o = part_o.data_ptr<float>();
+  a.part_ml = part_ml.data_ptr<float>();
+  a.max_chunks = max_chunks;
+  a.nitems = max_chunks * B * Hkv;
+  if (B == 0) return;
+  auto st = at::cuda::getCurrentCUDAStream();
+  switch (Hq / Hkv) {
+    case 1: launch_dec_tc<1>(q, kc, vc, a, st); break;
+    case 2: launch_dec_tc<2>(q, kc, vc, a, st); break;
+    case 3: launch_dec_tc<3>(q, kc, vc, a, st); break;
+    case 4: launch_dec_tc<4>(q, kc, vc, a, st); break;
+    case 6: launch_dec_tc<6>(q, kc, vc, a, st); break;
+    case 8: launch_dec_tc<8>(q, kc, vc, a, st); break;
+    default: TORCH_CHECK(false, "unsupported GQA group");
+  }
+}
 
 bool attention_prefill_tc_supported(int64_t hd, int64_t hq, int64_t hkv) {
   if (hd != HD || hq % hkv) return false;

@@ -37,6 +37,17 @@ constexpr int D = 128;          // key == value head dim handled by these kernel
 constexpr int KW = 4;           // conv width
 constexpr int kThreads = 256;   // 8 row groups x 32 column groups
 
+__device__ unsigned int g_gdn_err;
+
+// One bulk asynchronous copy of a 64 KB state (global -> this CTA's shared memory), completing
+// on ``bar``.  Plain copy: no cluster multicast.
+__device__ __forceinline__ void bulk_g2s_state(float* dst, const float* src, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(reinterpret_cast<uint64_t>(src)), "r"(uint32_t(D * D * 4)), "r"(smem_u32(bar))
+               : "memory");
+}
+
 struct ScanArgs {
   const void* proj;        // [T, proj_stride] bf16, or fp32 accumulator that is consumed (read, then zeroed)
   int proj_stride;
@@ -84,8 +95,12 @@ __device__ __forceinline__ float take(const TIn* row, int idx, bool consume) {
   }
 }
 
-template <typename TIn>
-__global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
+// PERSIST (decode only): a grid of about two CTAs per SM walks the (key head, sequence) items;
+// each value head's 64 KB state is fetched into shared memory by one bulk asynchronous copy,
+// and the next one is requested as soon as every thread has the current state in registers,
+// so the state stream overlaps the per-token math and the write-back of the previous state.
+template <typename TIn, bool PERSIST>
+__global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nitems) {
   pdl_trigger();
   // Nothing is read before the wait: the state pools are also written by plainly launched
   // kernels (slot zeroing on allocation, checkpoint restore, MTP commit), and a dependent
@@ -94,11 +109,34 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
   __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
   __shared__ float red_k[8][D], red_q[8][D];
   __shared__ float scal[16];
+  __shared__ __align__(8) uint64_t st_bar;
+  extern __shared__ __align__(128) float st_s[];  // [D][D] prefetched state (PERSIST)
 
   const int tid = threadIdx.x;
   const int kr = tid >> 5, vc = (tid & 31) * 4;
-  const int hk = blockIdx.x, b = blockIdx.y;
   const int r = a.Hv / a.Hk;
+  // item order: (sequence, key head); value head j of an item is state unit (item * r + j)
+  auto unit_src = [&](int unit) -> const float* {
+    const int it = unit / r, jj = unit % r;
+    const int bb = it / a.Hk, hh = (it % a.Hk) * r + jj;
+    return a.rec + ((size_t(a.slots[bb]) * a.Hv + hh) * D) * D;
+  };
+  uint32_t st_phase = 0;
+  int unit = PERSIST ? int(blockIdx.x) * r : 0;
+  if constexpr (PERSIST) {
+    if (tid == 0) {
+      mbar_init(&st_bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (tid == 0 && int(blockIdx.x) < nitems) {
+      mbar_arrive_expect_tx(&st_bar, D * D * 4);
+      bulk_g2s_state(st_s, unit_src(unit), &st_bar);
+    }
+  }
+  for (int item = PERSIST ? int(blockIdx.x) : 0; PERSIST ? item < nitems : item < 1;
+       item += PERSIST ? int(gridDim.x) : 1) {
+  const int hk = PERSIST ? item % a.Hk : blockIdx.x, b = PERSIST ? item / a.Hk : blockIdx.y;
   const int t0 = a.cu_seqlens ? a.cu_seqlens[b] : b;
   const int t1 = a.cu_seqlens ? a.cu_seqlens[b + 1] : b + 1;
   const int slot = a.slots[b];
@@ -127,8 +165,21 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     // state tile
     float* S = a.rec + ((size_t(slot) * a.Hv + h) * D) * D;
     float4 st[16];
+    if constexpr (PERSIST) {
+      if (!mbar_wait(&st_bar, st_phase)) atomicOr(&g_gdn_err, 1u);
+      st_phase ^= 1u;
 #pragma unroll
-    for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
+      for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(st_s + (kr * 16 + i) * D + vc);
+      __syncthreads();  // every thread holds its part of the state: the buffer is free
+      unit = (j + 1 < r) ? unit + 1 : (item + int(gridDim.x)) * r;
+      if (tid == 0 && unit / r < nitems) {
+        mbar_arrive_expect_tx(&st_bar, D * D * 4);
+        bulk_g2s_state(st_s, unit_src(unit), &st_bar);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
+    }
 
     for (int t = t0; t < t1; ++t) {
       const TIn* x = static_cast<const TIn*>(a.proj) + size_t(t) * a.proj_stride;
@@ -246,6 +297,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a) {
     }
     __syncthreads();
   }
+  }  // items
 }
 
 __global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int pool_slots, const int* slots,
@@ -324,10 +376,46 @@ ScanArgs make_args(const at::Tensor& proj, const at::Tensor& slots, const at::Te
   return a;
 }
 
+bool gdn_persist_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ISB_GDN_PERSIST");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+int gdn_num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <typename TIn>
+void launch_scan_t(const ScanArgs& a, int64_t hk, int B, cudaStream_t st) {
+  const int items = int(hk) * B;
+  const int grid = 2 * gdn_num_sms();
+  if (a.cu_seqlens == nullptr && a.hist_row == nullptr && gdn_persist_enabled() && items >= 2 * grid) {
+    auto kern = gdn_scan_kernel<TIn, true>;
+    static bool attr = false;
+    if (!attr) {
+      TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, D * D * 4) == cudaSuccess,
+                  "persistent GDN smem attribute");
+      attr = true;
+    }
+    launch_pdl(kern, dim3(grid), dim3(kThreads), D * D * 4, st, a, items);
+    return;
+  }
+  launch_pdl(gdn_scan_kernel<TIn, false>, dim3(hk, B), dim3(kThreads), 0, st, a, 0);
+}
+
 void launch_scan(const ScanArgs& a, const at::Tensor& proj, int64_t hk, int B) {
   auto st = at::cuda::getCurrentCUDAStream();
-  if (proj.scalar_type() == at::kFloat) launch_pdl(gdn_scan_kernel<float>, dim3(hk, B), dim3(kThreads), 0, st, a);
-  else launch_pdl(gdn_scan_kernel<__nv_bfloat16>, dim3(hk, B), dim3(kThreads), 0, st, a);
+  if (proj.scalar_type() == at::kFloat) launch_scan_t<float>(a, hk, B, st);
+  else launch_scan_t<__nv_bfloat16>(a, hk, B, st);
 }
 
 }  // namespace
@@ -418,6 +506,14 @@ void gdn_conv_commit(at::Tensor conv, const at::Tensor& hist, const at::Tensor& 
       reinterpret_cast<__nv_bfloat16*>(conv.data_ptr()), conv.size(1),
       reinterpret_cast<const __nv_bfloat16*>(h.data_ptr()), h.size(1), sl.data_ptr<int>(), bd.data_ptr<int>(),
       int(steps), int(conv.size(2) * conv.size(3)));
+}
+
+int64_t gdn_error_word() {
+  unsigned int v = 0;
+  cudaMemcpyFromSymbol(&v, g_gdn_err, sizeof(v));
+  const unsigned int z = 0;
+  cudaMemcpyToSymbol(g_gdn_err, &z, sizeof(z));
+  return v;
 }
 
 }  // namespace isb

@@ -49,6 +49,8 @@ std::tuple<at::Tensor, at::Tensor> attn_prepare(const at::Tensor& qkv, const at:
                                                 bool gated, bool zc);
 at::Tensor attention_decode(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                             const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated);
+at::Tensor attention_decode_tc(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
+                               const at::Tensor& ctx_lens, const at::Tensor& block_tables, double scale, bool gated);
 at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                              double scale, bool gated, int64_t max_seqlen_q);
@@ -56,6 +58,7 @@ at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, con
                                 const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                                 double scale, bool gated, int64_t max_seqlen_q);
 int64_t attn_tc_error_word();
+int64_t gdn_error_word();
 void quantize_state_int8(const at::Tensor& state, at::Tensor q, at::Tensor scale);
 void dequantize_state_int8(const at::Tensor& q, const at::Tensor& scale, at::Tensor out);
 void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_t n);
@@ -75,7 +78,8 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
                         int64_t max_rows);
 
 int64_t error_word() {
-  return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24);
+  return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24) |
+         (gdn_error_word() << 32);
 }
 }  // namespace isb
 
@@ -112,6 +116,9 @@ TORCH_LIBRARY(isb, m) {
       "-> (Tensor, Tensor)");
   m.def(
       "attention_decode(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
+      "Tensor block_tables, float scale, bool gated) -> Tensor");
+  m.def(
+      "attention_decode_tc(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
   m.def(
       "attention_prefill_tc(Tensor q, Tensor gate, Tensor kc, Tensor vc, Tensor cu_q, Tensor ctx_lens, "
@@ -153,6 +160,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("gdn_conv_commit", &isb::gdn_conv_commit);
   m.impl("attn_prepare", &isb::attn_prepare);
   m.impl("attention_decode", &isb::attention_decode);
+  m.impl("attention_decode_tc", &isb::attention_decode_tc);
   m.impl("attention_prefill", &isb::attention_prefill);
   m.impl("quantize_state_int8", &isb::quantize_state_int8);
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);

@@ -120,7 +120,7 @@ def _gdn_inputs(b, hk, hv, seed, t=None):
     return proj, conv_w, a_log, dt_bias, norm_w, rec, conv, slot_ids
 
 
-@pytest.mark.parametrize("b,hk,hv", [(1, 16, 16), (7, 16, 16), (64, 4, 4), (5, 2, 6)])
+@pytest.mark.parametrize("b,hk,hv", [(1, 16, 16), (7, 16, 16), (64, 4, 4), (5, 2, 6), (48, 16, 16), (320, 2, 6)])
 def test_gdn_decode(b, hk, hv):
     proj, conv_w, a_log, dt_bias, norm_w, rec, conv, slots = _gdn_inputs(b, hk, hv, b + hk)
     rec_c, conv_c = rec.clone(), conv.clone()
@@ -234,13 +234,11 @@ def gate_ref(qkv, hq, hd):
     return qkv[:, : hq * hd * 2].reshape(t, hq, 2 * hd)[..., hd:].reshape(t, hq * hd)
 
 
-def _attn_case(seed, hq, hkv, hd, lens_new, lens_past, gated=True):
+def _attn_case(seed, hq, hkv, hd, lens_new, lens_past, gated=True, fill=0.0, nblocks=64, mb=8):
     g = torch.Generator().manual_seed(seed)
     b = len(lens_new)
-    nblocks = 64
-    kc = torch.zeros(nblocks, hkv, 256, hd, dtype=torch.bfloat16)
-    vc = torch.zeros_like(kc)
-    mb = 8
+    kc = torch.full((nblocks, hkv, 256, hd), fill, dtype=torch.bfloat16)
+    vc = torch.full_like(kc, fill)
     perm = torch.randperm(nblocks, generator=g)
     bt = torch.full((b, mb), -1, dtype=torch.int32)
     ids, pos, slots, cu, ctx = [], [], [], [0], []
@@ -333,6 +331,40 @@ def test_attention_decode(hq, hkv, past):
     out = torch.ops.isb.attention_decode(qg, gate, kc_g, vc_g, m["ctx"].to(DEV), m["bt"].to(DEV),
                                          hd ** -0.5, True)
     assert _rel(out.cpu(), exp) < 2e-2
+
+
+@pytest.mark.parametrize("hq,hkv,past", [
+    (8, 2, [0, 126, 127, 128, 129, 255, 256, 300, 511, 1000]),
+    (24, 8, [2000, 1, 383]),      # G = 3
+    (16, 2, [127, 700, 5]),       # G = 8
+    (6, 1, [128, 129]),           # G = 6
+    (2, 1, [40, 1500]),           # G = 2
+    (4, 4, [257, 64]),            # G = 1
+])
+def test_attention_decode_tc(hq, hkv, past):
+    """Tensor-core split-KV decode vs the fp32 reference and the SIMT kernel.  Cache rows
+    that no sequence owns hold NaN: the last-tile masking must keep them out."""
+    hd = 256
+    new = [1] * len(past)
+    qkv, qn, kn, cos_sin, kc, vc, m = _attn_case(7 * hq + sum(past), hq, hkv, hd, new, past, fill=float("nan"),
+                                                 nblocks=48, mb=9)
+    q, gate, k, v = ref.attn_qkv_prepare(qkv, m["positions"], qn, kn, cos_sin, hq, hkv, hd, 1e-6, True, True)
+    kc_r, vc_r = kc.clone(), vc.clone()
+    ref.store_kv(k, v, kc_r, vc_r, m["slot_mapping"])
+    exp = ref.paged_attention(q, kc_r, vc_r, m["cu"], m["ctx"], m["bt"], hd ** -0.5, gate)
+    assert torch.isfinite(exp).all()
+    kc_g, vc_g = kc.to(DEV), vc.to(DEV)
+    qg, gate_g = torch.ops.isb.attn_prepare(qkv.to(DEV), m["positions"].to(DEV), m["slot_mapping"].to(DEV),
+                                            qn.to(DEV), kn.to(DEV), cos_sin.to(DEV), kc_g, vc_g, hq, hkv, hd, 1e-6,
+                                            True, True)
+    args = (qg, gate_g, kc_g, vc_g, m["ctx"].to(DEV), m["bt"].to(DEV), hd ** -0.5, True)
+    out_tc = torch.ops.isb.attention_decode_tc(*args)
+    torch.cuda.synchronize()
+    assert torch.ops.isb.error_word() == 0
+    assert torch.isfinite(out_tc.float()).all()
+    assert _rel(out_tc.cpu(), exp) < 2e-2
+    out_auto = torch.ops.isb.attention_decode(*args)
+    assert _rel(out_auto.float(), out_tc.float()) < 2e-2
 
 
 def test_state_int8_roundtrip_and_page_copy():
