@@ -1,6 +1,6 @@
 """Per-kernel microbenchmarks of the sm_100a ops at Qwen3.5-0.8B decode shapes.
 
-    python bench_kernels.py [--batch 128] [--only gemm] [--json out.json] [--once]
+    python bench_kernels.py [--batch 128] [--only gemm[,attention]] [--json out.json] [--once]
     python -m torch.distributed.run --nproc-per-node N ... bench_kernels.py --tp   (fused TP paths)
 
 Method: every case builds R independent argument sets whose large operands
@@ -312,7 +312,7 @@ def main():
     hbm, tflops, src = peaks()
     rows = []
     for name, build in cases(args.batch).items():
-        if args.only and args.only not in name:
+        if args.only and not any(o in name for o in args.only.split(",")):
             continue
         fns, nbytes, flops = build()
         if args.once:

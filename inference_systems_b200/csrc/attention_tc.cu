@@ -481,17 +481,18 @@ __global__ void __launch_bounds__(192, 1)
         mma_commit(&pfree[b2]);
         return true;
       };
+      // In order, S then P V per item: P V frees the V slot as early as possible, and the ring
+      // (K of item j+1 waits for the slot of V of item j-1) keeps up to three tiles in flight.
+      // Issuing S of the next item first would make P V wait for that item's K to land.
       int L = 0, j = 0;
       bool ok = true;
       for (int it = blockIdx.x; it < a.nitems; it += gridDim.x) {
         int b, kvh, chunk, n;
         if (!item(it, b, kvh, chunk, n)) continue;
-        if (!issue_s(j, L)) { ok = false; break; }               // S of this item ...
-        if (j > 0 && !issue_pv(j - 1, L - 1)) { ok = false; break; }  // ... then P V of the previous
+        if (!issue_s(j, L) || !issue_pv(j, L + 1)) { ok = false; break; }
         L += 2;
         ++j;
       }
-      if (ok && j > 0 && !issue_pv(j - 1, L - 1)) ok = false;
       if (!ok) atomicOr(&g_attn_tc_err, 0x20u);
     }
   } else {

@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
   __shared__ float q_s[D], k_s[D], v_s[D], d_s[D];
   __shared__ float red_k[8][D], red_q[8][D];
   __shared__ float scal[16];
+  __shared__ float nrm[8], ep[4];
   __shared__ __align__(8) uint64_t st_bar;
   extern __shared__ __align__(128) float st_s[];  // [D][D] prefetched state (PERSIST)
 
@@ -121,6 +122,10 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
     const int bb = it / a.Hk, hh = (it % a.Hk) * r + jj;
     return a.rec + ((size_t(a.slots[bb]) * a.Hv + hh) * D) * D;
   };
+  auto issue_state = [&](int u) {  // bulk copy of state unit ``u`` into shared memory
+    mbar_arrive_expect_tx(&st_bar, D * D * 4);
+    bulk_g2s_state(st_s, unit_src(u), &st_bar);
+  };
   uint32_t st_phase = 0;
   int unit = PERSIST ? int(blockIdx.x) * r : 0;
   if constexpr (PERSIST) {
@@ -129,10 +134,7 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
       fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0 && int(blockIdx.x) < nitems) {
-      mbar_arrive_expect_tx(&st_bar, D * D * 4);
-      bulk_g2s_state(st_s, unit_src(unit), &st_bar);
-    }
+    if (tid == 0 && int(blockIdx.x) < nitems) issue_state(unit);
   }
   for (int item = PERSIST ? int(blockIdx.x) : 0; PERSIST ? item < nitems : item < 1;
        item += PERSIST ? int(gridDim.x) : 1) {
@@ -172,52 +174,49 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
       for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(st_s + (kr * 16 + i) * D + vc);
       __syncthreads();  // every thread holds its part of the state: the buffer is free
       unit = (j + 1 < r) ? unit + 1 : (item + int(gridDim.x)) * r;
-      if (tid == 0 && unit / r < nitems) {
-        mbar_arrive_expect_tx(&st_bar, D * D * 4);
-        bulk_g2s_state(st_s, unit_src(unit), &st_bar);
-      }
+      if (tid == 0 && unit / r < nitems) issue_state(unit);
     } else {
 #pragma unroll
       for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
     }
 
+    // Four block barriers per token.  q and k stay unnormalised in shared memory: their L2
+    // norms are reduced together with the k^T S / q^T S partial sums and applied as scalars
+    // (k^T S, q^T S, q.k and the key of the state update all scale linearly).
     for (int t = t0; t < t1; ++t) {
       const TIn* x = static_cast<const TIn*>(a.proj) + size_t(t) * a.proj_stride;
-      // --- conv + SiLU (an fp32 accumulator input is re-zeroed by its only reader)
+      // --- every input of this token first (an fp32 accumulator input is re-zeroed by its only reader)
       const float xq = take(x, qk_ch, j == r - 1);
+      float xv = 0.f, z = 0.f;
+      if (tid < 128) {
+        xv = take(x, v_ch, true);
+        z = take(x, a.C + h * D + tid, true);
+      }
+      float bb = 0.f, aa = 0.f;
+      if (tid == 0) {
+        bb = take(x, a.C + a.Hv * D + h, true);
+        aa = take(x, a.C + a.Hv * D + a.Hv + h, true);
+      }
+      // --- conv + SiLU
       const float aq = silu(wq0 * qs0 + wq1 * qs1 + wq2 * qs2 + wq3 * xq);
       qs0 = qs1; qs1 = qs2; qs2 = xq;
       if (tid < 128) {
         q_s[tid] = aq;
-        const float xv = take(x, v_ch, true);
         v_s[tid] = silu(wv0 * vs0 + wv1 * vs1 + wv2 * vs2 + wv3 * xv);
         vs0 = vs1; vs1 = vs2; vs2 = xv;
       } else {
         k_s[tid - 128] = aq;
       }
+      const float sq = warp_sum(aq * aq);
+      if ((tid & 31) == 0) nrm[tid >> 5] = sq;
       if (tid == 0) {
-        const float bb = take(x, a.C + a.Hv * D + h, true);
-        const float aa = take(x, a.C + a.Hv * D + a.Hv + h, true);
         const float g = A * softplusf(aa + dtb);
         scal[0] = 1.f / (1.f + expf(-bb));   // beta
         scal[1] = g;
         scal[2] = expf(g);                    // decay
       }
-      __syncthreads();
-      // --- L2 norms of q (threads 0..127) and k (128..255) and q.k
-      {
-        float sq = warp_sum(aq * aq);
-        if ((tid & 31) == 0) red_k[0][tid >> 5] = sq;
-        __syncthreads();
-        const float nq = red_k[0][0] + red_k[0][1] + red_k[0][2] + red_k[0][3];
-        const float nk = red_k[0][4] + red_k[0][5] + red_k[0][6] + red_k[0][7];
-        const float iq = rsqrtf(nq + 1e-6f) * inv_sqrt_d, ik = rsqrtf(nk + 1e-6f);
-        __syncthreads();
-        if (tid < 128) q_s[tid] = aq * iq; else k_s[tid - 128] = aq * ik;
-        __syncthreads();
-      }
-      const float beta = scal[0], g = scal[1], decay = scal[2];
-      // --- k^T S and q^T S for this thread's tile
+      __syncthreads();                                                     // (1) q, k, v, norms
+      // --- raw k^T S and q^T S for this thread's tile; raw q.k
       float ks[4] = {0.f, 0.f, 0.f, 0.f}, qsum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -227,27 +226,31 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
       }
       *reinterpret_cast<float4*>(&red_k[kr][vc]) = make_float4(ks[0], ks[1], ks[2], ks[3]);
       *reinterpret_cast<float4*>(&red_q[kr][vc]) = make_float4(qsum[0], qsum[1], qsum[2], qsum[3]);
-      // q.k for the output term
       float qk_part = tid < 128 ? q_s[tid] * k_s[tid] : 0.f;
       qk_part = warp_sum(qk_part);
       if ((tid & 31) == 0 && tid < 128) scal[4 + (tid >> 5)] = qk_part;
-      __syncthreads();
+      const float iq = rsqrtf(nrm[0] + nrm[1] + nrm[2] + nrm[3] + 1e-6f) * inv_sqrt_d;
+      const float ik = rsqrtf(nrm[4] + nrm[5] + nrm[6] + nrm[7] + 1e-6f);
+      const float beta = scal[0], g = scal[1], decay = scal[2];
+      __syncthreads();                                                     // (2) partial sums
       float o = 0.f;
       if (tid < 128) {
         float kS = 0.f, qS = 0.f;
 #pragma unroll
         for (int g8 = 0; g8 < 8; ++g8) { kS += red_k[g8][tid]; qS += red_q[g8][tid]; }
-        const float qk = scal[4] + scal[5] + scal[6] + scal[7];
+        kS *= ik;
+        qS *= iq;
+        const float qk = (scal[4] + scal[5] + scal[6] + scal[7]) * (iq * ik);
         const float delta = (v_s[tid] - decay * kS) * beta;
-        d_s[tid] = delta;
+        d_s[tid] = delta * ik;  // the state update multiplies by the raw key
         o = decay * qS + qk * delta;
         if (a.rec_k) {
-          a.rec_k[(size_t(t) * a.Hv + h) * D + tid] = k_s[tid];
+          a.rec_k[(size_t(t) * a.Hv + h) * D + tid] = k_s[tid] * ik;
           a.rec_delta[(size_t(t) * a.Hv + h) * D + tid] = delta;
           if (tid == 0) a.rec_g[size_t(t) * a.Hv + h] = g;
         }
       }
-      __syncthreads();
+      __syncthreads();                                                     // (3) delta
       // --- state update
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -274,11 +277,15 @@ __global__ void __launch_bounds__(kThreads) gdn_scan_kernel(ScanArgs a, int nite
           p[0] = __float2bfloat16(vs0); p[1] = __float2bfloat16(vs1); p[2] = __float2bfloat16(vs2);
         }
       }
-      // --- gated RMSNorm epilogue
+      // --- gated RMSNorm epilogue.  Its barrier also ends the token: every thread has finished
+      // reading q/k/v/d of this token before the next one overwrites them, and ``ep`` is written
+      // again only after barrier (1) of the next token.
       const float ob = __bfloat162float(__float2bfloat16(o));
-      const float ss = block_sum_128(tid < 128 ? ob * ob : 0.f, &scal[8], tid);
+      const float osq = warp_sum(tid < 128 ? ob * ob : 0.f);
+      if ((tid & 31) == 0 && tid < 128) ep[tid >> 5] = osq;
+      __syncthreads();                                                     // (4) output norm
       if (tid < 128) {
-        const float z = take(x, a.C + h * D + tid, true);
+        const float ss = ep[0] + ep[1] + ep[2] + ep[3];
         const float y = ob * rsqrtf(ss / float(D) + a.eps) * __bfloat162float(a.norm_w[tid]) * silu(z);
         a.out[size_t(t) * (a.Hv * D) + h * D + tid] = __float2bfloat16(y);
       }
