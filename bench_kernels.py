@@ -262,23 +262,35 @@ def tp_bench(batches=(1, 8, 128)) -> None:
         del gr
         return float(t.item())
 
-    for b in batches:
-        x = (torch.randn(b, inter, device=dev, generator=g)).to(bf)
-        res = torch.randn(b, h, device=dev, generator=g).to(bf)
-        fused = timed(lambda: comm.row_parallel_residual_norm(x, w, res, nw, 1e-6, True))
+    shapes = [(1024, 3584, b) for b in batches] + [(5120, 17408, 64)]  # 0.8B MLP down; 27B MLP down
+    for hh, full_inter, b in shapes:
+        ii = full_inter // world
+        cm = comm if hh == h else TPComm(dev, rank, world, hh, None, max_rows=256)
+        wd = w if hh == h else (torch.randn(hh, ii, device=dev, generator=g) * 0.02).to(bf)
+        nwd = nw if hh == h else torch.zeros(hh, device=dev).to(bf)
+        x = (torch.randn(b, ii, device=dev, generator=g)).to(bf)
+        res = torch.randn(b, hh, device=dev, generator=g).to(bf)
+        fused = timed(lambda: cm.row_parallel_residual_norm(x, wd, res, nwd, 1e-6, True))
+        local_gemm = timed(lambda: ops.linear(x, wd))
+        local_norm = timed(lambda: ops.add_rmsnorm(torch.zeros(b, hh, device=dev, dtype=bf), res, nwd, 1e-6, True))
 
         def nccl_path():
-            y = ops.linear(x, w)
+            y = ops.linear(x, wd)
             dist.all_reduce(y)
-            return ops.add_rmsnorm(y, res, nw, 1e-6, True)
+            return ops.add_rmsnorm(y, res, nwd, 1e-6, True)
 
         base = timed(nccl_path)
-        flops = 2 * b * inter * h
-        link = (world - 1) * b * h * 4 / (nvlink * 1e9) * 1e6
-        roof = max(flops / (tflops * 1e12) * 1e6, link, (h * inter * 2) / (hbm * 1e9) * 1e6)
+        flops = 2 * b * ii * hh
+        link = (world - 1) * b * hh * 4 / (nvlink * 1e9) * 1e6
+        roof = max(flops / (tflops * 1e12) * 1e6, link, (hh * ii * 2) / (hbm * 1e9) * 1e6)
         rows.append({"path": "row-parallel GEMM -> all-reduce -> residual + RMSNorm", "tp": world, "batch": b,
-                     "fused_us": round(fused, 2), "nccl_baseline_us": round(base, 2),
-                     "roofline_us": round(roof, 2), "fraction_of_roofline": round(roof / fused, 3)})
+                     "hidden": hh, "inter_per_rank": ii, "fused_us": round(fused, 2),
+                     "nccl_baseline_us": round(base, 2), "local_gemm_us": round(local_gemm, 2),
+                     "local_add_norm_us": round(local_norm, 2), "roofline_us": round(roof, 2),
+                     "fraction_of_roofline": round(roof / fused, 3)})
+        if cm is not comm:
+            cm.close()
+    for b in batches:
         hid = torch.randn(b, h, device=dev, generator=g).to(bf)
         temps = torch.zeros(b, device=dev)
         rng = torch.zeros(2, dtype=torch.int32, device=dev)
