@@ -96,8 +96,89 @@ ISB_DEVICE bool wait_counters(const unsigned long long* flags, int n, unsigned i
   return true;
 }
 
-// One block of 128 threads per row (8 columns per thread per step).
-__global__ void __launch_bounds__(128) acc_norm_tp_kernel(const unsigned long long* __restrict__ accs,
+// One block per row, 8 columns per thread (blockDim = H / 8 rounded up to a warp, at most
+// 512).  Every peer's slice of a chunk is loaded before any of it is summed (the peer loop
+// is unrolled over kMaxWorld with predication), so a thread has 2 x world NVLink loads in
+// flight instead of one round trip per peer.
+constexpr int kMaxWorld = 8;
+
+// Wait (threads 0..world-1, one peer each) until every rank's counter flags[r] has reached
+// this rank's own ``*my_flag``; returns the block-wide verdict.
+__device__ __forceinline__ bool wait_all_ranks(const unsigned long long* flags, const unsigned int* my_flag,
+                                               int world) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < world) {  // one NVLink round trip per peer, all in parallel
+    const unsigned int target = ld_acquire_sys(my_flag);
+    if (!wait_counters(flags + threadIdx.x, 1, target)) ok = 0;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+// out_row = RMSNorm(res_row + sum_r accs[r][acc_row]); res_row is updated in place.
+__device__ __forceinline__ void pull_add_norm_row(const unsigned long long* __restrict__ accs, int world, bool ok,
+                                                  size_t acc_row, __nv_bfloat16* __restrict__ res,
+                                                  const __nv_bfloat16* __restrict__ w,
+                                                  __nv_bfloat16* __restrict__ out, int H, float eps, bool zc) {
+  __shared__ float red[32];
+  const int tid = threadIdx.x, nt = blockDim.x;
+  const float* peer[kMaxWorld];
+#pragma unroll
+  for (int r = 0; r < kMaxWorld; ++r) peer[r] = r < world ? reinterpret_cast<const float*>(accs[r]) + acc_row * H : nullptr;
+  float ss = 0.f;
+  constexpr int kMaxChunks = 4;  // H <= 4 * 8 * 512
+  float v[kMaxChunks][8];
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = (tid + k * nt) * 8;
+    if (c >= H) break;
+    float4 lo[kMaxWorld], hi[kMaxWorld];
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+      if (r < world && ok) {
+        lo[r] = __ldcv(reinterpret_cast<const float4*>(peer[r] + c));
+        hi[r] = __ldcv(reinterpret_cast<const float4*>(peer[r] + c + 4));
+      } else {
+        lo[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+        hi[r] = lo[r];
+      }
+    }
+    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < kMaxWorld; ++r) {
+      x[0] += lo[r].x; x[1] += lo[r].y; x[2] += lo[r].z; x[3] += lo[r].w;
+      x[4] += hi[r].x; x[5] += hi[r].y; x[6] += hi[r].z; x[7] += hi[r].w;
+    }
+    const Vec8 rr = load8(res + c);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      v[k][i] = x[i] + rr.v[i];
+      ss += v[k][i] * v[k][i];
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (nt + 31) / 32; ++i) tot += red[i];
+  const float rs = rsqrtf(tot / float(H) + eps);
+#pragma unroll
+  for (int k = 0; k < kMaxChunks; ++k) {
+    const int c = (tid + k * nt) * 8;
+    if (c >= H) break;
+    store8(res + c, v[k]);
+    const Vec8 wv = load8(w + c);
+    float y[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      y[i] = zc ? v[k][i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[k][i] * rs)) * wv.v[i];
+    store8(out + c, y);
+  }
+}
+
+__global__ void __launch_bounds__(512) acc_norm_tp_kernel(const unsigned long long* __restrict__ accs,
                                                           float* __restrict__ my_other,
                                                           __nv_bfloat16* __restrict__ residual,
                                                           const __nv_bfloat16* __restrict__ w,
@@ -107,64 +188,89 @@ __global__ void __launch_bounds__(128) acc_norm_tp_kernel(const unsigned long lo
                                                           unsigned int* rows_used, int parity) {
   pdl_trigger();
   pdl_wait();
-  __shared__ int ok;
-  __shared__ float red[4];
-  const int tid = threadIdx.x, row = blockIdx.x;
-  if (tid == 0) ok = 1;
-  __syncthreads();
-  if (tid < world) {  // every peer's counter is polled by its own thread: one NVLink round trip, not world
-    const unsigned int target = ld_acquire_sys(my_flag);  // this rank's GEMM of this call has completed
-    if (!wait_counters(flags + tid, 1, target)) ok = 0;
-  }
-  __syncthreads();
+  const int tid = threadIdx.x, row = blockIdx.x, nt = blockDim.x;
+  const bool ok = wait_all_ranks(flags, my_flag, world);
   // re-zero the accumulator rows of the previous call (other parity); peers are done with them
   const int prev_rows = int(rows_used[parity ^ 1]);
   for (int r = row; r < prev_rows; r += gridDim.x)
-    for (int c = tid * 4; c < H; c += 512) *reinterpret_cast<float4*>(my_other + size_t(r) * H + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (row < rows) {
-    __nv_bfloat16* res = residual + size_t(row) * H;
-    float ss = 0.f;
-    constexpr int kMaxChunks = 8;  // H <= 8 * 1024
-    float v[kMaxChunks][8];
-#pragma unroll
-    for (int k = 0; k < kMaxChunks; ++k) {
-      const int c = tid * 8 + k * 1024;
-      if (c >= H) break;
-      float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      if (ok) {
-        for (int r = 0; r < world; ++r) {
-          const float* a = reinterpret_cast<const float*>(accs[r]) + size_t(row) * H + c;
-          const float4 x0 = __ldcv(reinterpret_cast<const float4*>(a));
-          const float4 x1 = __ldcv(reinterpret_cast<const float4*>(a + 4));
-          x[0] += x0.x; x[1] += x0.y; x[2] += x0.z; x[3] += x0.w;
-          x[4] += x1.x; x[5] += x1.y; x[6] += x1.z; x[7] += x1.w;
-        }
-      }
-      const Vec8 rr = load8(res + c);
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        v[k][i] = x[i] + rr.v[i];
-        ss += v[k][i] * v[k][i];
-      }
-    }
-    ss = warp_sum(ss);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    const float rs = rsqrtf((red[0] + red[1] + red[2] + red[3]) / float(H) + eps);
-#pragma unroll
-    for (int k = 0; k < kMaxChunks; ++k) {
-      const int c = tid * 8 + k * 1024;
-      if (c >= H) break;
-      store8(res + c, v[k]);
-      const Vec8 wv = load8(w + c);
-      float y[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i)
-        y[i] = zc ? v[k][i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[k][i] * rs)) * wv.v[i];
-      store8(out + size_t(row) * H + c, y);
+    for (int c = tid * 4; c < H; c += nt * 4) *reinterpret_cast<float4*>(my_other + size_t(r) * H + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (row < rows)
+    pull_add_norm_row(accs, world, ok, size_t(row), residual + size_t(row) * H, w, out + size_t(row) * H, H, eps, zc);
+  if (row == 0 && tid == 0) rows_used[parity] = unsigned(rows);
+}
+
+// Every CTA makes its writes visible system-wide and counts itself in; the last one resets the
+// counter and releases ``*ready += 1`` at system scope.
+__device__ __forceinline__ void finish_and_release(unsigned int* done_ctr, unsigned int* ready) {
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(done_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      atomicExch(done_ctr, 0u);
+      __threadfence_system();
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ready) : "memory");
     }
   }
-  if (row == 0 && tid == 0) rows_used[parity] = unsigned(rows);
+}
+
+// Token-sharded (sequence-parallel) reduce-scatter + residual + RMSNorm: rank r owns rows
+// [row_base, row_base + rows) of the T tokens.  Each CTA pulls one of those rows from every
+// rank's fp32 partial product (after every rank's row-parallel GEMM counter has caught up with
+// this rank's), adds the shard's residual row, and writes the normalised row into this rank's
+// shard buffer, which peers read in their all-gather GEMMs once ``*ready`` has moved on.
+__global__ void __launch_bounds__(512) sp_rs_norm_kernel(const unsigned long long* __restrict__ accs,
+                                                         const unsigned long long* gflags,
+                                                         const unsigned int* my_gflag, int world,
+                                                         __nv_bfloat16* __restrict__ residual,
+                                                         const __nv_bfloat16* __restrict__ w,
+                                                         __nv_bfloat16* __restrict__ xs, int rows, int row_base, int H,
+                                                         float eps, bool zc, unsigned int* done_ctr,
+                                                         unsigned int* ready) {
+  pdl_trigger();
+  pdl_wait();
+  const bool ok = wait_all_ranks(gflags, my_gflag, world);
+  const int row = blockIdx.x;
+  if (row < rows)
+    pull_add_norm_row(accs, world, ok, size_t(row_base + row), residual + size_t(row) * H, w, xs + size_t(row) * H,
+                      H, eps, zc);
+  finish_and_release(done_ctr, ready);
+}
+
+// Copy this rank's first normalised shard (embedding + first RMSNorm) into its shard buffer
+// and release ``*ready``.
+__global__ void __launch_bounds__(256) sp_publish_kernel(const __nv_bfloat16* __restrict__ x,
+                                                         __nv_bfloat16* __restrict__ xs, int rows, int H,
+                                                         unsigned int* done_ctr, unsigned int* ready) {
+  pdl_trigger();
+  pdl_wait();
+  const int row = blockIdx.x;
+  if (row < rows)
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(xs + size_t(row) * H + c) = *reinterpret_cast<const uint4*>(x + size_t(row) * H + c);
+  finish_and_release(done_ctr, ready);
+}
+
+// out[t] = row t of the token-sharded activation (owner t / S, its row t % S), read from the
+// owner's shard buffer once the owner's counter has reached this rank's.
+__global__ void __launch_bounds__(256) sp_gather_kernel(const unsigned long long* __restrict__ xs,
+                                                        const unsigned long long* flags, const unsigned int* my_flag,
+                                                        int S, int H, __nv_bfloat16* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int ok;
+  const int t = blockIdx.x, owner = t / S;
+  if (threadIdx.x == 0) {
+    const unsigned int target = ld_acquire_sys(my_flag);
+    ok = wait_counters(flags + owner, 1, target) ? 1 : 0;
+  }
+  __syncthreads();
+  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(xs[owner]) + size_t(t - owner * S) * H;
+  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+    uint4 v = make_uint4(0u, 0u, 0u, 0u);
+    if (ok) v = __ldcv(reinterpret_cast<const uint4*>(src + c));
+    *reinterpret_cast<uint4*>(out + size_t(t) * H + c) = v;
+  }
 }
 
 // Single CTA.  Publish this rank's (score, token) per row to every peer's exchange slot,
@@ -247,9 +353,11 @@ at::Tensor add_rmsnorm_acc_tp(const at::Tensor& accs, at::Tensor my_acc_other, a
   TORCH_CHECK(my_flag.scalar_type() == at::kInt && rows_used.scalar_type() == at::kInt && rows_used.numel() == 2,
               "int32 flag / row-count words");
   const int H = residual.size(-1), rows = residual.numel() / H;
-  TORCH_CHECK(H % 8 == 0 && H <= 8192, "hidden size must be a multiple of 8 and at most 8192");
+  TORCH_CHECK(H % 8 == 0 && H <= 16384, "hidden size must be a multiple of 8 and at most 16384");
   at::Tensor out = at::empty_like(residual);
-  launch_pdl(acc_norm_tp_kernel, dim3(std::max(rows, 1)), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+  TORCH_CHECK(flags.numel() <= kMaxWorld, "at most ", kMaxWorld, " ranks");
+  const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
+  launch_pdl(acc_norm_tp_kernel, dim3(std::max(rows, 1)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()), my_acc_other.data_ptr<float>(),
              reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H, float(eps), zc,
@@ -270,6 +378,47 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
       reinterpret_cast<const unsigned long long*>(peer_flags.data_ptr<int64_t>()),
       reinterpret_cast<unsigned int*>(my_flags.data_ptr<int>()), reinterpret_cast<const float2*>(my_xbuf.data_ptr()),
       int(rank), int(xbufs.numel()), int(max_rows), out.data_ptr<int>());
+  return out;
+}
+
+// ---------------------------------------------------------------- sequence-parallel (token-sharded) path
+void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
+                const at::Tensor& w, at::Tensor xs, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
+                at::Tensor ready) {
+  TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16 && residual.dim() == 2,
+              "residual shard: contiguous bf16 [rows, H]");
+  const int rows = residual.size(0), H = residual.size(1);
+  TORCH_CHECK(H % 8 == 0 && H <= 16384 && xs.size(-1) == H && xs.numel() >= int64_t(rows) * H, "shard buffer shape");
+  TORCH_CHECK(gflags.numel() <= kMaxWorld && accs.numel() == gflags.numel(), "one accumulator and counter per rank");
+  const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
+  launch_pdl(sp_rs_norm_kernel, dim3(std::max(rows, 1)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned long long*>(gflags.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned int*>(my_gflag.data_ptr<int>()), int(gflags.numel()),
+             reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+             reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()), rows, int(row_base), H, float(eps), zc,
+             reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
+}
+
+void sp_publish(const at::Tensor& x, at::Tensor xs, at::Tensor done_ctr, at::Tensor ready) {
+  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "x: contiguous bf16 [rows, H]");
+  const int rows = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && xs.size(-1) == H && xs.numel() >= int64_t(rows) * H, "shard buffer shape");
+  launch_pdl(sp_publish_kernel, dim3(std::max(rows, 1)), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()), rows,
+             H, reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
+}
+
+at::Tensor sp_gather(const at::Tensor& xs_ptrs, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
+                     int64_t T, int64_t H, const at::Tensor& like) {
+  TORCH_CHECK(H % 8 == 0 && S > 0 && T <= S * flags.numel(), "gather shape");
+  at::Tensor out = at::empty({T, H}, like.options().dtype(at::kBFloat16));
+  if (T == 0) return out;
+  launch_pdl(sp_gather_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const unsigned long long*>(xs_ptrs.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned int*>(my_flag.data_ptr<int>()), int(S), int(H),
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
   return out;
 }
 

@@ -21,6 +21,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdlib>
+#include <vector>
 #include <torch/extension.h>
 
 #include "common.cuh"
@@ -77,6 +78,15 @@ struct GemmArgs {
   // when set, the grid's last CTA releases ``*signal += 1`` at system scope after every CTA's tile
   // is in ``acc`` (tensor-parallel peers poll it before reading this rank's accumulator)
   unsigned int* signal;
+  // All-gather operand (non-swap path only): the activation rows are token-sharded over the
+  // tensor-parallel ranks, ``ag_rows`` rows per rank (a multiple of BM), each rank's shard in its
+  // own symmetric buffer described by ``ag_maps[rank]`` (tensor maps in device memory).  The M
+  // tile at row m*BM is read from rank m*BM / ag_rows once that rank's shard counter
+  // (``ag_flags[rank]``, peer memory) has reached this rank's own counter ``*ag_own``.
+  const CUtensorMap* ag_maps;
+  const unsigned long long* ag_flags;
+  const unsigned int* ag_own;
+  int ag_rows;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -192,9 +202,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (SWAP) tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
         else tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
       };
+      // all-gather operand: the rank that owns this M tile and the tile's row inside its shard
+      const CUtensorMap* x_map = &tmP;
+      int x_row = tile_p * BM;
+      if constexpr (!SWAP) {
+        if (args.ag_maps != nullptr) {
+          const int owner = (tile_p * BM) / args.ag_rows;
+          x_map = args.ag_maps + owner;
+          x_row = tile_p * BM - owner * args.ag_rows;
+        }
+      }
       auto load_x = [&](uint8_t* sp, uint64_t* bar, int kx) {
         if constexpr (SWAP) tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
-        else tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
+        else tma_load_2d(sp, x_map, bar, kx, x_row);
       };
       const int pre = min(nkb, Cfg::STAGES);
       for (int i = 0; i < pre; ++i) {  // fresh stages: nothing to wait for
@@ -202,6 +222,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_w(smem + i * Cfg::STAGE_BYTES, &full[i], (kb_begin + i) * BK);
       }
       pdl_wait();
+      if constexpr (!SWAP) {
+        if (args.ag_maps != nullptr) {
+          // the owner's shard of this call is published once its counter reaches ours (every
+          // rank publishes once per call); bounded wait
+          const int owner = (tile_p * BM) / args.ag_rows;
+          unsigned int target;
+          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(target) : "l"(args.ag_own) : "memory");
+          const unsigned int* f = reinterpret_cast<const unsigned int*>(args.ag_flags[owner]);
+          const uint64_t t0 = globaltimer_ns();
+          uint32_t spins = 0;
+          bool ok = true;
+          for (;;) {
+            unsigned int v;
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if (int(v - target) >= 0) break;
+            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) { ok = false; break; }
+          }
+          if (!ok) atomicOr(&g_gemm_err, 8u);  // loads proceed: the result is flagged as invalid
+        }
+      }
       for (int i = 0; i < nkb; ++i) {
         if (dbg && i == 0) dbg[2] = globaltimer_ns();
         const int s = i % Cfg::STAGES;
@@ -1155,6 +1195,61 @@ void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, 
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+}
+
+// Tensor maps of every rank's shard buffer for the all-gather GEMM: ``ptrs`` (CPU int64 [W])
+// are the shard buffers' device addresses (peer mappings for the other ranks), each [rows, cols]
+// bf16.  Returns W 128-byte tensor maps in device memory.
+at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, const at::Tensor& like) {
+  TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == at::kLong, "ptrs: CPU int64");
+  TORCH_CHECK(cols % 8 == 0 && rows % BM == 0, "shard rows must be a multiple of 128, columns of 8");
+  const int W = ptrs.numel();
+  std::vector<CUtensorMap> maps(W);
+  for (int r = 0; r < W; ++r) {
+    const void* p = reinterpret_cast<const void*>(ptrs.data_ptr<int64_t>()[r]);
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(p) % 16 == 0, "shard buffer must be 16-byte aligned");
+    maps[r] = make_kmajor_map(p, rows, cols, BM);
+  }
+  at::Tensor out = at::empty({int64_t(W) * int64_t(sizeof(CUtensorMap))}, like.options().dtype(at::kByte));
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 64 == 0, "tensor maps need 64-byte alignment");
+  TORCH_CHECK(cudaMemcpy(out.data_ptr(), maps.data(), W * sizeof(CUtensorMap), cudaMemcpyHostToDevice) == cudaSuccess,
+              "copying tensor maps");
+  return out;
+}
+
+// out[T, N] (or [T, N/2] for the SiLU-mul epilogue) = gather_rows(shards)[T, K] . b[N, K]^T, the
+// activation rows read straight from their owners' shard buffers (see GemmArgs::ag_maps).
+// ``local`` is this rank's shard buffer [shard_rows, K] (gives the K extent and a valid default
+// map); ``flags`` (int64 [W], device) are the ranks' shard counters; ``own`` is this rank's.
+at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
+                   int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue) {
+  check_operands(local, b);
+  const int K = local.size(1), N = b.size(0);
+  const int W = flags.numel();
+  TORCH_CHECK(maps.numel() == int64_t(W) * int64_t(sizeof(CUtensorMap)), "one tensor map per rank");
+  TORCH_CHECK(shard_rows % BM == 0 && shard_rows <= local.size(0) && T > BM && T <= int64_t(W) * shard_rows,
+              "all-gather GEMM: shard rows a multiple of 128 within the buffer, 128 < T <= ranks * shard rows");
+  TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm_ag: unknown epilogue");
+  at::Tensor out = at::empty({T, epilogue == kSiluMul ? N / 2 : N}, b.options());
+  GemmArgs args = {};
+  args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  args.K = K;
+  args.ldo = out.size(1);
+  const int kb_total = (K + BK - 1) / BK;
+  args.kb_per_split = kb_total;
+  args.P_rows = int(T);
+  args.Q_rows = N;
+  args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
+  args.ag_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
+  args.ag_own = reinterpret_cast<const unsigned int*>(own.data_ptr<int>());
+  args.ag_rows = int(shard_rows);
+  const CUtensorMap tp = make_kmajor_map(local.data_ptr(), local.size(0), K, BM);
+  const CUtensorMap tq = make_kmajor_map(b.data_ptr(), N, K, 256);
+  const int tiles_p = int((T + BM - 1) / BM), tiles_q = (N + 255) / 256;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (epilogue == kStore) launch_gemm<256, false, kStore>(tp, tq, tp, args, tiles_p, tiles_q, 1, st);
+  else launch_gemm<256, false, kSiluMul>(tp, tq, tp, args, tiles_p, tiles_q, 1, st);
+  return out;
 }
 
 at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, int64_t splits) {

@@ -77,6 +77,16 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
                         const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
                         int64_t max_rows);
 
+at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, const at::Tensor& like);
+at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
+                   int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue);
+void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
+                const at::Tensor& w, at::Tensor xs, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
+                at::Tensor ready);
+void sp_publish(const at::Tensor& x, at::Tensor xs, at::Tensor done_ctr, at::Tensor ready);
+at::Tensor sp_gather(const at::Tensor& xs_ptrs, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
+                     int64_t T, int64_t H, const at::Tensor& like);
+
 int64_t error_word() {
   return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24) |
          (gdn_error_word() << 32);
@@ -117,6 +127,14 @@ TORCH_LIBRARY(isb, m) {
   m.def(
       "attention_decode(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
+  m.def("ag_tensor_maps(Tensor ptrs, int rows, int cols, Tensor like) -> Tensor");
+  m.def("gemm_ag(Tensor local, Tensor maps, Tensor flags, Tensor own, int shard_rows, int T, Tensor b, int epilogue) "
+        "-> Tensor");
+  m.def(
+      "sp_rs_norm(Tensor accs, Tensor gflags, Tensor my_gflag, Tensor(a!) residual, Tensor w, Tensor(b!) xs, "
+      "int row_base, float eps, bool zc, Tensor(c!) done_ctr, Tensor(d!) ready) -> ()");
+  m.def("sp_publish(Tensor x, Tensor(a!) xs, Tensor(b!) done_ctr, Tensor(c!) ready) -> ()");
+  m.def("sp_gather(Tensor xs_ptrs, Tensor flags, Tensor my_flag, int S, int T, int H, Tensor like) -> Tensor");
   m.def(
       "attention_decode_tc(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
@@ -161,6 +179,11 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("attn_prepare", &isb::attn_prepare);
   m.impl("attention_decode", &isb::attention_decode);
   m.impl("attention_decode_tc", &isb::attention_decode_tc);
+  m.impl("ag_tensor_maps", &isb::ag_tensor_maps);
+  m.impl("gemm_ag", &isb::gemm_ag);
+  m.impl("sp_rs_norm", &isb::sp_rs_norm);
+  m.impl("sp_publish", &isb::sp_publish);
+  m.impl("sp_gather", &isb::sp_gather);
   m.impl("attention_prefill", &isb::attention_prefill);
   m.impl("quantize_state_int8", &isb::quantize_state_int8);
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);

@@ -19,7 +19,16 @@ Here, on GPUs:
 * ``lm_head_sample`` = the LM-head GEMM with its fused greedy/Gumbel-max
   selection on this rank's vocab slice + ``xrank_argmax``, which exchanges 8
   bytes per row with every peer; every rank ends with the same token ids.
-* Prefill chunks larger than ``max_rows`` tokens use NCCL all-reduce.
+* Prefill chunks larger than ``max_rows`` tokens run token-sharded (sequence
+  parallel within the TP group) when ``sp_rows`` allows: the residual stream is
+  split by tokens; each row-parallel GEMM stores its fp32 partial product and
+  ``sp_rs_norm`` (reduce-scatter + residual + RMSNorm) pulls only this rank's
+  token rows from every peer and publishes the normalised shard; the next
+  column-parallel GEMM (``gemm_ag``) reads every M tile straight from the
+  owning rank's shard buffer (all-gather fused into the GEMM's operand loads).
+  Per layer a rank moves ``(W-1)/W * T/W * H`` fp32 values in and
+  ``(W-1)/W * T * H`` bf16 values through its GEMM, instead of all-reducing
+  ``T * H``.  Otherwise larger chunks use NCCL all-reduce.
 
 On CPU (gloo process groups, used by the tests) the same methods run with
 ``torch.distributed`` collectives.
@@ -27,16 +36,43 @@ On CPU (gloo process groups, used by the tests) the same methods run with
 
 from __future__ import annotations
 
+import os
+from dataclasses import dataclass
+
 import torch
 import torch.distributed as dist
 
 from inference_systems_b200 import ops
 
 _ALIGN = 256
+_SP_TILE = 128  # shard rows are a multiple of the GEMM's M tile
 
 
 def _align(n: int) -> int:
     return (n + _ALIGN - 1) // _ALIGN * _ALIGN
+
+
+@dataclass
+class ShardedActivation:
+    """A normalised activation ``[T, H]`` split by tokens over the TP group.
+
+    Rank ``r`` holds rows ``[r*S, min((r+1)*S, T))`` in ``local`` (on GPUs: a
+    view of its symmetric shard buffer of parity ``parity``).  Column-parallel
+    layers consume it through ``TPComm.sp_linear``.
+    """
+    comm: "TPComm"
+    local: torch.Tensor
+    T: int
+    S: int
+    parity: int
+
+    @property
+    def shape(self):
+        return (self.T, self.local.shape[1])
+
+    @property
+    def is_cuda(self) -> bool:
+        return self.local.is_cuda
 
 
 class TPComm:
@@ -44,13 +80,21 @@ class TPComm:
                  max_rows: int = 256, max_sample_rows: int | None = None, group=None):
         self.device, self.rank, self.world, self.hidden = device, rank, world, hidden
         self.group = group
-        self.max_rows = max_rows
+        self.max_rows = int(os.environ.get("ISB_TP_MAX_ROWS", max_rows))
         spec = getattr(config, "num_speculative_tokens", 0) if config is not None else 0
         seqs = getattr(config, "max_num_seqs", 256) if config is not None else 256
         self.max_sample_rows = max_sample_rows or max(512, seqs * (spec + 1))
         self.set = 0
         self.fused = device.type == "cuda"
+        # shard rows are a multiple of the GEMM's 128-row M tile on GPUs; CPU ranks split finer
+        self.sp_tile = _SP_TILE if self.fused else 8
         self._peer_ptrs: list[int] = []
+        # token-sharded prefill: ISB_TP_SP=1 enables it, for chunks of max_rows < T <= max_sp_rows
+        self.sp = os.environ.get("ISB_TP_SP", "0") == "1" and world > 1
+        tokens = getattr(config, "max_num_batched_tokens", 8192) if config is not None else 8192
+        self.max_sp_rows = min(int(tokens), 16384) if self.sp else 0
+        self.sp_shard_max = self._shard_rows(self.max_sp_rows) if self.sp else 0
+        self.sp_set = 0
         if self.fused:
             self._setup_symmetric()
 
@@ -62,7 +106,10 @@ class TPComm:
         layout = {}
         for name, nbytes in (("acc0", self.max_rows * h * 4), ("acc1", self.max_rows * h * 4),
                              ("accflag0", w * 4), ("accflag1", w * 4), ("gdone0", 4), ("gdone1", 4),
-                             ("ndone0", 4), ("ndone1", 4), ("xbuf", w * self.max_sample_rows * 8), ("xflag", w * 4)):
+                             ("ndone0", 4), ("ndone1", 4), ("xbuf", w * self.max_sample_rows * 8), ("xflag", w * 4),
+                             ("spacc0", self.max_sp_rows * h * 4), ("spacc1", self.max_sp_rows * h * 4),
+                             ("xs0", self.sp_shard_max * h * 2), ("xs1", self.sp_shard_max * h * 2),
+                             ("spgflag", 4), ("spgdone", 4), ("xsflag", 4), ("spdone", 4)):
             layout[name] = off
             off += _align(nbytes)
         self.layout, self.nbytes = layout, off
@@ -98,6 +145,20 @@ class TPComm:
         self.xflag_ptrs = table("xflag")
         self.xbuf_local = local("xbuf", torch.float32, w * self.max_sample_rows * 2)
         self.xflag_local = local("xflag", torch.int32, w)
+        if self.sp:
+            c2 = ops.cuda_ops()
+            self.spacc_ptrs = [table("spacc0"), table("spacc1")]
+            self.spacc_local = [local(f"spacc{i}", torch.float32, self.max_sp_rows * h).view(self.max_sp_rows, h)
+                                for i in range(2)]
+            self.xs_local = [local(f"xs{i}", torch.bfloat16, self.sp_shard_max * h).view(self.sp_shard_max, h)
+                             for i in range(2)]
+            self.xs_ptrs = [table("xs0"), table("xs1")]
+            self.xs_maps = [c2.ag_tensor_maps(torch.tensor([b + layout[f"xs{i}"] for b in bases], dtype=torch.int64),
+                                              self.sp_shard_max, h, self.region) for i in range(2)]
+            self.spgflag_ptrs, self.spgflag_local = table("spgflag"), local("spgflag", torch.int32, 1)
+            self.spgdone = local("spgdone", torch.int32, 1)
+            self.xsflag_ptrs, self.xsflag_local = table("xsflag"), local("xsflag", torch.int32, 1)
+            self.spdone = local("spdone", torch.int32, 1)
         torch.cuda.synchronize(self.device)
         dist.barrier(group=self.group)
 
@@ -125,6 +186,74 @@ class TPComm:
         y = ops.linear(x, w)
         dist.all_reduce(y, group=self.group)
         return ops.add_rmsnorm(y, residual, norm_w, eps, zero_centered)
+
+    # ------------------------------------------------------------ token-sharded prefill
+    def _shard_rows(self, T: int) -> int:
+        per = (T + self.world - 1) // self.world
+        return max(self.sp_tile, (per + self.sp_tile - 1) // self.sp_tile * self.sp_tile)
+
+    def sp_rows(self, T: int) -> int:
+        """Shard rows S for a ``T``-token forward, or 0 when it runs replicated."""
+        if not self.sp or T <= self.max_rows or T > self.max_sp_rows:
+            return 0
+        return self._shard_rows(T)
+
+    def sp_range(self, T: int, S: int) -> tuple[int, int]:
+        lo = min(self.rank * S, T)
+        return lo, min(lo + S, T)
+
+    def sp_publish(self, x: torch.Tensor, T: int, S: int) -> ShardedActivation:
+        """Make this rank's first normalised shard ``x`` ``[rows, H]`` visible to the group."""
+        if not self.fused:
+            return ShardedActivation(self, x, T, S, 0)
+        q = self.sp_set
+        self.sp_set ^= 1
+        ops.cuda_ops().sp_publish(x.contiguous(), self.xs_local[q], self.spdone, self.xsflag_local)
+        return ShardedActivation(self, self.xs_local[q][: x.shape[0]], T, S, q)
+
+    def sp_linear(self, x: ShardedActivation, w: torch.Tensor, silu_mul: bool = False) -> torch.Tensor:
+        """All-gather -> column-parallel GEMM: ``gather(x) @ w^T`` (SiLU-mul epilogue optional)."""
+        if not self.fused:
+            full = self._gather_cpu(x)
+            return ops.linear_silu_mul(full, w) if silu_mul else ops.linear(full, w)
+        c = ops.cuda_ops()
+        return c.gemm_ag(self.xs_local[x.parity], self.xs_maps[x.parity], self.xsflag_ptrs, self.xsflag_local,
+                         x.S, x.T, w, 1 if silu_mul else 0)
+
+    def sp_row_parallel_norm(self, y: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor,
+                             eps: float, zero_centered: bool, T: int, S: int) -> ShardedActivation:
+        """Row-parallel GEMM -> reduce-scatter -> ``residual += ...`` -> RMSNorm, on this rank's token rows.
+
+        ``y`` is ``[T, in/W]`` (all tokens), ``residual`` this rank's shard ``[rows, H]``.
+        """
+        lo, hi = self.sp_range(T, S)
+        if not self.fused:
+            full = ops.linear(y, w)
+            dist.all_reduce(full, group=self.group)
+            x = ops.add_rmsnorm(full[lo:hi].contiguous(), residual, norm_w, eps, zero_centered)
+            return ShardedActivation(self, x, T, S, 0)
+        c = ops.cuda_ops()
+        s = self.sp_set
+        self.sp_set ^= 1
+        c.tp_gemm_accum(y, w, self.spacc_local[s], self.spgflag_local, self.spgdone, 1)
+        c.sp_rs_norm(self.spacc_ptrs[s], self.spgflag_ptrs, self.spgflag_local, residual, norm_w, self.xs_local[s],
+                     lo, eps, zero_centered, self.spdone, self.xsflag_local)
+        return ShardedActivation(self, self.xs_local[s][: hi - lo], T, S, s)
+
+    def sp_gather(self, x: ShardedActivation) -> torch.Tensor:
+        """All rows ``[T, H]`` of a token-sharded activation on every rank."""
+        if not self.fused:
+            return self._gather_cpu(x)
+        return ops.cuda_ops().sp_gather(self.xs_ptrs[x.parity], self.xsflag_ptrs, self.xsflag_local, x.S, x.T,
+                                        x.local.shape[1], x.local)
+
+    def _gather_cpu(self, x: ShardedActivation) -> torch.Tensor:
+        h = x.local.shape[1]
+        pad = torch.zeros(x.S, h, dtype=x.local.dtype, device=x.local.device)
+        pad[: x.local.shape[0]] = x.local
+        parts = [torch.empty_like(pad) for _ in range(self.world)]
+        dist.all_gather(parts, pad, group=self.group)
+        return torch.cat(parts)[: x.T].contiguous()
 
     def lm_head_sample(self, hidden: torch.Tensor, w_local: torch.Tensor, temperatures: torch.Tensor,
                        rng: torch.Tensor, vocab_start: int) -> torch.Tensor:

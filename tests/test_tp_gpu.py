@@ -47,3 +47,27 @@ def test_tp2_matches_tp1(ckpt, eager):
         llm.exit()
     agree = sum(a == b for x, y in zip(*outs) for a, b in zip(x[:4], y[:4]))
     assert agree >= 10, outs
+
+
+def test_tp2_token_sharded_prefill(ckpt, monkeypatch):
+    """Prefill chunks above the fused-row limit run token-sharded: reduce-scatter + residual +
+    RMSNorm on each rank's rows (``sp_rs_norm``) and the all-gather fused into every
+    column-parallel GEMM's operand loads (``gemm_ag``).  Tokens must agree with TP=1 and with
+    the replicated TP=2 path."""
+    from inference_systems_b200.llm import LLM
+
+    d, cfg = ckpt
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in (300, 257, 333)]
+    sp = SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True)
+    outs = []
+    for tp, sharded in ((1, "0"), (2, "0"), (2, "1")):
+        monkeypatch.setenv("ISB_TP_SP", sharded)
+        llm = LLM(d, device="cuda", tensor_parallel_size=tp, max_num_seqs=4, max_num_state_slots=4,
+                  max_model_len=512, num_kvcache_blocks=16, enforce_eager=True, dist_port=_free_port())
+        outs.append([o["token_ids"] for o in llm.generate(prompts, sp, use_tqdm=False)])
+        llm.exit()
+        assert torch.ops.isb.error_word() == 0
+    agree_tp1 = sum(a == b for x, y in zip(outs[0], outs[2]) for a, b in zip(x[:4], y[:4]))
+    agree_rep = sum(a == b for x, y in zip(outs[1], outs[2]) for a, b in zip(x[:4], y[:4]))
+    assert agree_tp1 >= 10 and agree_rep >= 10, outs
