@@ -288,6 +288,8 @@ def tp_bench(batches=(1, 8, 128)) -> None:
                      "nccl_baseline_us": round(base, 2), "local_gemm_us": round(local_gemm, 2),
                      "local_add_norm_us": round(local_norm, 2), "roofline_us": round(roof, 2),
                      "fraction_of_roofline": round(roof / fused, 3)})
+        if rank == 0:
+            print(json.dumps(rows[-1]), flush=True)
         if cm is not comm:
             cm.close()
     for b in batches:
@@ -300,9 +302,46 @@ def tp_bench(batches=(1, 8, 128)) -> None:
         rows.append({"path": "vocab-parallel LM head -> cross-rank argmax", "tp": world, "batch": b,
                      "fused_us": round(fused, 2), "roofline_us": round(roof, 2),
                      "fraction_of_roofline": round(roof / fused, 3)})
-    if rank == 0:
-        for r in rows:
-            print(json.dumps(r), flush=True)
+        if rank == 0:
+            print(json.dumps(rows[-1]), flush=True)
+    # token-sharded prefill chunk: row-parallel GEMM -> reduce-scatter + residual + RMSNorm ->
+    # all-gather fused into the next column-parallel GEMM (MLP down, then gate_up + SiLU)
+    os.environ["ISB_TP_SP"] = "1"
+    for hh, full_inter, T in ((1024, 3584, 2048), (5120, 17408, 2048)):
+        ii = full_inter // world
+        cm = TPComm(dev, rank, world, hh, None, max_rows=256)
+        S = cm.sp_rows(T)
+        lo, hi = cm.sp_range(T, S)
+        wd = (torch.randn(hh, ii, device=dev, generator=g) * 0.02).to(bf)
+        wgu = (torch.randn(2 * ii, hh, device=dev, generator=g) * 0.02).to(bf)
+        nwd = torch.zeros(hh, device=dev).to(bf)
+        y = torch.randn(T, ii, device=dev, generator=g).to(bf)
+        res_shard = torch.randn(hi - lo, hh, device=dev, generator=g).to(bf)
+        res_full = torch.randn(T, hh, device=dev, generator=g).to(bf)
+
+        def sp_path():
+            x = cm.sp_row_parallel_norm(y, wd, res_shard, nwd, 1e-6, True, T, S)
+            return cm.sp_linear(x, wgu, True)
+
+        def nccl_path2():
+            z = ops.linear(y, wd)
+            dist.all_reduce(z)
+            x = ops.add_rmsnorm(z, res_full, nwd, 1e-6, True)
+            return ops.linear_silu_mul(x, wgu)
+
+        fused = timed(sp_path, calls=4)
+        base = timed(nccl_path2, calls=4)
+        flops = 2 * T * ii * hh + 2 * T * hh * 2 * ii
+        link = ((world - 1) * (T / world) * hh * 4 + (world - 1) / world * T * hh * 2) / (nvlink * 1e9) * 1e6
+        wbytes = (hh * ii + 2 * ii * hh) * 2
+        roof = max(flops / (tflops * 1e12) * 1e6, link, wbytes / (hbm * 1e9) * 1e6)
+        rows.append({"path": "row GEMM -> reduce-scatter + residual + RMSNorm -> all-gather fused into gate_up GEMM",
+                     "tp": world, "tokens": T, "hidden": hh, "inter_per_rank": ii, "shard_rows": S,
+                     "fused_us": round(fused, 2), "nccl_baseline_us": round(base, 2), "roofline_us": round(roof, 2),
+                     "fraction_of_roofline": round(roof / fused, 3)})
+        if rank == 0:
+            print(json.dumps(rows[-1]), flush=True)
+        cm.close()
     comm.close()
     dist.barrier()
     dist.destroy_process_group()
