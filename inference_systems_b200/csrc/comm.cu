@@ -117,11 +117,14 @@ __device__ __forceinline__ bool wait_all_ranks(const unsigned long long* flags, 
   return ok != 0;
 }
 
-// out_row = RMSNorm(res_row + sum_r accs[r][acc_row]); res_row is updated in place.
+// out_row = RMSNorm(res_row + sum_r accs[r][acc_row]); res_row is updated in place.  With ``outs``
+// (nout buffer bases, peer memory included) the row is written to row ``acc_row`` of every one of
+// them instead of to ``out``.
 __device__ __forceinline__ void pull_add_norm_row(const unsigned long long* __restrict__ accs, int world, bool ok,
                                                   size_t acc_row, __nv_bfloat16* __restrict__ res,
                                                   const __nv_bfloat16* __restrict__ w,
-                                                  __nv_bfloat16* __restrict__ out, int H, float eps, bool zc) {
+                                                  __nv_bfloat16* __restrict__ out, int H, float eps, bool zc,
+                                                  const unsigned long long* outs = nullptr, int nout = 0) {
   __shared__ float red[32];
   const int tid = threadIdx.x, nt = blockDim.x;
   const float* peer[kMaxWorld];
@@ -174,7 +177,11 @@ __device__ __forceinline__ void pull_add_norm_row(const unsigned long long* __re
 #pragma unroll
     for (int i = 0; i < 8; ++i)
       y[i] = zc ? v[k][i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[k][i] * rs)) * wv.v[i];
-    store8(out + c, y);
+    if (outs == nullptr) {
+      store8(out + c, y);
+    } else {
+      for (int r = 0; r < nout; ++r) store8(reinterpret_cast<__nv_bfloat16*>(outs[r]) + acc_row * H + c, y);
+    }
   }
 }
 
@@ -214,46 +221,51 @@ __device__ __forceinline__ void finish_and_release(unsigned int* done_ctr, unsig
   }
 }
 
-// Token-sharded (sequence-parallel) reduce-scatter + residual + RMSNorm: rank r owns rows
-// [row_base, row_base + rows) of the T tokens.  Each CTA pulls one of those rows from every
-// rank's fp32 partial product (after every rank's row-parallel GEMM counter has caught up with
-// this rank's), adds the shard's residual row, and writes the normalised row into this rank's
-// shard buffer, which peers read in their all-gather GEMMs once ``*ready`` has moved on.
+// Token-sharded (sequence-parallel) reduce-scatter + residual + RMSNorm + all-gather: rank r
+// owns rows [row_base, row_base + rows) of the T tokens.  Each CTA pulls one of those rows from
+// every rank's fp32 partial product (after every rank's row-parallel GEMM counter has caught up
+// with this rank's), adds the shard's residual row, and pushes the normalised row into row
+// (row_base + row) of every rank's full activation buffer (``xf``, peer memory), so each remote
+// row crosses NVLink once; peers' GEMMs read it from their own memory once ``*ready`` has moved on.
 __global__ void __launch_bounds__(512) sp_rs_norm_kernel(const unsigned long long* __restrict__ accs,
                                                          const unsigned long long* gflags,
                                                          const unsigned int* my_gflag, int world,
                                                          __nv_bfloat16* __restrict__ residual,
                                                          const __nv_bfloat16* __restrict__ w,
-                                                         __nv_bfloat16* __restrict__ xs, int rows, int row_base, int H,
-                                                         float eps, bool zc, unsigned int* done_ctr,
-                                                         unsigned int* ready) {
+                                                         const unsigned long long* __restrict__ xf, int rows,
+                                                         int row_base, int H, float eps, bool zc,
+                                                         unsigned int* done_ctr, unsigned int* ready) {
   pdl_trigger();
   pdl_wait();
   const bool ok = wait_all_ranks(gflags, my_gflag, world);
   const int row = blockIdx.x;
   if (row < rows)
-    pull_add_norm_row(accs, world, ok, size_t(row_base + row), residual + size_t(row) * H, w, xs + size_t(row) * H,
-                      H, eps, zc);
+    pull_add_norm_row(accs, world, ok, size_t(row_base + row), residual + size_t(row) * H, w, nullptr, H, eps, zc,
+                      xf, world);
   finish_and_release(done_ctr, ready);
 }
 
-// Copy this rank's first normalised shard (embedding + first RMSNorm) into its shard buffer
-// and release ``*ready``.
+// Push this rank's first normalised shard (embedding + first RMSNorm) into rows
+// [row_base, row_base + rows) of every rank's full activation buffer and release ``*ready``.
 __global__ void __launch_bounds__(256) sp_publish_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         __nv_bfloat16* __restrict__ xs, int rows, int H,
-                                                         unsigned int* done_ctr, unsigned int* ready) {
+                                                         const unsigned long long* __restrict__ xf, int world,
+                                                         int rows, int row_base, int H, unsigned int* done_ctr,
+                                                         unsigned int* ready) {
   pdl_trigger();
   pdl_wait();
   const int row = blockIdx.x;
   if (row < rows)
-    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8)
-      *reinterpret_cast<uint4*>(xs + size_t(row) * H + c) = *reinterpret_cast<const uint4*>(x + size_t(row) * H + c);
+    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(x + size_t(row) * H + c);
+      for (int r = 0; r < world; ++r)
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xf[r]) + size_t(row_base + row) * H + c) = v;
+    }
   finish_and_release(done_ctr, ready);
 }
 
-// out[t] = row t of the token-sharded activation (owner t / S, its row t % S), read from the
-// owner's shard buffer once the owner's counter has reached this rank's.
-__global__ void __launch_bounds__(256) sp_gather_kernel(const unsigned long long* __restrict__ xs,
+// out[t] = row t of this rank's full activation buffer, once its owner (t / S) has pushed it
+// (the owner's counter has reached this rank's).
+__global__ void __launch_bounds__(256) sp_gather_kernel(const __nv_bfloat16* __restrict__ xf,
                                                         const unsigned long long* flags, const unsigned int* my_flag,
                                                         int S, int H, __nv_bfloat16* __restrict__ out) {
   pdl_trigger();
@@ -265,10 +277,9 @@ __global__ void __launch_bounds__(256) sp_gather_kernel(const unsigned long long
     ok = wait_counters(flags + owner, 1, target) ? 1 : 0;
   }
   __syncthreads();
-  const __nv_bfloat16* src = reinterpret_cast<const __nv_bfloat16*>(xs[owner]) + size_t(t - owner * S) * H;
   for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
     uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (ok) v = __ldcv(reinterpret_cast<const uint4*>(src + c));
+    if (ok) v = __ldcv(reinterpret_cast<const uint4*>(xf + size_t(t) * H + c));
     *reinterpret_cast<uint4*>(out + size_t(t) * H + c) = v;
   }
 }
@@ -382,40 +393,47 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
 }
 
 // ---------------------------------------------------------------- sequence-parallel (token-sharded) path
+// ``xf``: int64 [W] device addresses of every rank's full activation buffer (>= row_base + rows
+// rows of H bf16 each; the caller sizes them).
 void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
-                const at::Tensor& w, at::Tensor xs, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
+                const at::Tensor& w, const at::Tensor& xf, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
                 at::Tensor ready) {
   TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16 && residual.dim() == 2,
               "residual shard: contiguous bf16 [rows, H]");
   const int rows = residual.size(0), H = residual.size(1);
-  TORCH_CHECK(H % 8 == 0 && H <= 16384 && xs.size(-1) == H && xs.numel() >= int64_t(rows) * H, "shard buffer shape");
-  TORCH_CHECK(gflags.numel() <= kMaxWorld && accs.numel() == gflags.numel(), "one accumulator and counter per rank");
+  TORCH_CHECK(H % 8 == 0 && H <= 16384, "hidden size must be a multiple of 8 and at most 16384");
+  TORCH_CHECK(gflags.numel() <= kMaxWorld && accs.numel() == gflags.numel() && xf.numel() == gflags.numel(),
+              "one accumulator, counter and activation buffer per rank");
   const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
   launch_pdl(sp_rs_norm_kernel, dim3(std::max(rows, 1)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()),
              reinterpret_cast<const unsigned long long*>(gflags.data_ptr<int64_t>()),
              reinterpret_cast<const unsigned int*>(my_gflag.data_ptr<int>()), int(gflags.numel()),
              reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()), rows, int(row_base), H, float(eps), zc,
+             reinterpret_cast<const unsigned long long*>(xf.data_ptr<int64_t>()), rows, int(row_base), H, float(eps), zc,
              reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
 }
 
-void sp_publish(const at::Tensor& x, at::Tensor xs, at::Tensor done_ctr, at::Tensor ready) {
+void sp_publish(const at::Tensor& x, const at::Tensor& xf, int64_t row_base, at::Tensor done_ctr, at::Tensor ready) {
   TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "x: contiguous bf16 [rows, H]");
   const int rows = x.size(0), H = x.size(1);
-  TORCH_CHECK(H % 8 == 0 && xs.size(-1) == H && xs.numel() >= int64_t(rows) * H, "shard buffer shape");
+  TORCH_CHECK(H % 8 == 0 && xf.numel() <= kMaxWorld, "hidden size a multiple of 8, at most 8 ranks");
   launch_pdl(sp_publish_kernel, dim3(std::max(rows, 1)), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), reinterpret_cast<__nv_bfloat16*>(xs.data_ptr()), rows,
+             reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+             reinterpret_cast<const unsigned long long*>(xf.data_ptr<int64_t>()), int(xf.numel()), rows, int(row_base),
              H, reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
 }
 
-at::Tensor sp_gather(const at::Tensor& xs_ptrs, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
-                     int64_t T, int64_t H, const at::Tensor& like) {
+at::Tensor sp_gather(const at::Tensor& xf_local, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
+                     int64_t T) {
+  TORCH_CHECK(xf_local.is_contiguous() && xf_local.scalar_type() == at::kBFloat16 && xf_local.dim() == 2 &&
+                  xf_local.size(0) >= T, "local activation buffer [>= T, H] bf16");
+  const int64_t H = xf_local.size(1);
   TORCH_CHECK(H % 8 == 0 && S > 0 && T <= S * flags.numel(), "gather shape");
-  at::Tensor out = at::empty({T, H}, like.options().dtype(at::kBFloat16));
+  at::Tensor out = at::empty({T, H}, xf_local.options());
   if (T == 0) return out;
   launch_pdl(sp_gather_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const unsigned long long*>(xs_ptrs.data_ptr<int64_t>()),
+             reinterpret_cast<const __nv_bfloat16*>(xf_local.data_ptr()),
              reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()),
              reinterpret_cast<const unsigned int*>(my_flag.data_ptr<int>()), int(S), int(H),
              reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));

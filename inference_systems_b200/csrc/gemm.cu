@@ -79,10 +79,11 @@ struct GemmArgs {
   // is in ``acc`` (tensor-parallel peers poll it before reading this rank's accumulator)
   unsigned int* signal;
   // All-gather operand (non-swap path only): the activation rows are token-sharded over the
-  // tensor-parallel ranks, ``ag_rows`` rows per rank (a multiple of BM), each rank's shard in its
-  // own symmetric buffer described by ``ag_maps[rank]`` (tensor maps in device memory).  The M
-  // tile at row m*BM is read from rank m*BM / ag_rows once that rank's shard counter
-  // (``ag_flags[rank]``, peer memory) has reached this rank's own counter ``*ag_own``.
+  // tensor-parallel ranks, ``ag_rows`` rows per rank (a multiple of BM).  The M tile at row
+  // m*BM belongs to rank m*BM / ag_rows and is read once that rank's counter (``ag_flags[rank]``,
+  // peer memory) has reached this rank's own counter ``*ag_own``: from the owner's own shard
+  // buffer through ``ag_maps[rank]`` (tensor maps in device memory) when ``ag_maps`` is set,
+  // else from row m*BM of the local buffer behind ``tmP``, into which every owner pushed its rows.
   const CUtensorMap* ag_maps;
   const unsigned long long* ag_flags;
   const unsigned int* ag_own;
@@ -206,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const CUtensorMap* x_map = &tmP;
       int x_row = tile_p * BM;
       if constexpr (!SWAP) {
-        if (args.ag_maps != nullptr) {
+        if (args.ag_maps != nullptr && args.ag_flags != nullptr) {
           const int owner = (tile_p * BM) / args.ag_rows;
           x_map = args.ag_maps + owner;
           x_row = tile_p * BM - owner * args.ag_rows;
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       pdl_wait();
       if constexpr (!SWAP) {
-        if (args.ag_maps != nullptr) {
+        if (args.ag_flags != nullptr) {
           // the owner's shard of this call is published once its counter reaches ours (every
           // rank publishes once per call); bounded wait
           const int owner = (tile_p * BM) / args.ag_rows;
@@ -980,13 +981,6 @@ static CUtensorMap make_store_map(const void* ptr, int64_t rows, int64_t cols, i
   return m;
 }
 
-static int pick_bn_swap(int tokens) {
-  if (tokens <= 16) return 16;
-  if (tokens <= 32) return 32;
-  if (tokens <= 64) return 64;
-  return 128;
-}
-
 static int num_sms() {
   static int n = 0;
   if (!n) {
@@ -995,6 +989,29 @@ static int num_sms() {
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
   }
   return n;
+}
+
+// ISB_GEMM_SWAP_HALVE=0 keeps one token tile per weight tile for 65..128 tokens.
+static bool swap_halve_enabled() {
+  static const bool on = [] {
+    const char* e = std::getenv("ISB_GEMM_SWAP_HALVE");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Token tile of a swap-AB GEMM.  For the store and SiLU-mul GEMMs with 65..128 tokens and fewer
+// than half as many weight tiles as SMs, two 64-token tiles per weight tile put twice as many SMs
+// to work (the tensor-core time of one 128-token tile, not the weight stream, bounds such a CTA;
+// the second read of a weight tile mostly hits L2): gate_up + SiLU at 128 tokens 16.2 -> 12.1 us,
+// qkv 8.2 -> 7.6 us.  The split-K accumulating GEMMs keep 128-token tiles (halving them costs
+// K splits: down 10.2 -> 13.1 us).
+static int pick_bn_swap(int tokens, int weight_tiles = 1 << 30) {
+  if (tokens <= 16) return 16;
+  if (tokens <= 32) return 32;
+  if (tokens <= 64) return 64;
+  if (swap_halve_enabled() && 2 * weight_tiles <= num_sms()) return 64;
+  return 128;
 }
 
 // Split-K factor: grow while the grid stays within ~1.5 waves and every split keeps >= 2 k-blocks.
@@ -1036,14 +1053,15 @@ struct Plan {
   CUtensorMap tp, tq;
 };
 
-static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split, int force_splits = 0) {
+static Plan plan_gemm(const at::Tensor& a, const at::Tensor& b, bool allow_split, int force_splits = 0,
+                      bool halve_tokens = false) {
   const int M = a.size(0), K = a.size(1), N = b.size(0);
   Plan p;
   p.swap = M <= 128;
   const int kb_total = (K + BK - 1) / BK;
   if (p.swap) {
-    p.bn = pick_bn_swap(M);
     p.tiles_p = (N + BM - 1) / BM;
+    p.bn = halve_tokens ? pick_bn_swap(M, p.tiles_p) : pick_bn_swap(M);
     p.tiles_q = (M + p.bn - 1) / p.bn;
     p.tp = make_kmajor_map(b.data_ptr(), N, K, BM);
     p.tq = make_kmajor_map(a.data_ptr(), M, K, p.bn);
@@ -1077,7 +1095,7 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
                      unsigned long long* dbg) {
   const int M = a.size(0), N = b.size(0);
   const int out_cols = out.size(1);
-  Plan p = plan_gemm(a, b, false, force_splits);
+  Plan p = plan_gemm(a, b, false, force_splits, /*halve_tokens=*/force_splits == 0);
   const int kb_total = (int(a.size(1)) + BK - 1) / BK;
   // two CTAs per weight tile (split K over a cluster pair) when the doubled grid still fits in a
   // wave and the token tile is narrow (measured: a win up to 32 tokens, a loss at 128, where
@@ -1217,17 +1235,22 @@ at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, co
   return out;
 }
 
-// out[T, N] (or [T, N/2] for the SiLU-mul epilogue) = gather_rows(shards)[T, K] . b[N, K]^T, the
-// activation rows read straight from their owners' shard buffers (see GemmArgs::ag_maps).
-// ``local`` is this rank's shard buffer [shard_rows, K] (gives the K extent and a valid default
-// map); ``flags`` (int64 [W], device) are the ranks' shard counters; ``own`` is this rank's.
+// out[T, N] (or [T, N/2] for the SiLU-mul epilogue) = gather_rows(shards)[T, K] . b[N, K]^T; each
+// M tile waits for its owner's counter (see GemmArgs::ag_flags).  With ``maps`` (one tensor map per
+// rank) the rows are read from the owners' shard buffers and ``local`` is this rank's shard buffer
+// [>= shard_rows, K]; with an empty ``maps`` every owner has pushed its rows into ``local``
+// [>= T, K] at their token positions and the GEMM reads only local memory (a remote tile crosses
+// NVLink once instead of once per column tile).  ``flags`` (int64 [W], device) are the ranks'
+// counters, ``own`` this rank's.
 at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
                    int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue) {
   check_operands(local, b);
   const int K = local.size(1), N = b.size(0);
   const int W = flags.numel();
-  TORCH_CHECK(maps.numel() == int64_t(W) * int64_t(sizeof(CUtensorMap)), "one tensor map per rank");
-  TORCH_CHECK(shard_rows % BM == 0 && shard_rows <= local.size(0) && T > BM && T <= int64_t(W) * shard_rows,
+  const bool peer_maps = maps.numel() > 0;
+  TORCH_CHECK(!peer_maps || maps.numel() == int64_t(W) * int64_t(sizeof(CUtensorMap)), "one tensor map per rank");
+  TORCH_CHECK(shard_rows % BM == 0 && T > BM && T <= int64_t(W) * shard_rows &&
+                  (peer_maps ? shard_rows <= local.size(0) : T <= local.size(0)),
               "all-gather GEMM: shard rows a multiple of 128 within the buffer, 128 < T <= ranks * shard rows");
   TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm_ag: unknown epilogue");
   at::Tensor out = at::empty({T, epilogue == kSiluMul ? N / 2 : N}, b.options());
@@ -1239,7 +1262,7 @@ at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Te
   args.kb_per_split = kb_total;
   args.P_rows = int(T);
   args.Q_rows = N;
-  args.ag_maps = reinterpret_cast<const CUtensorMap*>(maps.data_ptr());
+  args.ag_maps = peer_maps ? reinterpret_cast<const CUtensorMap*>(maps.data_ptr()) : nullptr;
   args.ag_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
   args.ag_own = reinterpret_cast<const unsigned int*>(own.data_ptr<int>());
   args.ag_rows = int(shard_rows);

@@ -81,11 +81,11 @@ at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, co
 at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
                    int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue);
 void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
-                const at::Tensor& w, at::Tensor xs, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
+                const at::Tensor& w, const at::Tensor& xf, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
                 at::Tensor ready);
-void sp_publish(const at::Tensor& x, at::Tensor xs, at::Tensor done_ctr, at::Tensor ready);
-at::Tensor sp_gather(const at::Tensor& xs_ptrs, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
-                     int64_t T, int64_t H, const at::Tensor& like);
+void sp_publish(const at::Tensor& x, const at::Tensor& xf, int64_t row_base, at::Tensor done_ctr, at::Tensor ready);
+at::Tensor sp_gather(const at::Tensor& xf_local, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
+                     int64_t T);
 
 int64_t error_word() {
   return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24) |
@@ -131,10 +131,10 @@ TORCH_LIBRARY(isb, m) {
   m.def("gemm_ag(Tensor local, Tensor maps, Tensor flags, Tensor own, int shard_rows, int T, Tensor b, int epilogue) "
         "-> Tensor");
   m.def(
-      "sp_rs_norm(Tensor accs, Tensor gflags, Tensor my_gflag, Tensor(a!) residual, Tensor w, Tensor(b!) xs, "
+      "sp_rs_norm(Tensor accs, Tensor gflags, Tensor my_gflag, Tensor(a!) residual, Tensor w, Tensor xf, "
       "int row_base, float eps, bool zc, Tensor(c!) done_ctr, Tensor(d!) ready) -> ()");
-  m.def("sp_publish(Tensor x, Tensor(a!) xs, Tensor(b!) done_ctr, Tensor(c!) ready) -> ()");
-  m.def("sp_gather(Tensor xs_ptrs, Tensor flags, Tensor my_flag, int S, int T, int H, Tensor like) -> Tensor");
+  m.def("sp_publish(Tensor x, Tensor xf, int row_base, Tensor(b!) done_ctr, Tensor(c!) ready) -> ()");
+  m.def("sp_gather(Tensor xf_local, Tensor flags, Tensor my_flag, int S, int T) -> Tensor");
   m.def(
       "attention_decode_tc(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");

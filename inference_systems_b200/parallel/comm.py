@@ -22,12 +22,13 @@ Here, on GPUs:
 * Prefill chunks larger than ``max_rows`` tokens run token-sharded (sequence
   parallel within the TP group) when ``sp_rows`` allows: the residual stream is
   split by tokens; each row-parallel GEMM stores its fp32 partial product and
-  ``sp_rs_norm`` (reduce-scatter + residual + RMSNorm) pulls only this rank's
-  token rows from every peer and publishes the normalised shard; the next
-  column-parallel GEMM (``gemm_ag``) reads every M tile straight from the
-  owning rank's shard buffer (all-gather fused into the GEMM's operand loads).
-  Per layer a rank moves ``(W-1)/W * T/W * H`` fp32 values in and
-  ``(W-1)/W * T * H`` bf16 values through its GEMM, instead of all-reducing
+  ``sp_rs_norm`` (reduce-scatter + residual + RMSNorm + all-gather) pulls only
+  this rank's token rows from every peer, normalises them and pushes them into
+  every rank's full activation buffer; the next column-parallel GEMM
+  (``gemm_ag``) waits, per 128-row M tile, for the owning rank's counter and
+  reads the tile from its own memory (a remote row crosses NVLink once, not
+  once per column tile).  Per layer a rank pulls ``(W-1)/W * T/W * H`` fp32
+  values and pushes ``(W-1) * T/W * H`` bf16 values, instead of all-reducing
   ``T * H``.  Otherwise larger chunks use NCCL all-reduce.
 
 On CPU (gloo process groups, used by the tests) the same methods run with
@@ -93,7 +94,6 @@ class TPComm:
         self.sp = os.environ.get("ISB_TP_SP", "0") == "1" and world > 1
         tokens = getattr(config, "max_num_batched_tokens", 8192) if config is not None else 8192
         self.max_sp_rows = min(int(tokens), 16384) if self.sp else 0
-        self.sp_shard_max = self._shard_rows(self.max_sp_rows) if self.sp else 0
         self.sp_set = 0
         if self.fused:
             self._setup_symmetric()
@@ -108,7 +108,7 @@ class TPComm:
                              ("accflag0", w * 4), ("accflag1", w * 4), ("gdone0", 4), ("gdone1", 4),
                              ("ndone0", 4), ("ndone1", 4), ("xbuf", w * self.max_sample_rows * 8), ("xflag", w * 4),
                              ("spacc0", self.max_sp_rows * h * 4), ("spacc1", self.max_sp_rows * h * 4),
-                             ("xs0", self.sp_shard_max * h * 2), ("xs1", self.sp_shard_max * h * 2),
+                             ("xf0", self.max_sp_rows * h * 2), ("xf1", self.max_sp_rows * h * 2),
                              ("spgflag", 4), ("spgdone", 4), ("xsflag", 4), ("spdone", 4)):
             layout[name] = off
             off += _align(nbytes)
@@ -146,15 +146,13 @@ class TPComm:
         self.xbuf_local = local("xbuf", torch.float32, w * self.max_sample_rows * 2)
         self.xflag_local = local("xflag", torch.int32, w)
         if self.sp:
-            c2 = ops.cuda_ops()
             self.spacc_ptrs = [table("spacc0"), table("spacc1")]
             self.spacc_local = [local(f"spacc{i}", torch.float32, self.max_sp_rows * h).view(self.max_sp_rows, h)
                                 for i in range(2)]
-            self.xs_local = [local(f"xs{i}", torch.bfloat16, self.sp_shard_max * h).view(self.sp_shard_max, h)
+            self.xf_local = [local(f"xf{i}", torch.bfloat16, self.max_sp_rows * h).view(self.max_sp_rows, h)
                              for i in range(2)]
-            self.xs_ptrs = [table("xs0"), table("xs1")]
-            self.xs_maps = [c2.ag_tensor_maps(torch.tensor([b + layout[f"xs{i}"] for b in bases], dtype=torch.int64),
-                                              self.sp_shard_max, h, self.region) for i in range(2)]
+            self.xf_ptrs = [table("xf0"), table("xf1")]
+            self.no_maps = torch.empty(0, dtype=torch.uint8, device=self.device)  # gemm_ag: read local rows
             self.spgflag_ptrs, self.spgflag_local = table("spgflag"), local("spgflag", torch.int32, 1)
             self.spgdone = local("spgdone", torch.int32, 1)
             self.xsflag_ptrs, self.xsflag_local = table("xsflag"), local("xsflag", torch.int32, 1)
@@ -208,8 +206,9 @@ class TPComm:
             return ShardedActivation(self, x, T, S, 0)
         q = self.sp_set
         self.sp_set ^= 1
-        ops.cuda_ops().sp_publish(x.contiguous(), self.xs_local[q], self.spdone, self.xsflag_local)
-        return ShardedActivation(self, self.xs_local[q][: x.shape[0]], T, S, q)
+        lo, hi = self.sp_range(T, S)
+        ops.cuda_ops().sp_publish(x.contiguous(), self.xf_ptrs[q], lo, self.spdone, self.xsflag_local)
+        return ShardedActivation(self, self.xf_local[q][lo:hi], T, S, q)
 
     def sp_linear(self, x: ShardedActivation, w: torch.Tensor, silu_mul: bool = False) -> torch.Tensor:
         """All-gather -> column-parallel GEMM: ``gather(x) @ w^T`` (SiLU-mul epilogue optional)."""
@@ -217,8 +216,8 @@ class TPComm:
             full = self._gather_cpu(x)
             return ops.linear_silu_mul(full, w) if silu_mul else ops.linear(full, w)
         c = ops.cuda_ops()
-        return c.gemm_ag(self.xs_local[x.parity], self.xs_maps[x.parity], self.xsflag_ptrs, self.xsflag_local,
-                         x.S, x.T, w, 1 if silu_mul else 0)
+        return c.gemm_ag(self.xf_local[x.parity], self.no_maps, self.xsflag_ptrs, self.xsflag_local, x.S, x.T, w,
+                         1 if silu_mul else 0)
 
     def sp_row_parallel_norm(self, y: torch.Tensor, w: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor,
                              eps: float, zero_centered: bool, T: int, S: int) -> ShardedActivation:
@@ -236,16 +235,15 @@ class TPComm:
         s = self.sp_set
         self.sp_set ^= 1
         c.tp_gemm_accum(y, w, self.spacc_local[s], self.spgflag_local, self.spgdone, 1)
-        c.sp_rs_norm(self.spacc_ptrs[s], self.spgflag_ptrs, self.spgflag_local, residual, norm_w, self.xs_local[s],
+        c.sp_rs_norm(self.spacc_ptrs[s], self.spgflag_ptrs, self.spgflag_local, residual, norm_w, self.xf_ptrs[s],
                      lo, eps, zero_centered, self.spdone, self.xsflag_local)
-        return ShardedActivation(self, self.xs_local[s][: hi - lo], T, S, s)
+        return ShardedActivation(self, self.xf_local[s][lo:hi], T, S, s)
 
     def sp_gather(self, x: ShardedActivation) -> torch.Tensor:
         """All rows ``[T, H]`` of a token-sharded activation on every rank."""
         if not self.fused:
             return self._gather_cpu(x)
-        return ops.cuda_ops().sp_gather(self.xs_ptrs[x.parity], self.xsflag_ptrs, self.xsflag_local, x.S, x.T,
-                                        x.local.shape[1], x.local)
+        return ops.cuda_ops().sp_gather(self.xf_local[x.parity], self.xsflag_ptrs, self.xsflag_local, x.S, x.T)
 
     def _gather_cpu(self, x: ShardedActivation) -> torch.Tensor:
         h = x.local.shape[1]
