@@ -1006,11 +1006,11 @@ static bool swap_halve_enabled() {
 // the second read of a weight tile mostly hits L2): gate_up + SiLU at 128 tokens 16.2 -> 12.1 us,
 // qkv 8.2 -> 7.6 us.  The split-K accumulating GEMMs keep 128-token tiles (halving them costs
 // K splits: down 10.2 -> 13.1 us).
-static int pick_bn_swap(int tokens, int weight_tiles = 1 << 30) {
+static int pick_bn_swap(int tokens, int weight_tiles = 0) {  // 0: keep one token tile
   if (tokens <= 16) return 16;
   if (tokens <= 32) return 32;
   if (tokens <= 64) return 64;
-  if (swap_halve_enabled() && 2 * weight_tiles <= num_sms()) return 64;
+  if (swap_halve_enabled() && weight_tiles > 0 && 2 * weight_tiles <= num_sms()) return 64;
   return 128;
 }
 
