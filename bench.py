@@ -54,6 +54,8 @@ def parse():
                    help="profile one prefill step of --batch prompts of --prompt-len tokens (kernel-time shares) and exit")
     p.add_argument("--breakdown", action="store_true",
                    help="after timing, profile 3 decode-graph replays with torch.profiler (kernel-time shares)")
+    p.add_argument("--breakdown-dir", default="breakdowns",
+                   help="folder (relative to the repository) for the --breakdown / --prefill-breakdown tables")
     return p.parse_args()
 
 
@@ -73,6 +75,7 @@ def kernel_breakdown(replay, path: str, n: int = 3) -> None:
             agg.setdefault(ev.name, []).append(ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total)
     total = sum(sum(v) for v in agg.values())
     rows = sorted(agg.items(), key=lambda kv: -sum(kv[1]))
+    os.makedirs(os.path.dirname(path), exist_ok=True)
     with open(path, "w") as f:
         f.write(f"total device us per replay: {total / n:.1f}\n")
         for name, v in rows:
@@ -244,7 +247,7 @@ def prefill_breakdown(args) -> None:
             continue
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        kernel_breakdown(lambda: llm.step(), os.path.join(ROOT, "gpurun_out", f"prefill_b{b}_len{args.prompt_len}.txt"), n=1)
+        kernel_breakdown(lambda: llm.step(), os.path.join(ROOT, args.breakdown_dir, f"prefill_b{b}_len{args.prompt_len}.txt"), n=1)
         print(json.dumps({"prefill_step_s": round(time.perf_counter() - t0, 4), "batch": b,
                           "prompt_len": args.prompt_len}), flush=True)
         while not llm.is_finished():
@@ -277,7 +280,7 @@ def run_isb(args, rank: int, world: int) -> dict | None:
     launches = runner.graph_kernel_count(args.batch)
     if args.breakdown:
         g = runner.graphs[runner._graph_bucket(args.batch)]
-        kernel_breakdown(g.replay, os.path.join(ROOT, "gpurun_out", f"breakdown_tp{world}_b{args.batch}.txt"))
+        kernel_breakdown(g.replay, os.path.join(ROOT, args.breakdown_dir, f"breakdown_tp{world}_b{args.batch}.txt"))
     out = {
         "metric": METRIC,
         "value": head["value"],
@@ -378,7 +381,7 @@ def run_mtp(args, rank: int, world: int) -> dict | None:
             if args.breakdown:
                 drv = llm.model_runner.mtp_driver
                 kernel_breakdown(drv.graphs[drv._bucket(args.batch)].replay,
-                                 os.path.join(ROOT, "gpurun_out", f"breakdown_mtp{args.mtp}_b{args.batch}.txt"))
+                                 os.path.join(ROOT, args.breakdown_dir, f"breakdown_mtp{args.mtp}_b{args.batch}.txt"))
         llm.exit()
     if rank > 0:
         return None
