@@ -5,7 +5,7 @@
 For N > 1 the script is launched once per GPU by ``torch.distributed.run``;
 rank 0 drives the engine, the other ranks serve it (tensor parallelism).
 
-Workload: random-init Qwen3.5-0.8B-shape weights (bf16,
+Workload (the 0.8B decode configuration): random-init Qwen3.5-0.8B-shape weights (bf16,
 fp32 GDN state), ``--batch`` prompts of 512 uniform-random tokens, greedy
 decoding with CUDA-graph decode steps.
 
@@ -48,7 +48,7 @@ def parse():
     p.add_argument("--impl", default="isb", choices=["isb", "reference"])
     p.add_argument("--model", default=MODEL)
     p.add_argument("--mtp", type=int, default=0,
-                   help="K > 0: MTP speculative decode with K drafts vs target-only (BASELINE config 3)")
+                   help="K > 0: MTP speculative decode with K drafts vs target-only")
     p.add_argument("--mtp-accept", type=float, default=0.6, help="seeded draft/target agreement probability")
     p.add_argument("--prefill-breakdown", action="store_true",
                    help="profile one prefill step of --batch prompts of --prompt-len tokens (kernel-time shares) and exit")
@@ -316,7 +316,7 @@ def run_isb(args, rank: int, world: int) -> dict | None:
     return out
 
 
-# ------------------------------------------------------------ MTP (config 3)
+# ------------------------------------------------------------ MTP speculative decoding
 def _decode_run(llm, cfg, b: int, args) -> dict:
     """B requests to completion; device-timed decode phase (after every first token)."""
     import torch

@@ -4,7 +4,7 @@
     python -m torch.distributed.run --nnodes=1 --nproc-per-node 8 --master-addr 127.0.0.1 \\
         --master-port 29600 bench_serving.py --gpus 8 --rate 32
 
-Workload: arrivals are a Poisson process at ``--rate``
+Workload (the online serving configuration): arrivals are a Poisson process at ``--rate``
 requests/s; prompt lengths are lognormal with median ``--prompt-median``
 (clipped to ``--prompt-max``); output lengths are lognormal with median
 ``--output-median``; a ``--prefix-share`` fraction of the requests starts with

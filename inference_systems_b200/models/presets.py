@@ -43,7 +43,7 @@ _QWEN35_COMMON = {
 }
 
 PRESETS: dict[str, dict[str, Any]] = {
-    # CPU oracle shape.
+    # the CPU oracle shape (4 layers, hidden 256)
     "tiny": {
         **_QWEN35_COMMON,
         "vocab_size": 1024,

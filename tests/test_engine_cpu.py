@@ -1,4 +1,4 @@
-"""CPU engine end to end against the stand-alone fp32 oracle (BASELINE config 1 and variants)."""
+"""CPU engine end to end against the stand-alone fp32 oracle (the tiny 4-layer shape and variants)."""
 
 import os
 
