@@ -293,7 +293,11 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   pdl_wait();
   const int h = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int ctx = ctx_lens[b];
-  const int chunks = (ctx + chunk - 1) / chunk;
+  int chunks = (ctx + chunk - 1) / chunk;
+  if (chunks > max_chunks) {  // context longer than the block table covers: combine what was computed
+    if (d == 0) atomicOr(&g_attn_err, 2u);
+    chunks = max_chunks;
+  }
   const size_t base = (size_t(b) * Hq + h) * max_chunks;
   float m = -INFINITY;
   for (int p = 0; p < chunks; ++p) m = fmaxf(m, part_ml[(base + p) * 2]);
@@ -683,9 +687,9 @@ __attribute__((visibility("default"))) size_t isb_attention_decode_noalloc_scrat
                                                                                          int head_dim,
                                                                                          int max_blocks) {
   if (batch <= 0 || num_q_heads <= 0 || head_dim <= 0 || max_blocks <= 0) return 0;
-  const int max_chunks = max_blocks * (isb::PAGE / isb::DCHUNK);
-  return isb::part_o_bytes(batch, num_q_heads, head_dim, max_chunks) +
-         size_t(batch) * num_q_heads * max_chunks * 2 * sizeof(float);
+  const size_t max_chunks = size_t(max_blocks) * (isb::PAGE / isb::DCHUNK);  // size_t: no int overflow
+  const size_t part_o = (size_t(batch) * num_q_heads * max_chunks * head_dim * sizeof(float) + 255) / 256 * 256;
+  return part_o + size_t(batch) * num_q_heads * max_chunks * 2 * sizeof(float);
 }
 
 __attribute__((visibility("default"))) int isb_noalloc_setup(void) {
@@ -700,6 +704,8 @@ __attribute__((visibility("default"))) int isb_attention_decode_noalloc(
     void* out, cudaStream_t stream) {
   if (batch <= 0 || num_q_heads <= 0 || num_kv_heads <= 0 || head_dim <= 0 || max_blocks <= 0)
     return ISB_NOALLOC_EINVAL;
+  // The decode grid has one z-slice per 64-token chunk and gridDim.z stops at 65535.
+  if (max_blocks > ISB_NOALLOC_MAX_BLOCKS || batch > 65535) return ISB_NOALLOC_EINVAL;
   // Size check first: it never touches a pointer.
   const size_t need = isb_attention_decode_noalloc_scratch_bytes(batch, num_q_heads, head_dim, max_blocks);
   if (need > ISB_NOALLOC_SCRATCH_BYTES) return ISB_NOALLOC_ETOOBIG;
@@ -710,6 +716,9 @@ __attribute__((visibility("default"))) int isb_attention_decode_noalloc(
   const bool hd128 = head_dim == 128 && (G == 1 || G == 2 || G == 4);
   if (!hd256 && !hd128) return ISB_NOALLOC_EUNSUPPORTED;
 
+  // An error left pending by earlier work of the caller stays theirs: report it without clearing it
+  // and launch nothing, so the check after the launches below covers only this call's kernels.
+  if (cudaPeekAtLastError() != cudaSuccess) return ISB_NOALLOC_EPENDING;
   int code = ISB_NOALLOC_OK;
   unsigned char* scratch = isb::noalloc_scratch(&code);
   if (scratch == nullptr) return code;
@@ -738,6 +747,14 @@ __attribute__((visibility("default"))) int isb_attention_decode_noalloc(
   return cudaGetLastError() == cudaSuccess ? ISB_NOALLOC_OK : ISB_NOALLOC_ELAUNCH;
 }
 
+__attribute__((visibility("default"))) unsigned int isb_noalloc_error_word(void) {
+  unsigned int v = 0;
+  if (cudaMemcpyFromSymbol(&v, isb::g_attn_err, sizeof(v)) != cudaSuccess) return 0xFFFFFFFFu;
+  const unsigned int z = 0;
+  cudaMemcpyToSymbol(isb::g_attn_err, &z, sizeof(z));
+  return v;
+}
+
 __attribute__((visibility("default"))) const char* isb_noalloc_strerror(int code) {
   switch (code) {
     case ISB_NOALLOC_OK: return "ok";
@@ -746,6 +763,7 @@ __attribute__((visibility("default"))) const char* isb_noalloc_strerror(int code
     case ISB_NOALLOC_EINVAL: return "null pointer or non-positive size";
     case ISB_NOALLOC_ESETUP: return "per-device set-up failed (cudaGetSymbolAddress or kernel attribute)";
     case ISB_NOALLOC_ELAUNCH: return "kernel launch failed";
+    case ISB_NOALLOC_EPENDING: return "a CUDA error from earlier work was pending; nothing was launched";
     default: return "unknown code";
   }
 }

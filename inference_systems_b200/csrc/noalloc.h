@@ -28,6 +28,8 @@ extern "C" {
 #endif
 
 #define ISB_NOALLOC_SCRATCH_BYTES (16u << 20)
+// Block-table width limit: one grid slice per 64-token chunk, at most 65535 slices.
+#define ISB_NOALLOC_MAX_BLOCKS (65535 / 4)
 
 enum {
   ISB_NOALLOC_OK = 0,
@@ -36,6 +38,8 @@ enum {
   ISB_NOALLOC_EINVAL = 3,       // null pointer or non-positive size
   ISB_NOALLOC_ESETUP = 4,       // symbol lookup or kernel attribute call failed
   ISB_NOALLOC_ELAUNCH = 5,      // kernel launch reported an error
+  ISB_NOALLOC_EPENDING = 6,     // a CUDA error from the caller's earlier work was pending (left
+                                // for the caller to read); nothing was launched
 };
 
 // Bytes of scratch one call with these sizes uses (partial outputs + softmax stats).
@@ -48,7 +52,10 @@ int isb_noalloc_setup(void);
 //   q            [batch, num_q_heads, head_dim] bf16 (normed, rotated)
 //   gate         [batch, num_q_heads * head_dim] bf16 sigmoid output gate, or NULL
 //   k_cache/v_cache [num_blocks, num_kv_heads, 256, head_dim] bf16
-//   ctx_lens     [batch] int32 tokens visible to each sequence (new token included)
+//   ctx_lens     [batch] int32 tokens visible to each sequence (new token included);
+//                each must be <= max_blocks * 256.  A longer context is cut to the
+//                block table's pages and sets 0x2 in the error word below.
+//                max_blocks <= ISB_NOALLOC_MAX_BLOCKS and batch <= 65535.
 //   block_tables [batch, max_blocks] int32 page ids
 //   out          [batch, num_q_heads * head_dim] bf16
 // head_dim 256 with 1, 2, 3, 4, 6 or 8 q heads per kv head, or head_dim 128
@@ -57,6 +64,13 @@ int isb_attention_decode_noalloc(const void* q, const void* gate, const void* k_
                                  const int* ctx_lens, const int* block_tables, int max_blocks, int batch,
                                  int num_q_heads, int num_kv_heads, int head_dim, float scale, void* out,
                                  cudaStream_t stream);
+
+// Device error word of the attention kernels, read and cleared (a synchronous copy on the
+// current device; it allocates nothing).  0x1: a bounded wait for a key/value copy ran
+// out; 0x2: a context was longer than its block table.  A nonzero word means the output
+// of the calls made since the last read is not valid.  The word is shared with the
+// library's PyTorch-facing attention ops on the same device.  0xFFFFFFFF: the read failed.
+unsigned int isb_noalloc_error_word(void);
 
 // Text for an ISB_NOALLOC_* code.
 const char* isb_noalloc_strerror(int code);

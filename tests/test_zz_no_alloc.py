@@ -33,6 +33,8 @@ def _lib():
     lib.isb_noalloc_strerror.restype = ctypes.c_char_p
     lib.isb_noalloc_strerror.argtypes = [ctypes.c_int]
     lib.isb_noalloc_setup.restype = ctypes.c_int
+    lib.isb_noalloc_error_word.restype = ctypes.c_uint
+    lib.isb_noalloc_error_word.argtypes = []
     return lib
 
 
@@ -75,13 +77,37 @@ def test_noalloc_decode_matches_allocating_entry_point():
         out = torch.full((b, hq * hd), float("nan"), device="cuda", dtype=torch.bfloat16)
         torch.cuda.synchronize()
         before = torch.cuda.memory_allocated()
+        free_before = torch.cuda.mem_get_info()[0]
         code = _call(lib, q, gate if gated else None, kc, vc, cl, bt, scale, out)
         torch.cuda.synchronize()
         assert code == OK, lib.isb_noalloc_strerror(code).decode()
         assert torch.cuda.memory_allocated() == before
+        # a cudaMalloc inside the call would take device memory outside PyTorch's allocator
+        assert torch.cuda.mem_get_info()[0] == free_before
         assert torch.isfinite(out.float()).all()
         torch.testing.assert_close(out.float(), want.float(), atol=2e-2, rtol=2e-2)
+    assert lib.isb_noalloc_error_word() == 0
     assert torch.ops.isb.error_word() == 0
+
+
+def test_noalloc_context_past_block_table_is_flagged():
+    """A context one page longer than the block table: finite output over the pages it has, and
+    the error word (read through the C API) says the call's output is not valid."""
+    lib = _lib()
+    assert lib.isb_noalloc_setup() == OK
+    assert lib.isb_noalloc_error_word() == 0
+    b, hq, hkv, hd, mb = 2, 8, 2, 256, 2
+    q, gate, kc, vc, cl, bt = _case(b, hq, hkv, hd, [100, mb * 256 + 256], mb, seed=31)
+    out = torch.full((b, hq * hd), float("nan"), device="cuda", dtype=torch.bfloat16)
+    code = _call(lib, q, gate, kc, vc, cl, bt, hd ** -0.5, out)
+    torch.cuda.synchronize()
+    assert code == OK, lib.isb_noalloc_strerror(code).decode()
+    assert torch.isfinite(out.float()).all()
+    assert lib.isb_noalloc_error_word() == 0x2
+    assert lib.isb_noalloc_error_word() == 0  # read-and-clear
+    # the in-range sequence is unaffected
+    want = torch.ops.isb.attention_decode(q[:1], gate[:1], kc, vc, cl[:1], bt[:1], hd ** -0.5, True)
+    torch.testing.assert_close(out[:1].float(), want.float(), atol=2e-2, rtol=2e-2)
 
 
 def test_noalloc_rejects_oversized_and_invalid():
@@ -93,6 +119,9 @@ def test_noalloc_rejects_oversized_and_invalid():
     assert code == ETOOBIG
     assert b"scratch" in lib.isb_noalloc_strerror(code)
     code = lib.isb_attention_decode_noalloc(None, None, None, None, None, None, 3, 8, 8, 2, 256, 1.0, None, None)
+    assert code == EINVAL
+    # a block table wider than the decode grid can cover is invalid, not an int overflow
+    code = lib.isb_attention_decode_noalloc(None, None, None, None, None, None, 1 << 29, 1, 8, 2, 256, 1.0, None, None)
     assert code == EINVAL
     # The largest batch of the 0.8B decode shape (8 q heads, head_dim 256, 3 pages) fits.
     assert lib.isb_attention_decode_noalloc_scratch_bytes(128, 8, 256, 3) <= SCRATCH_BYTES
