@@ -59,27 +59,13 @@ def parse():
     return p.parse_args()
 
 
-def kernel_breakdown(replay, path: str, n: int = 3) -> None:
-    """Per-kernel device time of ``n`` replays (torch.profiler / CUPTI), written as a text table."""
-    import torch
-    from torch.profiler import ProfilerActivity, profile
+def kernel_breakdown(run, path: str, n: int = 3) -> None:
+    """Per-kernel device time of ``n`` calls of ``run`` written as a text table (single process)."""
+    from inference_systems_b200.engine.profiler import kernel_time_table
 
-    torch.cuda.synchronize()
-    with profile(activities=[ProfilerActivity.CUDA]) as prof:
-        for _ in range(n):
-            replay()
-        torch.cuda.synchronize()
-    agg: dict[str, list[float]] = {}
-    for ev in prof.events():
-        if ev.device_type == torch.autograd.DeviceType.CUDA:
-            agg.setdefault(ev.name, []).append(ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time_total)
-    total = sum(sum(v) for v in agg.values())
-    rows = sorted(agg.items(), key=lambda kv: -sum(kv[1]))
     os.makedirs(os.path.dirname(path), exist_ok=True)
     with open(path, "w") as f:
-        f.write(f"total device us per replay: {total / n:.1f}\n")
-        for name, v in rows:
-            f.write(f"{sum(v) / n:10.1f} us  {100 * sum(v) / total:5.1f}%  x{len(v) // n:<4d} {name[:160]}\n")
+        f.write(kernel_time_table(run, n))
 
 
 # ------------------------------------------------------------------ clocks
@@ -278,9 +264,9 @@ def run_isb(args, rank: int, world: int) -> dict | None:
     results = {b: _serve_batch(llm, runner, cfg, b, args, clk) for b in batches}
     head = results[args.batch]
     launches = runner.graph_kernel_count(args.batch)
-    if args.breakdown:
-        g = runner.graphs[runner._graph_bucket(args.batch)]
-        kernel_breakdown(g.replay, os.path.join(ROOT, args.breakdown_dir, f"breakdown_tp{world}_b{args.batch}.txt"))
+    if args.breakdown:  # every rank replays and profiles (the exchanges need all ranks)
+        runner.call("breakdown_replays", args.batch,
+                    os.path.join(ROOT, args.breakdown_dir, f"breakdown_tp{world}_b{args.batch}.txt"))
     out = {
         "metric": METRIC,
         "value": head["value"],

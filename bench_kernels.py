@@ -211,15 +211,20 @@ def cases(b: int) -> dict:
 def tp_bench(batches=(1, 8, 128)) -> None:
     """Fused tensor-parallel paths vs the NCCL baseline; run under torch.distributed.run.
 
-    Row-parallel down projection (hidden 1024, intermediate 3584 / TP) fused with the
-    all-reduce, residual add and RMSNorm; vocab-parallel LM head fused with the
-    cross-rank argmax.  Device time per call inside a CUDA graph (20 calls per graph,
-    5 replays), max over ranks.  Roofline = max(FLOPs / measured bf16 peak, bytes
-    this rank must pull over NVLink / 770 GB/s, bytes read from HBM / measured HBM).
+    * Row-parallel GEMM fused with the reduce-scatter (fp32 partial rows red.add'ed into their
+      owner's accumulator over NVLink) + the owner's residual add + RMSNorm + all-gather push
+      (``TPComm.row_parallel_residual_norm``), at the decode shape (0.8B MLP down, hidden 1024,
+      intermediate 3584 / TP) for several batches, at the 27B MLP down shape (batch 64), and for a
+      2048-token prefill chunk followed by the gate_up + SiLU GEMM.
+    * Vocab-parallel LM head fused with the cross-rank argmax.
+    Device time per call inside a CUDA graph (20 calls per graph, 5 replays), max over ranks.
+    Roofline = max(FLOPs / measured bf16 peak, bytes this rank sends over NVLink / 770 GB/s,
+    weight bytes / measured HBM).  The NCCL baseline is the same GEMM + ``dist.all_reduce`` of
+    the bf16 product + the add+RMSNorm kernel.
     """
     import torch.distributed as dist
 
-    from inference_systems_b200.parallel.comm import TPComm
+    from inference_systems_b200.parallel.comm import TPComm, shard_rows
 
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
@@ -227,13 +232,16 @@ def tp_bench(batches=(1, 8, 128)) -> None:
     dist.init_process_group("nccl", init_method="env://")
     hbm, tflops, src = peaks()
     nvlink = 770.0
-    h, inter, vocab = 1024, 3584 // world, 248320 // world
-    comm = TPComm(dev, rank, world, h, None, max_rows=256)
+    h, vocab = 1024, 248320 // world
     bf = torch.bfloat16
     g = torch.Generator(device=dev).manual_seed(rank)
-    w = (torch.randn(h, inter, device=dev, generator=g) * 0.02).to(bf)
-    nw = torch.zeros(h, device=dev).to(bf)
-    lm = (torch.randn(vocab, h, device=dev, generator=g) * 0.02).to(bf)
+    comms: dict[int, TPComm] = {}
+
+    def comm_for(hh: int) -> TPComm:
+        if hh not in comms:
+            comms[hh] = TPComm(dev, rank, world, hh, None, max_tokens=2048)
+        return comms[hh]
+
     rows = []
 
     def timed(fn, calls=20):
@@ -244,6 +252,7 @@ def tp_bench(batches=(1, 8, 128)) -> None:
                 fn()
         torch.cuda.current_stream().wait_stream(s)
         torch.cuda.synchronize()
+        dist.barrier()
         gr = torch.cuda.CUDAGraph()
         with torch.cuda.graph(gr):
             for _ in range(calls):
@@ -262,17 +271,28 @@ def tp_bench(batches=(1, 8, 128)) -> None:
         del gr
         return float(t.item())
 
-    shapes = [(1024, 3584, b) for b in batches] + [(5120, 17408, 64)]  # 0.8B MLP down; 27B MLP down
-    for hh, full_inter, b in shapes:
+    def emit(row):
+        rows.append(row)
+        if rank == 0:
+            print(json.dumps(row), flush=True)
+
+    def link_bytes(T, hh):
+        """Bytes this rank sends per exchange: partial sums of the other ranks' rows + its rows to every peer."""
+        s = shard_rows(T, world)
+        return (T - min(s, T)) * hh * 2 + (world - 1) * min(s, T) * hh * 2
+
+    # decode: MLP down projection + exchange; 0.8B at several batches and the 27B shape at 64
+    for hh, full_inter, b in [(1024, 3584, bb) for bb in batches] + [(5120, 17408, 64)]:
         ii = full_inter // world
-        cm = comm if hh == h else TPComm(dev, rank, world, hh, None, max_rows=256)
-        wd = w if hh == h else (torch.randn(hh, ii, device=dev, generator=g) * 0.02).to(bf)
-        nwd = nw if hh == h else torch.zeros(hh, device=dev).to(bf)
-        x = (torch.randn(b, ii, device=dev, generator=g)).to(bf)
+        cm = comm_for(hh)
+        wd = (torch.randn(hh, ii, device=dev, generator=g) * 0.02).to(bf)
+        nwd = torch.zeros(hh, device=dev).to(bf)
+        x = torch.randn(b, ii, device=dev, generator=g).to(bf)
         res = torch.randn(b, hh, device=dev, generator=g).to(bf)
         fused = timed(lambda: cm.row_parallel_residual_norm(x, wd, res, nwd, 1e-6, True))
         local_gemm = timed(lambda: ops.linear(x, wd))
-        local_norm = timed(lambda: ops.add_rmsnorm(torch.zeros(b, hh, device=dev, dtype=bf), res, nwd, 1e-6, True))
+        zero = torch.zeros(b, hh, device=dev, dtype=bf)
+        local_norm = timed(lambda: ops.add_rmsnorm(zero, res, nwd, 1e-6, True))
 
         def nccl_path():
             y = ops.linear(x, wd)
@@ -281,70 +301,61 @@ def tp_bench(batches=(1, 8, 128)) -> None:
 
         base = timed(nccl_path)
         flops = 2 * b * ii * hh
-        link = (world - 1) * b * hh * 4 / (nvlink * 1e9) * 1e6
-        roof = max(flops / (tflops * 1e12) * 1e6, link, (hh * ii * 2) / (hbm * 1e9) * 1e6)
-        rows.append({"path": "row-parallel GEMM -> all-reduce -> residual + RMSNorm", "tp": world, "batch": b,
-                     "hidden": hh, "inter_per_rank": ii, "fused_us": round(fused, 2),
-                     "nccl_baseline_us": round(base, 2), "local_gemm_us": round(local_gemm, 2),
-                     "local_add_norm_us": round(local_norm, 2), "roofline_us": round(roof, 2),
-                     "fraction_of_roofline": round(roof / fused, 3)})
-        if rank == 0:
-            print(json.dumps(rows[-1]), flush=True)
-        if cm is not comm:
-            cm.close()
+        roof = max(flops / (tflops * 1e12) * 1e6, link_bytes(b, hh) / (nvlink * 1e9) * 1e6,
+                   (hh * ii * 2) / (hbm * 1e9) * 1e6)
+        emit({"path": "row-parallel GEMM + reduce-scatter -> residual + RMSNorm + all-gather", "tp": world,
+              "batch": b, "hidden": hh, "inter_per_rank": ii, "fused_us": round(fused, 2),
+              "nccl_baseline_us": round(base, 2), "local_gemm_us": round(local_gemm, 2),
+              "local_add_norm_us": round(local_norm, 2), "roofline_us": round(roof, 3),
+              "fraction_of_roofline": round(roof / fused, 3)})
+    # LM head + cross-rank argmax
+    cm = comm_for(h)
+    lm = (torch.randn(vocab, h, device=dev, generator=g) * 0.02).to(bf)
     for b in batches:
         hid = torch.randn(b, h, device=dev, generator=g).to(bf)
         temps = torch.zeros(b, device=dev)
         rng = torch.zeros(2, dtype=torch.int32, device=dev)
-        fused = timed(lambda: comm.lm_head_sample(hid, lm, temps, rng, rank * vocab), calls=4)
+        fused = timed(lambda: cm.lm_head_sample(hid, lm, temps, rng, rank * vocab), calls=4)
         roof = max(2 * b * vocab * h / (tflops * 1e12) * 1e6, vocab * h * 2 / (hbm * 1e9) * 1e6,
                    (world - 1) * b * 8 / (nvlink * 1e9) * 1e6)
-        rows.append({"path": "vocab-parallel LM head -> cross-rank argmax", "tp": world, "batch": b,
-                     "fused_us": round(fused, 2), "roofline_us": round(roof, 2),
-                     "fraction_of_roofline": round(roof / fused, 3)})
-        if rank == 0:
-            print(json.dumps(rows[-1]), flush=True)
-    # token-sharded prefill chunk: row-parallel GEMM -> reduce-scatter + residual + RMSNorm ->
-    # all-gather fused into the next column-parallel GEMM (MLP down, then gate_up + SiLU)
-    os.environ["ISB_TP_SP"] = "1"
+        emit({"path": "vocab-parallel LM head -> cross-rank argmax", "tp": world, "batch": b,
+              "fused_us": round(fused, 2), "roofline_us": round(roof, 2), "fraction_of_roofline": round(roof / fused, 3)})
+    # prefill chunk: row GEMM + reduce-scatter -> norm + all-gather -> gate_up + SiLU GEMM
     for hh, full_inter, T in ((1024, 3584, 2048), (5120, 17408, 2048)):
         ii = full_inter // world
-        cm = TPComm(dev, rank, world, hh, None, max_rows=256)
-        S = cm.sp_rows(T)
-        lo, hi = cm.sp_range(T, S)
+        cm = comm_for(hh)
         wd = (torch.randn(hh, ii, device=dev, generator=g) * 0.02).to(bf)
         wgu = (torch.randn(2 * ii, hh, device=dev, generator=g) * 0.02).to(bf)
         nwd = torch.zeros(hh, device=dev).to(bf)
         y = torch.randn(T, ii, device=dev, generator=g).to(bf)
-        res_shard = torch.randn(hi - lo, hh, device=dev, generator=g).to(bf)
-        res_full = torch.randn(T, hh, device=dev, generator=g).to(bf)
+        res = torch.randn(T, hh, device=dev, generator=g).to(bf)
 
-        def sp_path():
-            x = cm.sp_row_parallel_norm(y, wd, res_shard, nwd, 1e-6, True, T, S)
-            return cm.sp_linear(x, wgu, True)
+        def fused_path():
+            x = cm.row_parallel_residual_norm(y, wd, res, nwd, 1e-6, True)
+            return ops.linear_silu_mul(x, wgu)
 
         def nccl_path2():
             z = ops.linear(y, wd)
             dist.all_reduce(z)
-            x = ops.add_rmsnorm(z, res_full, nwd, 1e-6, True)
+            x = ops.add_rmsnorm(z, res, nwd, 1e-6, True)
             return ops.linear_silu_mul(x, wgu)
 
-        fused = timed(sp_path, calls=4)
+        fused = timed(fused_path, calls=4)
         base = timed(nccl_path2, calls=4)
         flops = 2 * T * ii * hh + 2 * T * hh * 2 * ii
-        link = ((world - 1) * (T / world) * hh * 4 + (world - 1) / world * T * hh * 2) / (nvlink * 1e9) * 1e6
         wbytes = (hh * ii + 2 * ii * hh) * 2
-        roof = max(flops / (tflops * 1e12) * 1e6, link, wbytes / (hbm * 1e9) * 1e6)
-        rows.append({"path": "row GEMM -> reduce-scatter + residual + RMSNorm -> all-gather fused into gate_up GEMM",
-                     "tp": world, "tokens": T, "hidden": hh, "inter_per_rank": ii, "shard_rows": S,
-                     "fused_us": round(fused, 2), "nccl_baseline_us": round(base, 2), "roofline_us": round(roof, 2),
-                     "fraction_of_roofline": round(roof / fused, 3)})
-        if rank == 0:
-            print(json.dumps(rows[-1]), flush=True)
+        roof = max(flops / (tflops * 1e12) * 1e6, link_bytes(T, hh) / (nvlink * 1e9) * 1e6, wbytes / (hbm * 1e9) * 1e6)
+        emit({"path": "row GEMM + reduce-scatter -> residual + RMSNorm + all-gather -> gate_up GEMM",
+              "tp": world, "tokens": T, "hidden": hh, "inter_per_rank": ii,
+              "fused_us": round(fused, 2), "nccl_baseline_us": round(base, 2), "roofline_us": round(roof, 2),
+              "fraction_of_roofline": round(roof / fused, 3)})
+    torch.cuda.synchronize()
+    err = torch.ops.isb.error_word()
+    for cm in comms.values():
         cm.close()
-    comm.close()
     dist.barrier()
     dist.destroy_process_group()
+    assert err == 0, f"device error word {err:#x}"
 
 
 def main():

@@ -570,6 +570,13 @@ int64_t attn_error_word() {
   return v;
 }
 
+// Device address of the error word (read by the per-step status kernel).
+int64_t attn_error_word_address() {
+  void* p = nullptr;
+  TORCH_CHECK(cudaGetSymbolAddress(&p, g_attn_err) == cudaSuccess, "error word address");
+  return reinterpret_cast<int64_t>(p);
+}
+
 at::Tensor attention_prefill(const at::Tensor& q, const at::Tensor& gate, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& cu_q, const at::Tensor& ctx_lens, const at::Tensor& block_tables,
                              double scale, bool gated, int64_t max_seqlen_q) {

@@ -777,4 +777,11 @@ int64_t attn_tc_error_word() {
   return v;
 }
 
+// Device address of the error word (read by the per-step status kernel).
+int64_t attn_tc_error_word_address() {
+  void* p = nullptr;
+  TORCH_CHECK(cudaGetSymbolAddress(&p, g_attn_tc_err) == cudaSuccess, "error word address");
+  return reinterpret_cast<int64_t>(p);
+}
+
 }  // namespace isb

@@ -2,21 +2,25 @@
 //
 // Symmetric buffers: every rank cudaMalloc's one region, exports a CUDA IPC
 // handle, and maps every peer's region (``symm_alloc`` / ``symm_open``); kernels
-// then address peers with plain device pointers (P2P loads and stores through
-// NVSwitch).  Synchronisation between ranks uses monotone counters in the
-// symmetric region, released at system scope by their owner and acquired by
-// peers.  Every wait is bounded by a %globaltimer deadline; a timeout records an
-// error word (read by ``comm_error_word``) and later waits return at once, so a
-// missing peer can never hang a GPU.
+// then address peers with plain device pointers (P2P loads, stores and red
+// atomics through NVSwitch).  Synchronisation between ranks uses monotone
+// counters in the symmetric region that other ranks bump with system-scope
+// releases; every wait polls THIS rank's memory (no NVLink round trip per poll)
+// and is bounded by a %globaltimer deadline (``comm_set_wait_timeout``); a
+// timeout records an error word (``comm_error_word``) and later waits return at
+// once, so a missing peer can never hang a GPU.
 //
-//  * add_rmsnorm_acc_tp: second half of the fused row-parallel GEMM all-reduce.
-//    Each rank's GEMM (gemm.cu ``tp_gemm_accum``) reduced its partial product
-//    into its own fp32 accumulator and bumped its own counter; this kernel waits
-//    until every peer's counter has reached this rank's, sums all ranks'
-//    accumulators with P2P loads, adds the residual and applies the next
-//    RMSNorm.  Accumulators alternate between two parities per call, and the
-//    buffer of the previous call is re-zeroed here: every peer finished reading
-//    it, because each peer's current GEMM started after its previous consumer.
+//  * tp_norm_allgather: second half of the fused row-parallel exchange.  The
+//    row-parallel GEMM (gemm.cu ``tp_gemm_rs``) reduce-scattered its partial
+//    product by token: every rank stored the complete bf16 rows owned by rank r
+//    into rank r's slot for that source, then bumped rank r's arrival counter.
+//    This kernel waits until all W ranks have arrived, and for each owned row
+//    sums the W slots in fp32, adds the residual, applies the next RMSNorm and
+//    pushes the normalised bf16 row into every rank's activation buffer (the
+//    all-gather, P2P stores), then releases every rank's gather counter; its
+//    last CTA waits for all owners' pushes, so the next kernel (a column-parallel
+//    GEMM, PDL-launched) reads a complete, local activation.  Per exchange a rank
+//    sends (W-1)/W * T * H bf16 partial sums and (W-1) * T/W * H bf16 activations.
 //  * xrank_argmax: cross-rank (score, token) argmax of the vocab-parallel LM
 //    head; each rank publishes 8 bytes per row to every peer instead of gathering logits.
 
@@ -29,6 +33,8 @@
 namespace isb {
 
 __device__ unsigned int g_comm_err;
+// Deadline of every cross-rank wait in this file (ns).
+__device__ unsigned long long g_comm_wait_ns = 2000000000ull;
 
 namespace {
 
@@ -38,17 +44,36 @@ ISB_DEVICE unsigned int ld_acquire_sys(const unsigned int* p) {
   return v;
 }
 
+ISB_DEVICE bool comm_failed() { return *reinterpret_cast<volatile unsigned int*>(&g_comm_err) != 0u; }
+
 // Wait until flags[0..n) are all >= 1 (bounded).  Returns false on timeout.
 ISB_DEVICE bool wait_flags(const unsigned int* flags, int n) {
-  if (*reinterpret_cast<volatile unsigned int*>(&g_comm_err) != 0u) return false;
+  if (comm_failed()) return false;
   const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_comm_wait_ns);
   for (int r = 0; r < n; ++r) {
     uint32_t spins = 0;
     while (ld_acquire_sys(flags + r) < 1u) {
-      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > limit) {
         atomicOr(&g_comm_err, 1u);
         return false;
       }
+    }
+  }
+  return true;
+}
+
+// Wait until the local counter ``*cnt`` has reached ``target`` (wrap-safe, bounded).  ``code`` is
+// OR'ed into the error word on timeout.
+ISB_DEVICE bool wait_geq(const unsigned int* cnt, unsigned int target, unsigned int code) {
+  if (comm_failed()) return false;
+  const uint64_t t0 = globaltimer_ns();
+  const uint64_t limit = *reinterpret_cast<volatile unsigned long long*>(&g_comm_wait_ns);
+  uint32_t spins = 0;
+  while (int(ld_acquire_sys(cnt) - target) < 0) {
+    if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > limit) {
+      atomicOr(&g_comm_err, code);
+      return false;
     }
   }
   return true;
@@ -79,208 +104,110 @@ __device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
   *reinterpret_cast<uint4*>(p) = raw;
 }
 
-// Wait until every counter flags[r] (peer memory) has reached ``target`` (bounded).
-ISB_DEVICE bool wait_counters(const unsigned long long* flags, int n, unsigned int target) {
-  if (*reinterpret_cast<volatile unsigned int*>(&g_comm_err) != 0u) return false;
-  const uint64_t t0 = globaltimer_ns();
-  for (int r = 0; r < n; ++r) {
-    const unsigned int* f = reinterpret_cast<const unsigned int*>(flags[r]);
-    uint32_t spins = 0;
-    while (int(ld_acquire_sys(f) - target) < 0) {
-      if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
-        atomicOr(&g_comm_err, 1u);
-        return false;
-      }
-    }
-  }
-  return true;
-}
-
-// One block per row, 8 columns per thread (blockDim = H / 8 rounded up to a warp, at most
-// 512).  Every peer's slice of a chunk is loaded before any of it is summed (the peer loop
-// is unrolled over kMaxWorld with predication), so a thread has 2 x world NVLink loads in
-// flight instead of one round trip per peer.
 constexpr int kMaxWorld = 8;
+constexpr int kMaxChunks = 4;  // columns per thread / 8: H <= 4 * 8 * 512
 
-// Wait (threads 0..world-1, one peer each) until every rank's counter flags[r] has reached
-// this rank's own ``*my_flag``; returns the block-wide verdict.
-__device__ __forceinline__ bool wait_all_ranks(const unsigned long long* flags, const unsigned int* my_flag,
-                                               int world) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) ok = 1;
-  __syncthreads();
-  if (threadIdx.x < world) {  // one NVLink round trip per peer, all in parallel
-    const unsigned int target = ld_acquire_sys(my_flag);
-    if (!wait_counters(flags + threadIdx.x, 1, target)) ok = 0;
-  }
-  __syncthreads();
-  return ok != 0;
-}
-
-// out_row = RMSNorm(res_row + sum_r accs[r][acc_row]); res_row is updated in place.  With ``outs``
-// (nout buffer bases, peer memory included) the row is written to row ``acc_row`` of every one of
-// them instead of to ``out``.
-__device__ __forceinline__ void pull_add_norm_row(const unsigned long long* __restrict__ accs, int world, bool ok,
-                                                  size_t acc_row, __nv_bfloat16* __restrict__ res,
-                                                  const __nv_bfloat16* __restrict__ w,
-                                                  __nv_bfloat16* __restrict__ out, int H, float eps, bool zc,
-                                                  const unsigned long long* outs = nullptr, int nout = 0) {
-  __shared__ float red[32];
+// Owned rows are spread over the grid (blockDim = H / 8 rounded up to a warp, at most 512; 8
+// columns per thread per chunk).  ``slots``: this rank's [world][slot_rows][H] bf16 partial sums;
+// row i of each source slot is token ``lo + i``.  ``ctl`` words: 0 arrivals of row-parallel GEMM
+// CTAs, 1 arrivals of owner CTAs, 2 / 3 the targets those counters reached at the end of the
+// previous exchange, 4 this kernel's CTA-completion counter.  ``rs_incr`` / ``ag_incr``: arrivals
+// this exchange adds to words 0 / 1.
+__global__ void __launch_bounds__(512) tp_norm_ag_kernel(
+    const __nv_bfloat16* __restrict__ slots, int slot_rows, __nv_bfloat16* __restrict__ residual,
+    const __nv_bfloat16* __restrict__ w, const unsigned long long* __restrict__ xdst,
+    const unsigned long long* __restrict__ ag_flags, unsigned int* ctl, int lo, int rows, int H, float eps,
+    bool zc, int world, bool wait_gather, unsigned int rs_incr, unsigned int ag_incr) {
+  pdl_trigger();
+  pdl_wait();
+  __shared__ int s_ok;
+  __shared__ float red[16];
   const int tid = threadIdx.x, nt = blockDim.x;
-  const float* peer[kMaxWorld];
+  // targets of this exchange; the previous exchange's last CTA wrote the bases before its grid
+  // completed (ordered by pdl_wait), and this exchange's last CTA moves them only after every CTA
+  // has read them
+  const unsigned int rs_target = ctl[2] + rs_incr, ag_target = ctl[3] + ag_incr;
+  if (tid == 0) s_ok = rows > 0 ? (wait_geq(ctl, rs_target, 2u) ? 1 : 0) : 1;
+  __syncthreads();
+  const size_t slot_stride = size_t(slot_rows) * H;
+  for (int i = blockIdx.x; i < rows; i += gridDim.x) {
+    const size_t r = size_t(lo) + i;
+    __nv_bfloat16* res = residual + r * H;
+    const __nv_bfloat16* mine = slots + size_t(i) * H;
+    float v[kMaxChunks][8];
+    float ss = 0.f;
 #pragma unroll
-  for (int r = 0; r < kMaxWorld; ++r) peer[r] = r < world ? reinterpret_cast<const float*>(accs[r]) + acc_row * H : nullptr;
-  float ss = 0.f;
-  constexpr int kMaxChunks = 4;  // H <= 4 * 8 * 512
-  float v[kMaxChunks][8];
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = (tid + k * nt) * 8;
+      if (c >= H) break;
+      // every source's slice first (written by other GPUs: read from L2, never a stale L1 line),
+      // so a thread has all of them in flight before it sums
+      uint4 raw[kMaxWorld];
 #pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    const int c = (tid + k * nt) * 8;
-    if (c >= H) break;
-    float4 lo[kMaxWorld], hi[kMaxWorld];
+      for (int q = 0; q < kMaxWorld; ++q)
+        raw[q] = q < world && s_ok ? __ldcg(reinterpret_cast<const uint4*>(mine + q * slot_stride + c))
+                                   : make_uint4(0u, 0u, 0u, 0u);
+      const Vec8 rr = load8(res + c);
 #pragma unroll
-    for (int r = 0; r < kMaxWorld; ++r) {
-      if (r < world && ok) {
-        lo[r] = __ldcv(reinterpret_cast<const float4*>(peer[r] + c));
-        hi[r] = __ldcv(reinterpret_cast<const float4*>(peer[r] + c + 4));
-      } else {
-        lo[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-        hi[r] = lo[r];
+      for (int e = 0; e < 8; ++e) v[k][e] = rr.v[e];
+#pragma unroll
+      for (int q = 0; q < kMaxWorld; ++q) {
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(h[e]);
+          v[k][2 * e] += f.x;
+          v[k][2 * e + 1] += f.y;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[k][e] * v[k][e];
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int q = 0; q < (nt + 31) / 32; ++q) tot += red[q];
+    __syncthreads();  // ``red`` is reused by the next row
+    const float rs = rsqrtf(tot / float(H) + eps);
+#pragma unroll
+    for (int k = 0; k < kMaxChunks; ++k) {
+      const int c = (tid + k * nt) * 8;
+      if (c >= H) break;
+      store8(res + c, v[k]);
+      const Vec8 wv = load8(w + c);
+      float y[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        y[e] = zc ? v[k][e] * rs * (1.f + wv.v[e]) : __bfloat162float(__float2bfloat16(v[k][e] * rs)) * wv.v[e];
+      uint4 out;
+      __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+      // the all-gather: the row goes to every rank's activation buffer (staggered start)
+      for (int q = 0; q < world; ++q) {
+        const int dst = (i + q) % world;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xdst[dst]) + r * H + c) = out;
       }
     }
-    float x[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int r = 0; r < kMaxWorld; ++r) {
-      x[0] += lo[r].x; x[1] += lo[r].y; x[2] += lo[r].z; x[3] += lo[r].w;
-      x[4] += hi[r].x; x[5] += hi[r].y; x[6] += hi[r].z; x[7] += hi[r].w;
-    }
-    const Vec8 rr = load8(res + c);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      v[k][i] = x[i] + rr.v[i];
-      ss += v[k][i] * v[k][i];
-    }
   }
-  ss = warp_sum(ss);
-  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  // Count this CTA in on every rank (a system-scope release after the CTA barrier orders all its
+  // threads' pushes); the last CTA here then moves the targets on and, unless told otherwise,
+  // waits until every owner's rows have arrived, so the grid completes with the full activation.
   __syncthreads();
-  float tot = 0.f;
-  for (int i = 0; i < (nt + 31) / 32; ++i) tot += red[i];
-  const float rs = rsqrtf(tot / float(H) + eps);
-#pragma unroll
-  for (int k = 0; k < kMaxChunks; ++k) {
-    const int c = (tid + k * nt) * 8;
-    if (c >= H) break;
-    store8(res + c, v[k]);
-    const Vec8 wv = load8(w + c);
-    float y[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i)
-      y[i] = zc ? v[k][i] * rs * (1.f + wv.v[i]) : __bfloat162float(__float2bfloat16(v[k][i] * rs)) * wv.v[i];
-    if (outs == nullptr) {
-      store8(out + c, y);
-    } else {
-      for (int r = 0; r < nout; ++r) store8(reinterpret_cast<__nv_bfloat16*>(outs[r]) + acc_row * H + c, y);
+  if (tid == 0) {
+    for (int q = 0; q < world; ++q) {
+      unsigned int* f = reinterpret_cast<unsigned int*>(ag_flags[q]);
+      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
     }
-  }
-}
-
-__global__ void __launch_bounds__(512) acc_norm_tp_kernel(const unsigned long long* __restrict__ accs,
-                                                          float* __restrict__ my_other,
-                                                          __nv_bfloat16* __restrict__ residual,
-                                                          const __nv_bfloat16* __restrict__ w,
-                                                          __nv_bfloat16* __restrict__ out, int rows, int H, float eps,
-                                                          bool zc, const unsigned long long* flags,
-                                                          const unsigned int* my_flag, int world,
-                                                          unsigned int* rows_used, int parity) {
-  pdl_trigger();
-  pdl_wait();
-  const int tid = threadIdx.x, row = blockIdx.x, nt = blockDim.x;
-  const bool ok = wait_all_ranks(flags, my_flag, world);
-  // re-zero the accumulator rows of the previous call (other parity); peers are done with them
-  const int prev_rows = int(rows_used[parity ^ 1]);
-  for (int r = row; r < prev_rows; r += gridDim.x)
-    for (int c = tid * 4; c < H; c += nt * 4) *reinterpret_cast<float4*>(my_other + size_t(r) * H + c) = make_float4(0.f, 0.f, 0.f, 0.f);
-  if (row < rows)
-    pull_add_norm_row(accs, world, ok, size_t(row), residual + size_t(row) * H, w, out + size_t(row) * H, H, eps, zc);
-  if (row == 0 && tid == 0) rows_used[parity] = unsigned(rows);
-}
-
-// Every CTA makes its writes visible system-wide and counts itself in; the last one resets the
-// counter and releases ``*ready += 1`` at system scope.
-__device__ __forceinline__ void finish_and_release(unsigned int* done_ctr, unsigned int* ready) {
-  __threadfence_system();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const unsigned int prev = atomicAdd(done_ctr, 1u);
+    unsigned int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctl + 4) : "memory");
     if (prev == gridDim.x - 1) {
-      atomicExch(done_ctr, 0u);
-      __threadfence_system();
-      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(ready) : "memory");
+      ctl[4] = 0u;
+      if (wait_gather) wait_geq(ctl + 1, ag_target, 4u);
+      ctl[2] = rs_target;
+      ctl[3] = ag_target;
     }
-  }
-}
-
-// Token-sharded (sequence-parallel) reduce-scatter + residual + RMSNorm + all-gather: rank r
-// owns rows [row_base, row_base + rows) of the T tokens.  Each CTA pulls one of those rows from
-// every rank's fp32 partial product (after every rank's row-parallel GEMM counter has caught up
-// with this rank's), adds the shard's residual row, and pushes the normalised row into row
-// (row_base + row) of every rank's full activation buffer (``xf``, peer memory), so each remote
-// row crosses NVLink once; peers' GEMMs read it from their own memory once ``*ready`` has moved on.
-__global__ void __launch_bounds__(512) sp_rs_norm_kernel(const unsigned long long* __restrict__ accs,
-                                                         const unsigned long long* gflags,
-                                                         const unsigned int* my_gflag, int world,
-                                                         __nv_bfloat16* __restrict__ residual,
-                                                         const __nv_bfloat16* __restrict__ w,
-                                                         const unsigned long long* __restrict__ xf, int rows,
-                                                         int row_base, int H, float eps, bool zc,
-                                                         unsigned int* done_ctr, unsigned int* ready) {
-  pdl_trigger();
-  pdl_wait();
-  const bool ok = wait_all_ranks(gflags, my_gflag, world);
-  const int row = blockIdx.x;
-  if (row < rows)
-    pull_add_norm_row(accs, world, ok, size_t(row_base + row), residual + size_t(row) * H, w, nullptr, H, eps, zc,
-                      xf, world);
-  finish_and_release(done_ctr, ready);
-}
-
-// Push this rank's first normalised shard (embedding + first RMSNorm) into rows
-// [row_base, row_base + rows) of every rank's full activation buffer and release ``*ready``.
-__global__ void __launch_bounds__(256) sp_publish_kernel(const __nv_bfloat16* __restrict__ x,
-                                                         const unsigned long long* __restrict__ xf, int world,
-                                                         int rows, int row_base, int H, unsigned int* done_ctr,
-                                                         unsigned int* ready) {
-  pdl_trigger();
-  pdl_wait();
-  const int row = blockIdx.x;
-  if (row < rows)
-    for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-      const uint4 v = *reinterpret_cast<const uint4*>(x + size_t(row) * H + c);
-      for (int r = 0; r < world; ++r)
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xf[r]) + size_t(row_base + row) * H + c) = v;
-    }
-  finish_and_release(done_ctr, ready);
-}
-
-// out[t] = row t of this rank's full activation buffer, once its owner (t / S) has pushed it
-// (the owner's counter has reached this rank's).
-__global__ void __launch_bounds__(256) sp_gather_kernel(const __nv_bfloat16* __restrict__ xf,
-                                                        const unsigned long long* flags, const unsigned int* my_flag,
-                                                        int S, int H, __nv_bfloat16* __restrict__ out) {
-  pdl_trigger();
-  pdl_wait();
-  __shared__ int ok;
-  const int t = blockIdx.x, owner = t / S;
-  if (threadIdx.x == 0) {
-    const unsigned int target = ld_acquire_sys(my_flag);
-    ok = wait_counters(flags + owner, 1, target) ? 1 : 0;
-  }
-  __syncthreads();
-  for (int c = threadIdx.x * 8; c < H; c += blockDim.x * 8) {
-    uint4 v = make_uint4(0u, 0u, 0u, 0u);
-    if (ok) v = __ldcv(reinterpret_cast<const uint4*>(xf + size_t(t) * H + c));
-    *reinterpret_cast<uint4*>(out + size_t(t) * H + c) = v;
   }
 }
 
@@ -323,6 +250,22 @@ __global__ void xrank_argmax_kernel(const float* __restrict__ val, const int* __
     for (int r = 0; r < world; ++r) atomicSub(my_xbuf_flags + r, 1u);
 }
 
+// The step's output row for the host: out[0..n) = the sampled tokens, out[n] = bit i set when
+// error word i (words[i], device addresses) is nonzero.  One launch and the token copy that
+// already happens carry every kernel's error state back each step.
+__global__ void step_status_kernel(const int* __restrict__ toks, int n, const unsigned long long* __restrict__ words,
+                                   int nwords, int* __restrict__ out) {
+  pdl_trigger();
+  pdl_wait();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = toks[i];
+  if (threadIdx.x == 0) {
+    int bits = 0;
+    for (int i = 0; i < nwords; ++i)
+      if (*reinterpret_cast<volatile const unsigned int*>(words[i]) != 0u) bits |= 1 << i;
+    out[n] = bits;
+  }
+}
+
 }  // namespace
 
 // ------------------------------------------------------------- host side
@@ -354,28 +297,45 @@ int64_t symm_open(const at::Tensor& handle) {
 
 void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
 
-at::Tensor add_rmsnorm_acc_tp(const at::Tensor& accs, at::Tensor my_acc_other, at::Tensor residual,
-                              const at::Tensor& w, double eps, bool zc, const at::Tensor& flags,
-                              const at::Tensor& my_flag, at::Tensor rows_used, int64_t parity) {
-  TORCH_CHECK(accs.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && accs.numel() == flags.numel(),
-              "accs / flags must be int64 device tables of equal length");
-  TORCH_CHECK(my_acc_other.scalar_type() == at::kFloat && my_acc_other.is_contiguous(), "fp32 accumulator");
-  TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16, "residual must be bf16");
-  TORCH_CHECK(my_flag.scalar_type() == at::kInt && rows_used.scalar_type() == at::kInt && rows_used.numel() == 2,
-              "int32 flag / row-count words");
-  const int H = residual.size(-1), rows = residual.numel() / H;
+// Owner side of the row-parallel exchange (see the file comment) for a ``T``-token exchange with
+// ``own_rows`` token rows per rank (rank r owns [r*own_rows, (r+1)*own_rows) clipped to T).
+// ``slots``: this rank's [W, slot_rows, H] bf16 partial sums; ``residual`` [T, H] bf16 (the owned
+// rows are read and updated); ``xdst`` / ``ag_flags``: int64 [W] device tables of every rank's
+// activation buffer [>= T, H] bf16 and owner-arrival counter; ``ctl``: this rank's int32 control
+// words (see the kernel); ``rs_incr``: row-parallel GEMM arrivals per exchange (W x its CTAs).
+// ``wait_gather`` false skips the final wait (single-GPU tests that emulate several ranks).
+constexpr int kNormMaxCtas = 296;  // two per SM: one exchange's rows never need more
+
+static int norm_ctas(int64_t rows) { return int(std::max<int64_t>(std::min<int64_t>(rows, kNormMaxCtas), 1)); }
+
+void tp_norm_allgather(const at::Tensor& slots, at::Tensor residual, const at::Tensor& w, const at::Tensor& xdst,
+                       const at::Tensor& ag_flags, at::Tensor ctl, int64_t T, int64_t own_rows, int64_t rank,
+                       int64_t rs_incr, double eps, bool zc, bool wait_gather) {
+  TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16 && residual.dim() == 2 &&
+                  residual.size(0) >= T, "residual must be contiguous bf16 [>= T, H]");
+  const int H = residual.size(1);
+  const int W = xdst.numel();
+  TORCH_CHECK(xdst.scalar_type() == at::kLong && ag_flags.scalar_type() == at::kLong && ag_flags.numel() == W &&
+                  W >= 1 && W <= kMaxWorld, "one activation buffer and counter per rank (<= 8)");
+  TORCH_CHECK(own_rows >= 1 && own_rows * W >= T && rank >= 0 && rank < W, "every token row needs an owner");
+  TORCH_CHECK(slots.scalar_type() == at::kBFloat16 && slots.is_contiguous() && slots.dim() == 3 &&
+                  slots.size(0) == W && slots.size(2) == H && slots.size(1) >= own_rows,
+              "slots: contiguous bf16 [W, >= own_rows, H]");
   TORCH_CHECK(H % 8 == 0 && H <= 16384, "hidden size must be a multiple of 8 and at most 16384");
-  at::Tensor out = at::empty_like(residual);
-  TORCH_CHECK(flags.numel() <= kMaxWorld, "at most ", kMaxWorld, " ranks");
+  TORCH_CHECK(ctl.scalar_type() == at::kInt && ctl.numel() >= 5 && ctl.is_contiguous(), "int32 control words");
+  auto owned = [&](int64_t r) { return std::max<int64_t>(0, std::min<int64_t>(own_rows, T - r * own_rows)); };
+  int64_t ag_incr = 0;  // every CTA of every rank's owner kernel signals every rank once
+  for (int64_t r = 0; r < W; ++r) ag_incr += norm_ctas(owned(r));
+  const int64_t rows = owned(rank);
+  const int64_t lo = std::min<int64_t>(rank * own_rows, T);
   const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
-  launch_pdl(acc_norm_tp_kernel, dim3(std::max(rows, 1)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()), my_acc_other.data_ptr<float>(),
+  launch_pdl(tp_norm_ag_kernel, dim3(norm_ctas(rows)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr()), int(slots.size(1)),
              reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), rows, H, float(eps), zc,
-             reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()),
-             reinterpret_cast<const unsigned int*>(my_flag.data_ptr<int>()), int(flags.numel()),
-             reinterpret_cast<unsigned int*>(rows_used.data_ptr<int>()), int(parity));
-  return out;
+             reinterpret_cast<const unsigned long long*>(xdst.data_ptr<int64_t>()),
+             reinterpret_cast<const unsigned long long*>(ag_flags.data_ptr<int64_t>()),
+             reinterpret_cast<unsigned int*>(ctl.data_ptr<int>()), int(lo), int(rows), H, float(eps), zc, W,
+             wait_gather, static_cast<unsigned int>(rs_incr), static_cast<unsigned int>(ag_incr));
 }
 
 at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,
@@ -392,51 +352,14 @@ at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::
   return out;
 }
 
-// ---------------------------------------------------------------- sequence-parallel (token-sharded) path
-// ``xf``: int64 [W] device addresses of every rank's full activation buffer (>= row_base + rows
-// rows of H bf16 each; the caller sizes them).
-void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
-                const at::Tensor& w, const at::Tensor& xf, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
-                at::Tensor ready) {
-  TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16 && residual.dim() == 2,
-              "residual shard: contiguous bf16 [rows, H]");
-  const int rows = residual.size(0), H = residual.size(1);
-  TORCH_CHECK(H % 8 == 0 && H <= 16384, "hidden size must be a multiple of 8 and at most 16384");
-  TORCH_CHECK(gflags.numel() <= kMaxWorld && accs.numel() == gflags.numel() && xf.numel() == gflags.numel(),
-              "one accumulator, counter and activation buffer per rank");
-  const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
-  launch_pdl(sp_rs_norm_kernel, dim3(std::max(rows, 1)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const unsigned long long*>(accs.data_ptr<int64_t>()),
-             reinterpret_cast<const unsigned long long*>(gflags.data_ptr<int64_t>()),
-             reinterpret_cast<const unsigned int*>(my_gflag.data_ptr<int>()), int(gflags.numel()),
-             reinterpret_cast<__nv_bfloat16*>(residual.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
-             reinterpret_cast<const unsigned long long*>(xf.data_ptr<int64_t>()), rows, int(row_base), H, float(eps), zc,
-             reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
-}
-
-void sp_publish(const at::Tensor& x, const at::Tensor& xf, int64_t row_base, at::Tensor done_ctr, at::Tensor ready) {
-  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.dim() == 2, "x: contiguous bf16 [rows, H]");
-  const int rows = x.size(0), H = x.size(1);
-  TORCH_CHECK(H % 8 == 0 && xf.numel() <= kMaxWorld, "hidden size a multiple of 8, at most 8 ranks");
-  launch_pdl(sp_publish_kernel, dim3(std::max(rows, 1)), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
-             reinterpret_cast<const unsigned long long*>(xf.data_ptr<int64_t>()), int(xf.numel()), rows, int(row_base),
-             H, reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>()), reinterpret_cast<unsigned int*>(ready.data_ptr<int>()));
-}
-
-at::Tensor sp_gather(const at::Tensor& xf_local, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
-                     int64_t T) {
-  TORCH_CHECK(xf_local.is_contiguous() && xf_local.scalar_type() == at::kBFloat16 && xf_local.dim() == 2 &&
-                  xf_local.size(0) >= T, "local activation buffer [>= T, H] bf16");
-  const int64_t H = xf_local.size(1);
-  TORCH_CHECK(H % 8 == 0 && S > 0 && T <= S * flags.numel(), "gather shape");
-  at::Tensor out = at::empty({T, H}, xf_local.options());
-  if (T == 0) return out;
-  launch_pdl(sp_gather_kernel, dim3(T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
-             reinterpret_cast<const __nv_bfloat16*>(xf_local.data_ptr()),
-             reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>()),
-             reinterpret_cast<const unsigned int*>(my_flag.data_ptr<int>()), int(S), int(H),
-             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()));
+at::Tensor step_status(const at::Tensor& toks, const at::Tensor& words) {
+  TORCH_CHECK(toks.scalar_type() == at::kInt && toks.is_contiguous() && toks.dim() == 1, "tokens: int32 [n]");
+  TORCH_CHECK(words.scalar_type() == at::kLong && words.is_cuda() && words.numel() <= 31, "error word addresses");
+  const int n = toks.numel();
+  at::Tensor out = at::empty({n + 1}, toks.options());
+  launch_pdl(step_status_kernel, dim3(1), dim3(256), 0, at::cuda::getCurrentCUDAStream(), toks.data_ptr<int>(), n,
+             reinterpret_cast<const unsigned long long*>(words.data_ptr<int64_t>()), int(words.numel()),
+             out.data_ptr<int>());
   return out;
 }
 
@@ -446,6 +369,21 @@ int64_t comm_error_word() {
   const unsigned int z = 0;
   cudaMemcpyToSymbol(g_comm_err, &z, sizeof(z));
   return v;
+}
+
+// Deadline of the cross-rank waits (ns) on the current device.  Tests shorten it to make a wait
+// on a counter that never advances run out quickly.
+void comm_set_wait_timeout(int64_t ns) {
+  const unsigned long long v = static_cast<unsigned long long>(ns);
+  TORCH_CHECK(ns > 0, "wait timeout must be positive");
+  TORCH_CHECK(cudaMemcpyToSymbol(g_comm_wait_ns, &v, sizeof(v)) == cudaSuccess, "setting the wait timeout");
+}
+
+// Device address of the error word (for the per-step error status kernel).
+int64_t comm_error_word_address() {
+  void* p = nullptr;
+  TORCH_CHECK(cudaGetSymbolAddress(&p, g_comm_err) == cudaSuccess, "comm error word address");
+  return reinterpret_cast<int64_t>(p);
 }
 
 }  // namespace isb

@@ -49,7 +49,7 @@ struct GemmCfg {
                 "split-K / SiLU staging must fit in the stage buffers");
 };
 
-enum Epilogue : int { kStore = 0, kSiluMul = 1, kArgmax = 2, kRedAdd = 3 };
+enum Epilogue : int { kStore = 0, kSiluMul = 1, kArgmax = 2, kRedAdd = 3, kRsPush = 4 };
 
 struct GemmArgs {
   __nv_bfloat16* out;      // kStore / kSiluMul output
@@ -66,28 +66,21 @@ struct GemmArgs {
   float* ws;                // split-K partials [tiles][splits][BM][BN] fp32
   float* acc;               // kRedAdd: fp32 accumulator [tokens][features], atomically added to
   unsigned int* counters;   // split-K arrival counters (self-resetting)
-  // kRedAdd across tensor-parallel ranks: the tile is added into every rank's accumulator
-  const unsigned long long* dsts;  // [ndst] accumulator base pointers (peer memory), or null
+  // kRsPush (tensor-parallel reduce-scatter by token): token row t of this rank's partial product
+  // belongs to rank o = t / own_rows.  Split-K CTAs first reduce into this rank's fp32 staging
+  // accumulator ``acc`` (local red.add; the tile's last CTA reads the sum back and re-zeroes it);
+  // the complete bf16 row is then stored into rank o's slot for this rank:
+  // ``dsts[o]`` + ((rank * slot_rows + t - o * own_rows) * ldo + feature) elements.  When every
+  // CTA's pushes are out, it releases ``+1`` on every rank's counter ``peer_flags[r]``.
+  const unsigned long long* dsts;  // [ndst] slot-array base addresses (peer memory included)
   int ndst;
-  unsigned int* done_ctr;          // local CTA-completion counter (self-resetting)
-  const unsigned long long* peer_flags;  // [ndst] flag-array base of each rank; flag index = rank
+  int own_rows;                    // token rows owned by each rank
+  int slot_rows;                   // rows of one source slot (>= own_rows)
+  const unsigned long long* peer_flags;  // [ndst] address of each rank's arrival counter
   int rank;
   // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
   // CTA and the accumulator is zero between uses, so plain stores replace the atomics
   bool acc_plain;
-  // when set, the grid's last CTA releases ``*signal += 1`` at system scope after every CTA's tile
-  // is in ``acc`` (tensor-parallel peers poll it before reading this rank's accumulator)
-  unsigned int* signal;
-  // All-gather operand (non-swap path only): the activation rows are token-sharded over the
-  // tensor-parallel ranks, ``ag_rows`` rows per rank (a multiple of BM).  The M tile at row
-  // m*BM belongs to rank m*BM / ag_rows and is read once that rank's counter (``ag_flags[rank]``,
-  // peer memory) has reached this rank's own counter ``*ag_own``: from the owner's own shard
-  // buffer through ``ag_maps[rank]`` (tensor maps in device memory) when ``ag_maps`` is set,
-  // else from row m*BM of the local buffer behind ``tmP``, into which every owner pushed its rows.
-  const CUtensorMap* ag_maps;
-  const unsigned long long* ag_flags;
-  const unsigned int* ag_own;
-  int ag_rows;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -107,20 +100,13 @@ ISB_DEVICE void red_add_v4_sys(float* p, float a, float b, float c, float d) {
                : "memory");
 }
 
-// Add 4 consecutive values at element offset ``off`` of the accumulator(s).
+// Add 4 consecutive values at element offset ``off`` of the accumulator.
 ISB_DEVICE void acc_add4(const GemmArgs& args, size_t off, float a, float b, float c, float d) {
   if (args.acc_plain) {
     *reinterpret_cast<float4*>(args.acc + off) = make_float4(a, b, c, d);
     return;
   }
-  if (args.ndst == 0) {
-    red_add_v4(args.acc + off, a, b, c, d);
-    return;
-  }
-  for (int r = 0; r < args.ndst; ++r) {
-    const int dst = (args.rank + r) % args.ndst;  // stagger the peers
-    red_add_v4_sys(reinterpret_cast<float*>(args.dsts[dst]) + off, a, b, c, d);
-  }
+  red_add_v4(args.acc + off, a, b, c, d);
 }
 
 ISB_DEVICE void acc_add1(const GemmArgs& args, size_t off, float a) {
@@ -128,11 +114,25 @@ ISB_DEVICE void acc_add1(const GemmArgs& args, size_t off, float a) {
     args.acc[off] = a;
     return;
   }
-  if (args.ndst == 0) {
-    atomicAdd(args.acc + off, a);
-    return;
-  }
-  for (int r = 0; r < args.ndst; ++r) atomicAdd_system(reinterpret_cast<float*>(args.dsts[r]) + off, a);
+  atomicAdd(args.acc + off, a);
+}
+
+// kRsPush: store 4 features of token ``tok`` (bf16) into the owner rank's slot for this rank.
+ISB_DEVICE void rs_push4(const GemmArgs& args, int tok, int f, float a, float b, float c, float d) {
+  const int owner = tok / args.own_rows;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dsts[owner]) +
+                       (size_t(args.rank) * args.slot_rows + (tok - owner * args.own_rows)) * args.ldo + f;
+  uint2 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+  h[0] = __floats2bfloat162_rn(a, b);
+  h[1] = __floats2bfloat162_rn(c, d);
+  *reinterpret_cast<uint2*>(dst) = raw;
+}
+
+// kRsPush: 4 features of token ``tok`` of this CTA's partial: staged (split K) or pushed.
+ISB_DEVICE void rs_emit4(const GemmArgs& args, bool staged, int tok, int f, float a, float b, float c, float d) {
+  if (staged) red_add_v4(args.acc + size_t(tok) * args.ldo + f, a, b, c, d);
+  else rs_push4(args, tok, f, a, b, c, d);
 }
 
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
@@ -203,19 +203,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (SWAP) tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
         else tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
       };
-      // all-gather operand: the rank that owns this M tile and the tile's row inside its shard
-      const CUtensorMap* x_map = &tmP;
-      int x_row = tile_p * BM;
-      if constexpr (!SWAP) {
-        if (args.ag_maps != nullptr && args.ag_flags != nullptr) {
-          const int owner = (tile_p * BM) / args.ag_rows;
-          x_map = args.ag_maps + owner;
-          x_row = tile_p * BM - owner * args.ag_rows;
-        }
-      }
       auto load_x = [&](uint8_t* sp, uint64_t* bar, int kx) {
         if constexpr (SWAP) tma_load_2d(sp + Cfg::P_BYTES, &tmQ, bar, kx, tile_q * BN);
-        else tma_load_2d(sp, x_map, bar, kx, x_row);
+        else tma_load_2d(sp, &tmP, bar, kx, tile_p * BM);
       };
       const int pre = min(nkb, Cfg::STAGES);
       for (int i = 0; i < pre; ++i) {  // fresh stages: nothing to wait for
@@ -223,26 +213,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         load_w(smem + i * Cfg::STAGE_BYTES, &full[i], (kb_begin + i) * BK);
       }
       pdl_wait();
-      if constexpr (!SWAP) {
-        if (args.ag_flags != nullptr) {
-          // the owner's shard of this call is published once its counter reaches ours (every
-          // rank publishes once per call); bounded wait
-          const int owner = (tile_p * BM) / args.ag_rows;
-          unsigned int target;
-          asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(target) : "l"(args.ag_own) : "memory");
-          const unsigned int* f = reinterpret_cast<const unsigned int*>(args.ag_flags[owner]);
-          const uint64_t t0 = globaltimer_ns();
-          uint32_t spins = 0;
-          bool ok = true;
-          for (;;) {
-            unsigned int v;
-            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
-            if (int(v - target) >= 0) break;
-            if ((++spins & 1023u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) { ok = false; break; }
-          }
-          if (!ok) atomicOr(&g_gemm_err, 8u);  // loads proceed: the result is flagged as invalid
-        }
-      }
       for (int i = 0; i < nkb; ++i) {
         if (dbg && i == 0) dbg[2] = globaltimer_ns();
         const int s = i % Cfg::STAGES;
@@ -387,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // ---- split-K: publish the fp32 partial to L2; the last CTA of the tile reduces
     bool reduce_here = true;
-    if (nsplit > 1 && EPI != kRedAdd) {
+    if (nsplit > 1 && EPI != kRedAdd && EPI != kRsPush) {
       // column-major partial [BN][BM]: a warp's 32 rows of one column are 128 contiguous bytes
       float* mine = args.ws + (size_t(tile_id) * nsplit + blockIdx.z) * BN * BM + row;
       for (int c = 0; c < BN / CH; ++c) {
@@ -425,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int j = 0; j < CH; ++j) acc[j] += __ldcg(src + size_t(j) * BM);
           }
         };
-        if (nsplit > 1 && EPI != kRedAdd) add_partials(v, c * CH);
+        if (nsplit > 1 && EPI != kRedAdd && EPI != kRsPush) add_partials(v, c * CH);
         if constexpr (EPI == kStore) {
           if constexpr (SWAP) {
             // transpose through shared memory: ostage[token][feature]
@@ -481,6 +451,21 @@ __global__ void __launch_bounds__(kThreads, 1)
               for (int j = 0; j < CH; ++j)
                 if (col0 + j < args.Q_rows / 2)
                   args.out[size_t(t) * args.ldo + col0 + j] = __float2bfloat16(silu(v[j]) * u[j]);
+            }
+          }
+        } else if constexpr (EPI == kRsPush) {
+          if constexpr (SWAP) {
+            float* fstage = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 (token-major)
+#pragma unroll
+            for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
+          } else {
+            const int t = p0 + row;
+            const int col0 = q0 + c * CH;
+            if (t < args.P_rows) {
+#pragma unroll
+              for (int j = 0; j < CH / 4; ++j)
+                if (col0 + 4 * j < args.Q_rows)
+                  rs_emit4(args, nsplit > 1, t, col0 + 4 * j, v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
             }
           }
         } else if constexpr (EPI == kRedAdd) {
@@ -585,6 +570,46 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if constexpr (EPI == kRsPush) {
+        const int tid = threadIdx.x - 64;
+        if constexpr (SWAP) {  // 4 consecutive features of one token per step from the staged tile
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const float* fstage = reinterpret_cast<const float*>(smem);
+          for (int i = tid; i < BN * (BM / 4); i += 128) {
+            const int t = i / (BM / 4), f4 = (i % (BM / 4)) * 4;
+            const int tok = q0 + t, f = p0 + f4;
+            if (tok >= args.Q_rows || f >= args.P_rows) continue;
+            const float4 w = *reinterpret_cast<const float4*>(fstage + t * BM + f4);
+            rs_emit4(args, nsplit > 1, tok, f, w.x, w.y, w.z, w.w);
+          }
+        }
+        if (nsplit > 1) {
+          // the tile's last split reads the reduced partial back, re-zeroes it and pushes it
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (threadIdx.x == 64) {
+            unsigned int* cnt = args.counters + tile_id;
+            const unsigned int old = atomicAdd(cnt, 1u);
+            s_last = old == unsigned(nsplit - 1);
+            if (s_last) *cnt = 0u;
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (s_last) {
+            __threadfence();
+            const int tok0 = SWAP ? q0 : p0, ntok = SWAP ? BN : BM;
+            const int f0 = SWAP ? p0 : q0, nf = SWAP ? BM : BN;
+            const int T = SWAP ? args.Q_rows : args.P_rows, F = SWAP ? args.P_rows : args.Q_rows;
+            for (int i = tid; i < ntok * (nf / 4); i += 128) {
+              const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
+              if (tok >= T || f >= F) continue;
+              float* a = args.acc + size_t(tok) * args.ldo + f;
+              const float4 w = __ldcg(reinterpret_cast<const float4*>(a));
+              *reinterpret_cast<float4*>(a) = make_float4(0.f, 0.f, 0.f, 0.f);
+              rs_push4(args, tok, f, w.x, w.y, w.z, w.w);
+            }
+          }
+        }
+      }
       // swap-AB stores leave through one TMA tensor store of the staged tile
       if constexpr (SWAP && (EPI == kStore || EPI == kSiluMul)) {
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -602,36 +627,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (dbg && threadIdx.x == 64) dbg[6] = globaltimer_ns();
-  if constexpr (EPI == kRedAdd) {
-    if (args.signal != nullptr) {
-      if (epi) asm volatile("bar.sync 1, 128;" ::: "memory");
+  if constexpr (EPI == kRsPush) {
+    // Every CTA counts itself in on every rank once its pushes are issued: the release at system
+    // scope by one thread after the epilogue barrier orders all 128 epilogue threads' stores (and,
+    // for the tile's last split, the staged sums it read) before the count; the owners wait for
+    // world x gridDim CTAs.  No CTA waits for another, no fence drains the whole grid.
+    if (epi) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-        unsigned int prev;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(args.done_ctr) : "memory");
-        if (prev == total - 1) {
-          *args.done_ctr = 0u;
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(args.signal) : "memory");
-        }
-      }
-    } else if (args.ndst > 0) {
-      // every rank's accumulator got this CTA's tile: count the CTA; the last one releases
-      // a flag on every rank (flag index = this rank) at system scope.
-      if (epi) asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (threadIdx.x == 64) {
-        asm volatile("fence.acq_rel.sys;" ::: "memory");
-        const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
-        unsigned int prev;
-        asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(args.done_ctr) : "memory");
-        if (prev == total - 1) {
-          *args.done_ctr = 0u;
-          asm volatile("fence.acq_rel.sys;" ::: "memory");
-          for (int r = 0; r < args.ndst; ++r) {
-            unsigned int* flag = reinterpret_cast<unsigned int*>(args.peer_flags[r]) + args.rank;
-            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
-          }
+        for (int r = 0; r < args.ndst; ++r) {
+          unsigned int* flag = reinterpret_cast<unsigned int*>(args.peer_flags[(args.rank + r) % args.ndst]);
+          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
         }
       }
     }
@@ -1178,20 +1184,27 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }
 
-// Tensor-parallel row-parallel GEMM, first half of the fused all-reduce: the rank-local
-// partial product is reduced into this rank's accumulator exactly as in ``gemm_accum``
-// (split-K CTAs add their fp32 tiles) and the grid's last CTA then releases ``flag += 1``
-// at system scope, so peers know the accumulator is complete and can read it over NVLink
-// (``add_rmsnorm_acc_tp`` sums every rank's accumulator).
-void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, at::Tensor flag,
-                   at::Tensor done_ctr, int64_t splits) {
+// Tensor-parallel row-parallel GEMM fused with the reduce-scatter.  ``a`` [T, K/W] . ``b`` [H, K/W]^T
+// is this rank's partial product.  Token rows [r*own_rows, (r+1)*own_rows) belong to rank r: each
+// complete bf16 row goes straight into rank r's slot for this rank (``slots``: int64 [W] device
+// table of the ranks' slot arrays [W][slot_rows][H] bf16, peer memory included), so a partial
+// crosses NVLink once, as bf16, with plain stores.  Split-K CTAs first reduce into ``staging``
+// (this rank's fp32 [>= T, H], zero between uses; the tile's last CTA re-zeroes it).  The grid's
+// last CTA then bumps every rank's arrival counter (``flags``: int64 [W] device addresses), which
+// the owner's ``tp_norm_allgather`` waits for.
+int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
+                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits) {
   at::Tensor a = a_in.contiguous();
   check_operands(a, b);
   const int M = a.size(0), N = b.size(0);
-  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) >= M && acc.size(1) == N,
-              "accumulator must be contiguous fp32 [>= M, N]");
-  TORCH_CHECK(flag.scalar_type() == at::kInt && done_ctr.scalar_type() == at::kInt, "int32 flag / counter words");
-  if (M == 0) return;
+  TORCH_CHECK(slots.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && slots.numel() == flags.numel() &&
+                  slots.is_cuda() && flags.is_cuda(), "slots / flags: int64 device tables, one entry per rank");
+  TORCH_CHECK(staging.scalar_type() == at::kFloat && staging.is_contiguous() && staging.size(0) >= M &&
+                  staging.size(1) == N, "staging accumulator must be contiguous fp32 [>= T, H]");
+  TORCH_CHECK(own_rows > 0 && own_rows <= slot_rows && int64_t(own_rows) * slots.numel() >= M && rank >= 0 &&
+                  rank < slots.numel(), "every token row needs an owner rank and a slot row");
+  TORCH_CHECK(N % 4 == 0, "output features must be a multiple of 4");
+  if (M == 0) return 0;
   const int kb_total = (int(a.size(1)) + BK - 1) / BK;
   Plan p = plan_gemm(a, b, false, 1);
   int sp = splits > 0 ? int(splits) : 1;
@@ -1201,78 +1214,24 @@ void tp_gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, 
   }
   p.kb_per = (kb_total + sp - 1) / sp;
   p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  TORCH_CHECK(p.tiles_p * p.tiles_q <= kCountersPerSlot || p.splits == 1, "too many split-K tiles");
   GemmArgs args = {};
-  args.acc = acc.data_ptr<float>();
   args.K = a.size(1);
   args.ldo = N;
   args.kb_per_split = p.kb_per;
-  args.acc_plain = p.splits == 1;
-  args.signal = reinterpret_cast<unsigned int*>(flag.data_ptr<int>());
-  args.done_ctr = reinterpret_cast<unsigned int*>(done_ctr.data_ptr<int>());
+  args.acc = staging.data_ptr<float>();
+  args.counters = p.splits > 1 ? counter_slot() : nullptr;
+  args.dsts = reinterpret_cast<const unsigned long long*>(slots.data_ptr<int64_t>());
+  args.ndst = int(slots.numel());
+  args.own_rows = int(own_rows);
+  args.slot_rows = int(slot_rows);
+  args.peer_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
+  args.rank = int(rank);
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
-  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
-}
-
-// Tensor maps of every rank's shard buffer for the all-gather GEMM: ``ptrs`` (CPU int64 [W])
-// are the shard buffers' device addresses (peer mappings for the other ranks), each [rows, cols]
-// bf16.  Returns W 128-byte tensor maps in device memory.
-at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, const at::Tensor& like) {
-  TORCH_CHECK(ptrs.device().is_cpu() && ptrs.scalar_type() == at::kLong, "ptrs: CPU int64");
-  TORCH_CHECK(cols % 8 == 0 && rows % BM == 0, "shard rows must be a multiple of 128, columns of 8");
-  const int W = ptrs.numel();
-  std::vector<CUtensorMap> maps(W);
-  for (int r = 0; r < W; ++r) {
-    const void* p = reinterpret_cast<const void*>(ptrs.data_ptr<int64_t>()[r]);
-    TORCH_CHECK(reinterpret_cast<uintptr_t>(p) % 16 == 0, "shard buffer must be 16-byte aligned");
-    maps[r] = make_kmajor_map(p, rows, cols, BM);
-  }
-  at::Tensor out = at::empty({int64_t(W) * int64_t(sizeof(CUtensorMap))}, like.options().dtype(at::kByte));
-  TORCH_CHECK(reinterpret_cast<uintptr_t>(out.data_ptr()) % 64 == 0, "tensor maps need 64-byte alignment");
-  TORCH_CHECK(cudaMemcpy(out.data_ptr(), maps.data(), W * sizeof(CUtensorMap), cudaMemcpyHostToDevice) == cudaSuccess,
-              "copying tensor maps");
-  return out;
-}
-
-// out[T, N] (or [T, N/2] for the SiLU-mul epilogue) = gather_rows(shards)[T, K] . b[N, K]^T; each
-// M tile waits for its owner's counter (see GemmArgs::ag_flags).  With ``maps`` (one tensor map per
-// rank) the rows are read from the owners' shard buffers and ``local`` is this rank's shard buffer
-// [>= shard_rows, K]; with an empty ``maps`` every owner has pushed its rows into ``local``
-// [>= T, K] at their token positions and the GEMM reads only local memory (a remote tile crosses
-// NVLink once instead of once per column tile).  ``flags`` (int64 [W], device) are the ranks'
-// counters, ``own`` this rank's.
-at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
-                   int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue) {
-  check_operands(local, b);
-  const int K = local.size(1), N = b.size(0);
-  const int W = flags.numel();
-  const bool peer_maps = maps.numel() > 0;
-  TORCH_CHECK(!peer_maps || maps.numel() == int64_t(W) * int64_t(sizeof(CUtensorMap)), "one tensor map per rank");
-  TORCH_CHECK(shard_rows % BM == 0 && T > BM && T <= int64_t(W) * shard_rows &&
-                  (peer_maps ? shard_rows <= local.size(0) : T <= local.size(0)),
-              "all-gather GEMM: shard rows a multiple of 128 within the buffer, 128 < T <= ranks * shard rows");
-  TORCH_CHECK(epilogue == kStore || epilogue == kSiluMul, "gemm_ag: unknown epilogue");
-  at::Tensor out = at::empty({T, epilogue == kSiluMul ? N / 2 : N}, b.options());
-  GemmArgs args = {};
-  args.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
-  args.K = K;
-  args.ldo = out.size(1);
-  const int kb_total = (K + BK - 1) / BK;
-  args.kb_per_split = kb_total;
-  args.P_rows = int(T);
-  args.Q_rows = N;
-  args.ag_maps = peer_maps ? reinterpret_cast<const CUtensorMap*>(maps.data_ptr()) : nullptr;
-  args.ag_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
-  args.ag_own = reinterpret_cast<const unsigned int*>(own.data_ptr<int>());
-  args.ag_rows = int(shard_rows);
-  const CUtensorMap tp = make_kmajor_map(local.data_ptr(), local.size(0), K, BM);
-  const CUtensorMap tq = make_kmajor_map(b.data_ptr(), N, K, 256);
-  const int tiles_p = int((T + BM - 1) / BM), tiles_q = (N + 255) / 256;
-  cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (epilogue == kStore) launch_gemm<256, false, kStore>(tp, tq, tp, args, tiles_p, tiles_q, 1, st);
-  else launch_gemm<256, false, kSiluMul>(tp, tq, tp, args, tiles_p, tiles_q, 1, st);
-  return out;
+  if (p.swap) dispatch_bn<kRsPush, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else launch_gemm<256, false, kRsPush>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  return int64_t(p.tiles_p) * p.tiles_q * p.splits;  // CTAs: each bumps every rank's counter once
 }
 
 at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, int64_t splits) {
@@ -1382,6 +1341,13 @@ int64_t gemm_error_word() {
   const unsigned int z = 0;
   cudaMemcpyToSymbol(g_gemm_err, &z, sizeof(z));
   return v;
+}
+
+// Device address of the error word (read by the per-step status kernel).
+int64_t gemm_error_word_address() {
+  void* p = nullptr;
+  TORCH_CHECK(cudaGetSymbolAddress(&p, g_gemm_err) == cudaSuccess, "error word address");
+  return reinterpret_cast<int64_t>(p);
 }
 
 }  // namespace isb

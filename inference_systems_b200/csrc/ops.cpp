@@ -65,27 +65,32 @@ void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_
 
 int64_t attn_error_word();
 int64_t comm_error_word();
-void tp_gemm_accum(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, at::Tensor flag, at::Tensor done_ctr,
-                   int64_t splits);
+int64_t tp_gemm_rs(const at::Tensor& a, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
+                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits);
+void tp_norm_allgather(const at::Tensor& slots, at::Tensor residual, const at::Tensor& w, const at::Tensor& xdst,
+                       const at::Tensor& ag_flags, at::Tensor ctl, int64_t T, int64_t own_rows, int64_t rank,
+                       int64_t rs_incr, double eps, bool zc, bool wait_gather);
 std::tuple<at::Tensor, at::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const at::Tensor& handle);
 void symm_close(int64_t ptr);
-at::Tensor add_rmsnorm_acc_tp(const at::Tensor& accs, at::Tensor my_acc_other, at::Tensor residual,
-                              const at::Tensor& w, double eps, bool zc, const at::Tensor& flags,
-                              const at::Tensor& my_flag, at::Tensor rows_used, int64_t parity);
 at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,
                         const at::Tensor& peer_flags, at::Tensor my_flags, const at::Tensor& my_xbuf, int64_t rank,
                         int64_t max_rows);
+void comm_set_wait_timeout(int64_t ns);
+at::Tensor step_status(const at::Tensor& toks, const at::Tensor& words);
+int64_t gemm_error_word_address();
+int64_t attn_error_word_address();
+int64_t comm_error_word_address();
+int64_t attn_tc_error_word_address();
+int64_t gdn_error_word_address();
 
-at::Tensor ag_tensor_maps(const at::Tensor& ptrs, int64_t rows, int64_t cols, const at::Tensor& like);
-at::Tensor gemm_ag(const at::Tensor& local, const at::Tensor& maps, const at::Tensor& flags, const at::Tensor& own,
-                   int64_t shard_rows, int64_t T, const at::Tensor& b, int64_t epilogue);
-void sp_rs_norm(const at::Tensor& accs, const at::Tensor& gflags, const at::Tensor& my_gflag, at::Tensor residual,
-                const at::Tensor& w, const at::Tensor& xf, int64_t row_base, double eps, bool zc, at::Tensor done_ctr,
-                at::Tensor ready);
-void sp_publish(const at::Tensor& x, const at::Tensor& xf, int64_t row_base, at::Tensor done_ctr, at::Tensor ready);
-at::Tensor sp_gather(const at::Tensor& xf_local, const at::Tensor& flags, const at::Tensor& my_flag, int64_t S,
-                     int64_t T);
+// Device addresses of the error words, in the bit order of ``step_status`` / ``error_word``:
+// gemm, attention, communication, tensor-core attention, GDN.
+at::Tensor error_word_addresses() {
+  return at::tensor({gemm_error_word_address(), attn_error_word_address(), comm_error_word_address(),
+                     attn_tc_error_word_address(), gdn_error_word_address()},
+                    at::TensorOptions().dtype(at::kLong));
+}
 
 int64_t error_word() {
   return gemm_error_word() | (attn_error_word() << 8) | (comm_error_word() << 16) | (attn_tc_error_word() << 24) |
@@ -127,14 +132,6 @@ TORCH_LIBRARY(isb, m) {
   m.def(
       "attention_decode(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
-  m.def("ag_tensor_maps(Tensor ptrs, int rows, int cols, Tensor like) -> Tensor");
-  m.def("gemm_ag(Tensor local, Tensor maps, Tensor flags, Tensor own, int shard_rows, int T, Tensor b, int epilogue) "
-        "-> Tensor");
-  m.def(
-      "sp_rs_norm(Tensor accs, Tensor gflags, Tensor my_gflag, Tensor(a!) residual, Tensor w, Tensor xf, "
-      "int row_base, float eps, bool zc, Tensor(c!) done_ctr, Tensor(d!) ready) -> ()");
-  m.def("sp_publish(Tensor x, Tensor xf, int row_base, Tensor(b!) done_ctr, Tensor(c!) ready) -> ()");
-  m.def("sp_gather(Tensor xf_local, Tensor flags, Tensor my_flag, int S, int T) -> Tensor");
   m.def(
       "attention_decode_tc(Tensor q, Tensor gate, Tensor k_cache, Tensor v_cache, Tensor context_lens, "
       "Tensor block_tables, float scale, bool gated) -> Tensor");
@@ -152,12 +149,17 @@ TORCH_LIBRARY(isb, m) {
   m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
-  m.def("tp_gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, Tensor(b!) flag, Tensor(c!) done_ctr, int splits=0) -> ()");
+  m.def("tp_gemm_rs(Tensor a, Tensor b, Tensor slots, int slot_rows, Tensor(a!) staging, Tensor flags, "
+        "int rank, int own_rows, int splits=0) -> int");
+  m.def("tp_norm_allgather(Tensor slots, Tensor(b!) residual, Tensor w, Tensor xdst, Tensor ag_flags, "
+        "Tensor(c!) ctl, int T, int own_rows, int rank, int rs_incr, float eps, bool zero_centered, "
+        "bool wait_gather) -> ()");
+  m.def("comm_set_wait_timeout(int ns) -> ()");
+  m.def("step_status(Tensor toks, Tensor words) -> Tensor");
+  m.def("error_word_addresses() -> Tensor");
   m.def("symm_alloc(int nbytes) -> (Tensor, Tensor)");
   m.def("symm_open(Tensor handle) -> int");
   m.def("symm_close(int ptr) -> ()");
-  m.def("add_rmsnorm_acc_tp(Tensor accs, Tensor(a!) my_acc_other, Tensor(b!) residual, Tensor w, float eps, "
-        "bool zero_centered, Tensor flags, Tensor my_flag, Tensor(c!) rows_used, int parity) -> Tensor");
   m.def("xrank_argmax(Tensor val, Tensor idx, Tensor xbufs, Tensor peer_flags, Tensor(a!) my_flags, Tensor my_xbuf, "
         "int rank, int max_rows) -> Tensor");
 }
@@ -179,11 +181,6 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("attn_prepare", &isb::attn_prepare);
   m.impl("attention_decode", &isb::attention_decode);
   m.impl("attention_decode_tc", &isb::attention_decode_tc);
-  m.impl("ag_tensor_maps", &isb::ag_tensor_maps);
-  m.impl("gemm_ag", &isb::gemm_ag);
-  m.impl("sp_rs_norm", &isb::sp_rs_norm);
-  m.impl("sp_publish", &isb::sp_publish);
-  m.impl("sp_gather", &isb::sp_gather);
   m.impl("attention_prefill", &isb::attention_prefill);
   m.impl("quantize_state_int8", &isb::quantize_state_int8);
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);
@@ -192,8 +189,9 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("gemm_accum", &isb::gemm_accum);
   m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);
   m.impl("silu_mul_acc", &isb::silu_mul_acc);
-  m.impl("tp_gemm_accum", &isb::tp_gemm_accum);
-  m.impl("add_rmsnorm_acc_tp", &isb::add_rmsnorm_acc_tp);
+  m.impl("tp_gemm_rs", &isb::tp_gemm_rs);
+  m.impl("tp_norm_allgather", &isb::tp_norm_allgather);
+  m.impl("step_status", &isb::step_status);
   m.impl("xrank_argmax", &isb::xrank_argmax);
 }
 
@@ -202,6 +200,8 @@ TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) {
   m.impl("symm_alloc", &isb::symm_alloc);
   m.impl("symm_open", &isb::symm_open);
   m.impl("symm_close", &isb::symm_close);
+  m.impl("comm_set_wait_timeout", &isb::comm_set_wait_timeout);
+  m.impl("error_word_addresses", &isb::error_word_addresses);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "sm_100a kernels (torch.ops.isb)"; }

@@ -1,31 +1,55 @@
-"""Paged-KV block allocator with a chained-hash prefix index.
+"""Paged KV allocator with a unit-granular prefix index.
 
-Parity: ``nanovllm/engine/block_manager.py:10-484`` -- ref-counted pages and a
-free deque; xxhash64 chained block hashes; a fine-grained prefix index at
-``prefix_match_unit`` granularity whose entries name the page that holds the
-unit's last token (``tail_block_id``) and how many tokens of that page are
-valid; partial-page copy-on-write plans (``KVPageCopy``); speculative
-``reserve_append`` / ``trim_to_sequence_length``; ``reclaimable_blocks``.
+Behavioural parity with ``nanovllm/engine/block_manager.py:10-484``:
+reference-counted 256-token pages; a freed page keeps its cached contents
+until it is handed out again (lazy eviction), so a prefix stays reusable after
+its producer finished; prefix reuse at ``prefix_match_unit`` granularity with a
+partial-page copy-on-write plan when the reusable prefix ends inside a page;
+speculative ``reserve_append`` / ``trim_to_sequence_length``; metrics under the
+same names.
 
-The cached page of a freed block stays indexed until the block is handed out
-again (lazy eviction), exactly like the reference, so a prefix can be reused
-after its producer finished.
+Design:
+* ONE index for both granularities.  Keys are chained hashes of consecutive
+  ``prefix_match_unit``-token units (``unit == block_size`` is the page-level
+  cache); an entry records the unit's tokens (collision guard), the page holding
+  its last token and how many tokens of that page are valid.  Page-aligned
+  entries double as full-page hits, so there is no separate page table.
+* Per-request hash chains are cached on the ``Sequence`` (``unit_hashes``) and
+  only extended as tokens arrive, so probing a waiting request again costs a
+  dictionary lookup per unit, not a rehash of its prompt.
+* Free pages live in an insertion-ordered map: handing out the oldest free page
+  first keeps recently freed (cached) pages around longest, and a cached free
+  page that is reused by a prefix hit leaves the free map in O(1).
+* Reference counts are a numpy array; the pages each index entry points at are
+  tracked per page, so reassigning a page drops exactly its entries.
+* Hashes are xxh3-64 of the unit's int64 token bytes seeded with the previous
+  unit's hash.
 """
 
 from __future__ import annotations
 
-from collections import deque
+from collections import Counter, OrderedDict
 from dataclasses import dataclass
 
 import numpy as np
 import xxhash
 
-from inference_systems_b200.engine.hybrid_prefix_cache import PrefixKVCandidate
 from inference_systems_b200.engine.sequence import Sequence
+
+_SEED_MASK = (1 << 64) - 1
+
+
+def chain_hash(token_ids, prev: int | None = None) -> int:
+    """Hash of one unit of tokens chained to the hash of everything before it."""
+    data = np.asarray(list(token_ids), dtype=np.int64).tobytes()
+    return xxhash.xxh3_64_intdigest(data, seed=0 if prev is None else (prev + 1) & _SEED_MASK)
 
 
 @dataclass(frozen=True, slots=True)
 class PrefixIndexEntry:
+    """One indexed unit: its chained hash, its tokens, the page holding its last token and how
+    many tokens of that page (from its start) are valid up to the unit's end."""
+
     prefix_hash: int
     unit_token_ids: tuple[int, ...]
     tail_block_id: int
@@ -34,355 +58,355 @@ class PrefixIndexEntry:
 
 @dataclass(frozen=True, slots=True)
 class KVPageCopy:
+    """Copy-on-write plan: the first ``num_tokens`` rows of page ``source_block_id`` go to
+    ``destination_block_id`` before the request writes the rest of that page."""
+
     source_block_id: int
     destination_block_id: int
     num_tokens: int
 
 
-class Block:
-    __slots__ = ("block_id", "ref_count", "hash", "token_ids", "prefix_hashes")
+@dataclass(frozen=True, slots=True)
+class PrefixKVCandidate:
+    """A reusable KV prefix of a request: ``boundary_tokens`` tokens, of which the first
+    ``num_cached_blocks`` pages are shared whole and, when ``tail_valid_tokens`` is less than a
+    page, the rest comes from copying that many rows of ``tail_block_id``."""
 
-    def __init__(self, block_id: int):
-        self.block_id = block_id
-        self.ref_count = 0
-        self.hash = -1
-        self.token_ids: list[int] = []
-        self.prefix_hashes: set[int] = set()
-
-    def update(self, h: int, token_ids: list[int]) -> None:
-        self.hash = h
-        self.token_ids = list(token_ids)
-
-    def reset(self) -> None:
-        self.ref_count = 1
-        self.hash = -1
-        self.token_ids = []
-        self.prefix_hashes.clear()
+    num_cached_blocks: int
+    boundary_tokens: int
+    prefix_hash: int
+    tail_block_id: int
+    tail_valid_tokens: int = 0
 
 
-def chain_hash(token_ids, prefix: int = -1) -> int:
-    h = xxhash.xxh64()
-    if prefix != -1:
-        h.update(prefix.to_bytes(8, "little"))
-    h.update(np.asarray(list(token_ids), dtype=np.int64).tobytes())
-    return h.intdigest()
+class _FreePages:
+    """Free page ids in release order (oldest first), with O(1) removal of any page."""
+
+    def __init__(self, n: int):
+        self._order: OrderedDict[int, None] = OrderedDict((i, None) for i in range(n))
+
+    def __len__(self) -> int:
+        return len(self._order)
+
+    def __contains__(self, page: int) -> bool:
+        return page in self._order
+
+    def pop_oldest(self) -> int:
+        if not self._order:
+            raise RuntimeError("no free KV blocks")
+        return self._order.popitem(last=False)[0]
+
+    def take(self, page: int) -> None:
+        del self._order[page]
+
+    def release(self, page: int) -> None:
+        self._order[page] = None
 
 
 class BlockManager:
     def __init__(self, num_blocks: int, block_size: int, prefix_match_unit: int | None = None):
+        if num_blocks <= 0 or block_size <= 0:
+            raise ValueError("block count and size must be positive")
         self.block_size = block_size
         self.prefix_match_unit = prefix_match_unit or block_size
         if self.prefix_match_unit <= 0 or block_size % self.prefix_match_unit:
             raise ValueError("prefix_match_unit must divide block_size")
-        self.blocks = [Block(i) for i in range(num_blocks)]
-        self.hash_to_block_id: dict[int, int] = {}
-        self.hash_to_prefix_entry: dict[int, PrefixIndexEntry] = {}
-        self.free_block_ids: deque[int] = deque(range(num_blocks))
-        self.used_block_ids: set[int] = set()
+        self.num_blocks = num_blocks
+        self.refs = np.zeros(num_blocks, dtype=np.int32)
+        self.free = _FreePages(num_blocks)
+        self.index: dict[int, PrefixIndexEntry] = {}
+        # unit hashes whose entry was registered on each page (stale ones are skipped on reuse)
+        self.page_units: list[set[int]] = [set() for _ in range(num_blocks)]
+        # page-aligned unit hash last registered on each page: the page "holds a cached block"
+        self.page_hash: list[int | None] = [None] * num_blocks
         self.reset_metrics()
 
-    compute_hash = staticmethod(chain_hash)
+    # ------------------------------------------------------------------ metrics
+    def reset_metrics(self) -> None:
+        self.stats: Counter = Counter()
+
+    @property
+    def prefix_cache_evictions(self) -> int:
+        return self.stats["prefix_cache_evictions"]
+
+    @property
+    def cached_block_reassignments(self) -> int:
+        return self.stats["cached_block_reassignments"]
+
+    @property
+    def duplicate_cache_registrations(self) -> int:
+        return self.stats["duplicate_cache_registrations"]
+
+    @property
+    def partial_prefix_cow_allocations(self) -> int:
+        return self.stats["partial_prefix_cow_allocations"]
 
     @property
     def fine_grained(self) -> bool:
         return self.prefix_match_unit < self.block_size
 
-    def reset_metrics(self) -> None:
-        self.prefix_cache_evictions = 0
-        self.cached_block_reassignments = 0
-        self.duplicate_cache_registrations = 0
-        self.partial_prefix_cow_allocations = 0
+    @property
+    def num_free_blocks(self) -> int:
+        return len(self.free)
 
-    # ------------------------------------------------------- raw pages
-    def _allocate_block(self) -> int:
-        block_id = self.free_block_ids.popleft()
-        block = self.blocks[block_id]
-        assert block.ref_count == 0
-        if block.hash != -1:
-            self.cached_block_reassignments += 1
-            if self.hash_to_block_id.get(block.hash) == block_id:
-                del self.hash_to_block_id[block.hash]
-                self.prefix_cache_evictions += 1
-        for ph in tuple(block.prefix_hashes):
-            entry = self.hash_to_prefix_entry.get(ph)
-            if entry is not None and entry.tail_block_id == block_id:
-                del self.hash_to_prefix_entry[ph]
-                self.prefix_cache_evictions += 1
-        block.reset()
-        self.used_block_ids.add(block_id)
-        return block_id
+    @property
+    def num_used_blocks(self) -> int:
+        return self.num_blocks - len(self.free)
 
-    def _deallocate_block(self, block_id: int) -> None:
-        assert self.blocks[block_id].ref_count == 0
-        self.used_block_ids.remove(block_id)
-        self.free_block_ids.append(block_id)
+    @property
+    def used_block_ids(self) -> frozenset[int]:
+        return frozenset(int(i) for i in np.flatnonzero(self.refs > 0))
 
-    def _reference_block(self, block_id: int) -> None:
-        block = self.blocks[block_id]
-        if block_id in self.used_block_ids:
-            block.ref_count += 1
-        else:
-            block.ref_count = 1
-            self.free_block_ids.remove(block_id)
-            self.used_block_ids.add(block_id)
+    def ref_count(self, page: int) -> int:
+        return int(self.refs[page])
 
-    def _release_block(self, block_id: int) -> None:
-        block = self.blocks[block_id]
-        block.ref_count -= 1
-        if block.ref_count == 0:
-            self._deallocate_block(block_id)
+    @property
+    def num_cached_blocks(self) -> int:
+        """Pages (free or in use) that still hold a registered full-page unit."""
+        return sum(h is not None for h in self.page_hash)
 
-    # ------------------------------------------------- prefix lookup
-    def _full_block_prefix(self, seq: Sequence):
-        """Yield ``(block_index, hash, block_id)`` along the cached full-block chain."""
-        h = -1
-        for i in range(seq.num_blocks - 1):
-            tokens = seq.block(i)
-            h = chain_hash(tokens, h)
-            bid = self.hash_to_block_id.get(h, -1)
-            if bid == -1 or self.blocks[bid].token_ids != tokens:
-                return
-            yield i, h, bid
+    @property
+    def num_reachable_cached_blocks(self) -> int:
+        """Pages that an index lookup can still reach."""
+        if self.fine_grained:
+            return len({e.tail_block_id for e in self.index.values()})
+        return sum(1 for p, h in enumerate(self.page_hash)
+                   if h is not None and (e := self.index.get(h)) is not None and e.tail_block_id == p)
 
+    def metrics(self) -> dict:
+        return {"prefix_cache_evictions": self.prefix_cache_evictions,
+                "cached_block_reassignments": self.cached_block_reassignments,
+                "duplicate_cache_registrations": self.duplicate_cache_registrations,
+                "partial_prefix_cow_allocations": self.partial_prefix_cow_allocations,
+                "cached_blocks": self.num_cached_blocks}
+
+    # ------------------------------------------------------------------- pages
+    def _fresh_page(self) -> int:
+        """Hand out the oldest free page, dropping whatever the index still knew about it."""
+        page = self.free.pop_oldest()
+        if self.page_units[page] or self.page_hash[page] is not None:
+            self.stats["cached_block_reassignments"] += 1
+            for h in self.page_units[page]:
+                e = self.index.get(h)
+                if e is not None and e.tail_block_id == page:
+                    del self.index[h]
+                    self.stats["prefix_cache_evictions"] += 1
+            self.page_units[page].clear()
+            self.page_hash[page] = None
+        self.refs[page] = 1
+        return page
+
+    def _share(self, page: int) -> None:
+        """One more reference to a cached page (revived from the free map if unreferenced)."""
+        if self.refs[page] == 0:
+            self.free.take(page)
+        self.refs[page] += 1
+
+    def _drop(self, page: int) -> None:
+        self.refs[page] -= 1
+        if self.refs[page] == 0:
+            self.free.release(page)
+        elif self.refs[page] < 0:
+            raise RuntimeError(f"page {page} released more often than referenced")
+
+    # ----------------------------------------------------------------- hashing
+    def _units(self, seq: Sequence, n_units: int) -> list[int]:
+        """The first ``n_units`` chained unit hashes of ``seq`` (cached on the request)."""
+        u = self.prefix_match_unit
+        chain = seq.unit_hashes.setdefault(u, [])
+        while len(chain) < n_units:
+            k = len(chain)
+            chain.append(chain_hash(seq.token_ids[k * u:(k + 1) * u], chain[-1] if chain else None))
+        return chain[:n_units]
+
+    def _lookup(self, seq: Sequence, k: int, h: int) -> PrefixIndexEntry | None:
+        u = self.prefix_match_unit
+        e = self.index.get(h)
+        if e is None or list(e.unit_token_ids) != seq.token_ids[k * u:(k + 1) * u]:
+            return None
+        return e
+
+    def _reusable_units(self, seq: Sequence) -> list[PrefixIndexEntry]:
+        """Indexed units along ``seq``'s chain, leaving at least one token to compute."""
+        u = self.prefix_match_unit
+        limit = (seq.num_tokens - 1) // u
+        out = []
+        for k, h in enumerate(self._units(seq, limit)):
+            e = self._lookup(seq, k, h)
+            if e is None:
+                break
+            out.append(e)
+        return out
+
+    def _full_page_chain(self, seq: Sequence, pages: int) -> list[int]:
+        """Page ids of the first ``pages`` whole pages along ``seq``'s indexed chain."""
+        per = self.block_size // self.prefix_match_unit
+        hashes = self._units(seq, pages * per)
+        return [self.index[hashes[(p + 1) * per - 1]].tail_block_id for p in range(pages)]
+
+    def hash_blocks(self, seq: Sequence) -> None:
+        """Index the units completed by the scheduled chunk of ``seq``."""
+        u, bs = self.prefix_match_unit, self.block_size
+        first = seq.num_cached_tokens // u
+        done = (seq.num_cached_tokens + seq.num_scheduled_tokens) // u
+        if done <= first:
+            return
+        hashes = self._units(seq, done)
+        for k in range(first, done):
+            end = (k + 1) * u
+            page = seq.block_table[(end - 1) // bs]
+            h = hashes[k]
+            prev = self.index.get(h)
+            toks = tuple(seq.token_ids[k * u:end])
+            if prev is not None and prev.tail_block_id != page and prev.unit_token_ids == toks:
+                self.stats["duplicate_cache_registrations"] += 1
+            self.index[h] = PrefixIndexEntry(h, toks, page, end % bs or bs)
+            self.page_units[page].add(h)
+            if end % bs == 0:
+                self.page_hash[page] = h
+
+    # ------------------------------------------------------------------ probes
     def can_allocate(self, seq: Sequence, use_prefix_cache: bool = True) -> int:
-        """Cached full blocks reusable by ``seq`` or -1 if pages are short."""
+        """Whole cached pages ``seq`` would reuse, or -1 when free pages are short."""
         if not use_prefix_cache:
-            return 0 if len(self.free_block_ids) >= seq.num_blocks else -1
-        cached, new = 0, seq.num_blocks
-        for _, _, bid in self._full_block_prefix(seq):
-            cached += 1
-            if bid in self.used_block_ids:
-                new -= 1
-        return cached if len(self.free_block_ids) >= new else -1
+            return 0 if len(self.free) >= seq.num_blocks else -1
+        per = self.block_size // self.prefix_match_unit
+        pages = len(self._reusable_units(seq)) // per
+        need = seq.num_blocks - sum(self.refs[p] > 0 for p in self._full_page_chain(seq, pages))
+        return pages if len(self.free) >= need else -1
 
     def find_prefix_candidates(self, seq: Sequence) -> list[PrefixKVCandidate]:
-        """All reusable prefix boundaries, longest first (one unit is always left to compute)."""
-        if self.fine_grained:
-            return self._find_fine_candidates(seq)
-        out = [PrefixKVCandidate(num_cached_blocks=i + 1, boundary_tokens=(i + 1) * self.block_size,
-                                 prefix_hash=h, tail_block_id=bid, tail_valid_tokens=self.block_size)
-               for i, h, bid in self._full_block_prefix(seq)]
-        out.reverse()
-        return out
-
-    def _find_fine_candidates(self, seq: Sequence) -> list[PrefixKVCandidate]:
-        unit = self.prefix_match_unit
-        limit = ((seq.num_tokens - 1) // unit) * unit
-        h = -1
+        """Every reusable prefix boundary of ``seq``, longest first."""
+        u, bs = self.prefix_match_unit, self.block_size
         out = []
-        for start in range(0, limit, unit):
-            end = start + unit
-            toks = tuple(seq.token_ids[start:end])
-            h = chain_hash(toks, h)
-            entry = self.hash_to_prefix_entry.get(h)
-            if entry is None or entry.unit_token_ids != toks:
-                break
-            out.append(PrefixKVCandidate(num_cached_blocks=end // self.block_size, boundary_tokens=end,
-                                         prefix_hash=h, tail_block_id=entry.tail_block_id,
-                                         tail_valid_tokens=end % self.block_size or self.block_size))
+        for k, e in enumerate(self._reusable_units(seq)):
+            end = (k + 1) * u
+            out.append(PrefixKVCandidate(end // bs, end, e.prefix_hash, e.tail_block_id, e.tail_valid_tokens))
         out.reverse()
         return out
 
-    def _full_prefix_block_ids(self, seq: Sequence, num_full_blocks: int) -> list[int]:
-        if not self.fine_grained:
-            ids, h = [], -1
-            for i in range(num_full_blocks):
-                h = chain_hash(seq.block(i), h)
-                ids.append(self.hash_to_block_id[h])
-            return ids
-        unit = self.prefix_match_unit
-        per_block = self.block_size // unit
-        ids, h = [], -1
-        for u in range(num_full_blocks * per_block):
-            h = chain_hash(seq.token_ids[u * unit:(u + 1) * unit], h)
-            if (u + 1) % per_block == 0:
-                ids.append(self.hash_to_prefix_entry[h].tail_block_id)
-        return ids
-
-    def can_allocate_with_prefix(self, seq: Sequence, num_cached_blocks: int) -> bool:
-        if num_cached_blocks < 0 or num_cached_blocks >= seq.num_blocks:
-            raise ValueError("invalid cached block count")
-        if num_cached_blocks and not any(c.num_cached_blocks == num_cached_blocks
-                                         for c in self.find_prefix_candidates(seq)):
-            return False
-        need = seq.num_blocks
-        h = -1
-        for i in range(num_cached_blocks):
-            h = chain_hash(seq.block(i), h)
-            if self.hash_to_block_id[h] in self.used_block_ids:
-                need -= 1
-        return len(self.free_block_ids) >= need
+    def _pages_needed(self, seq: Sequence, candidate: PrefixKVCandidate | None) -> int:
+        if candidate is None:
+            return seq.num_blocks
+        need = seq.num_blocks - sum(self.refs[p] > 0 for p in self._full_page_chain(seq, candidate.num_cached_blocks))
+        if candidate.tail_valid_tokens != self.block_size and self.refs[candidate.tail_block_id] == 0:
+            need += 1  # the copy source must stay pinned (out of the free map) until it is copied
+        return need
 
     def can_allocate_candidate(self, seq: Sequence, candidate: PrefixKVCandidate | None) -> bool:
-        if candidate is None:
-            return len(self.free_block_ids) >= seq.num_blocks
-        need = seq.num_blocks
-        for bid in self._full_prefix_block_ids(seq, candidate.num_cached_blocks):
-            if bid in self.used_block_ids:
-                need -= 1
-        partial = candidate.tail_valid_tokens != self.block_size
-        if partial and candidate.tail_block_id not in self.used_block_ids:
-            need += 1  # the COW source must stay pinned until its rows are copied
-        return len(self.free_block_ids) >= need
+        return len(self.free) >= self._pages_needed(seq, candidate)
 
-    # ------------------------------------------------------ allocation
+    def can_allocate_with_prefix(self, seq: Sequence, num_cached_blocks: int) -> bool:
+        if not 0 <= num_cached_blocks < seq.num_blocks:
+            raise ValueError("invalid cached block count")
+        cand = None
+        if num_cached_blocks:
+            cand = next((c for c in self.find_prefix_candidates(seq) if c.num_cached_blocks == num_cached_blocks
+                         and c.tail_valid_tokens == self.block_size), None)
+            if cand is None:
+                return False
+        return self.can_allocate_candidate(seq, cand)
+
+    def prefix_metadata_at_boundary(self, seq: Sequence, boundary_tokens: int) -> PrefixKVCandidate:
+        """The index entry of ``seq``'s prefix ending at ``boundary_tokens`` (must be indexed)."""
+        u, bs = self.prefix_match_unit, self.block_size
+        if boundary_tokens <= 0 or boundary_tokens % u:
+            raise ValueError("prefix boundary must align to prefix_match_unit")
+        page_idx = (boundary_tokens - 1) // bs
+        if page_idx >= len(seq.block_table):
+            raise ValueError("prefix boundary has no allocated block")
+        page = seq.block_table[page_idx]
+        k = boundary_tokens // u - 1
+        h = self._units(seq, k + 1)[k]
+        e = self._lookup(seq, k, h)
+        if e is None or e.tail_block_id != page:
+            raise ValueError("prefix boundary has not been indexed")
+        return PrefixKVCandidate(boundary_tokens // bs, boundary_tokens, h, page, e.tail_valid_tokens)
+
+    def reclaimable_blocks(self, seq: Sequence) -> int:
+        """Pages that preempting ``seq`` would free (those it does not share)."""
+        return sum(self.refs[p] == 1 for p in set(seq.block_table))
+
+    # -------------------------------------------------------------- allocation
+    def allocate(self, seq: Sequence, num_cached_blocks: int) -> None:
+        if seq.block_table:
+            raise RuntimeError("sequence already holds pages")
+        shared = self._full_page_chain(seq, num_cached_blocks)
+        for p in shared:
+            self._share(p)
+        seq.block_table.extend(shared)
+        while len(seq.block_table) < seq.num_blocks:
+            seq.block_table.append(self._fresh_page())
+        seq.num_cached_tokens = num_cached_blocks * self.block_size
+
     def allocate_candidate(self, seq: Sequence, candidate: PrefixKVCandidate | None) -> KVPageCopy | None:
-        """Allocate pages for ``seq``; pin and return a COW plan for a partial tail page."""
-        assert not seq.block_table
+        """Pages for ``seq`` reusing ``candidate``; a boundary inside a page pins that page and
+        returns the copy plan (release it with ``release_cow_source`` once copied)."""
         if candidate is None:
             self.allocate(seq, 0)
             return None
-        full_ids = self._full_prefix_block_ids(seq, candidate.num_cached_blocks)
+        if seq.block_table:
+            raise RuntimeError("sequence already holds pages")
         partial = candidate.tail_valid_tokens != self.block_size
         pinned = False
         try:
-            for bid in full_ids:
-                self._reference_block(bid)
-                seq.block_table.append(bid)
+            for p in self._full_page_chain(seq, candidate.num_cached_blocks):
+                self._share(p)
+                seq.block_table.append(p)
             if partial:
-                self._reference_block(candidate.tail_block_id)
+                self._share(candidate.tail_block_id)
                 pinned = True
             while len(seq.block_table) < seq.num_blocks:
-                seq.block_table.append(self._allocate_block())
-            seq.num_cached_tokens = candidate.boundary_tokens
-            if not partial:
-                return None
-            self.partial_prefix_cow_allocations += 1
-            return KVPageCopy(candidate.tail_block_id, seq.block_table[candidate.num_cached_blocks],
-                              candidate.tail_valid_tokens)
+                seq.block_table.append(self._fresh_page())
         except Exception:
             if pinned:
-                self._release_block(candidate.tail_block_id)
+                self._drop(candidate.tail_block_id)
             self.deallocate(seq)
             raise
+        seq.num_cached_tokens = candidate.boundary_tokens
+        if not partial:
+            return None
+        self.stats["partial_prefix_cow_allocations"] += 1
+        return KVPageCopy(candidate.tail_block_id, seq.block_table[candidate.num_cached_blocks],
+                          candidate.tail_valid_tokens)
 
     def release_cow_source(self, page_copy: KVPageCopy) -> None:
-        self._release_block(page_copy.source_block_id)
-
-    def prefix_metadata_at_boundary(self, seq: Sequence, boundary_tokens: int) -> PrefixKVCandidate:
-        if boundary_tokens <= 0 or boundary_tokens % self.prefix_match_unit:
-            raise ValueError("prefix boundary must align to prefix_match_unit")
-        bidx = (boundary_tokens - 1) // self.block_size
-        if bidx >= len(seq.block_table):
-            raise ValueError("prefix boundary has no allocated block")
-        bid = seq.block_table[bidx]
-        if self.fine_grained:
-            h = -1
-            for s in range(0, boundary_tokens, self.prefix_match_unit):
-                h = chain_hash(seq.token_ids[s:s + self.prefix_match_unit], h)
-            entry = self.hash_to_prefix_entry.get(h)
-            if entry is None or entry.tail_block_id != bid:
-                raise ValueError("prefix boundary has not been indexed")
-            return PrefixKVCandidate(boundary_tokens // self.block_size, boundary_tokens, h, bid,
-                                     boundary_tokens % self.block_size or self.block_size)
-        block = self.blocks[bid]
-        if block.hash == -1:
-            raise ValueError("prefix boundary block has not been hashed")
-        return PrefixKVCandidate(bidx + 1, boundary_tokens, block.hash, bid, self.block_size)
-
-    def allocate(self, seq: Sequence, num_cached_blocks: int) -> None:
-        assert not seq.block_table
-        h = -1
-        for i in range(num_cached_blocks):
-            h = chain_hash(seq.block(i), h)
-            bid = self.hash_to_block_id[h]
-            self._reference_block(bid)
-            seq.block_table.append(bid)
-        for _ in range(num_cached_blocks, seq.num_blocks):
-            seq.block_table.append(self._allocate_block())
-        seq.num_cached_tokens = num_cached_blocks * self.block_size
+        self._drop(page_copy.source_block_id)
 
     def deallocate(self, seq: Sequence) -> None:
-        for bid in reversed(seq.block_table):
-            self._release_block(bid)
-        seq.num_cached_tokens = 0
+        for p in reversed(seq.block_table):
+            self._drop(p)
         seq.block_table.clear()
+        seq.num_cached_tokens = 0
 
-    def reclaimable_blocks(self, seq: Sequence) -> int:
-        return sum(self.blocks[b].ref_count == 1 for b in set(seq.block_table))
-
+    # ------------------------------------------------------------------ growth
     def can_append(self, seq: Sequence) -> bool:
-        return len(self.free_block_ids) >= (len(seq) % self.block_size == 1)
+        """Room for the token just appended (a new page when it starts one)."""
+        return len(self.free) >= (1 if len(seq) % self.block_size == 1 else 0)
 
     def may_append(self, seq: Sequence) -> None:
         if len(seq) % self.block_size == 1:
-            seq.block_table.append(self._allocate_block())
+            seq.block_table.append(self._fresh_page())
 
     def additional_blocks_for_append(self, seq: Sequence, num_tokens: int) -> int:
         if num_tokens < 0:
             raise ValueError("num_tokens must be non-negative")
-        final = (len(seq) + num_tokens + self.block_size - 1) // self.block_size
-        return max(final - len(seq.block_table), 0)
+        return max(-(-(len(seq) + num_tokens) // self.block_size) - len(seq.block_table), 0)
 
     def can_reserve_append(self, seq: Sequence, num_tokens: int) -> bool:
-        return len(self.free_block_ids) >= self.additional_blocks_for_append(seq, num_tokens)
+        return len(self.free) >= self.additional_blocks_for_append(seq, num_tokens)
 
     def reserve_append(self, seq: Sequence, num_tokens: int) -> None:
         need = self.additional_blocks_for_append(seq, num_tokens)
-        if len(self.free_block_ids) < need:
+        if len(self.free) < need:
             raise RuntimeError("insufficient KV blocks for speculative append")
         for _ in range(need):
-            seq.block_table.append(self._allocate_block())
+            seq.block_table.append(self._fresh_page())
 
     def trim_to_sequence_length(self, seq: Sequence) -> None:
+        """Give back speculative pages beyond the sequence's committed length."""
         while len(seq.block_table) > seq.num_blocks:
-            bid = seq.block_table.pop()
-            block = self.blocks[bid]
-            block.ref_count -= 1
-            if block.ref_count != 0:
+            p = seq.block_table.pop()
+            if self.refs[p] != 1:
                 raise RuntimeError("speculative tail block is unexpectedly shared")
-            self._deallocate_block(bid)
-
-    # --------------------------------------------------------- hashing
-    def hash_blocks(self, seq: Sequence) -> None:
-        """Index the pages completed by the scheduled chunk of ``seq``."""
-        if self.fine_grained:
-            self._hash_units(seq)
-            return
-        start = seq.num_cached_tokens // self.block_size
-        end = (seq.num_cached_tokens + seq.num_scheduled_tokens) // self.block_size
-        if start == end:
-            return
-        h = self.blocks[seq.block_table[start - 1]].hash if start > 0 else -1
-        for i in range(start, end):
-            block = self.blocks[seq.block_table[i]]
-            tokens = seq.block(i)
-            h = chain_hash(tokens, h)
-            prev = self.hash_to_block_id.get(h)
-            if prev is not None and prev != block.block_id and self.blocks[prev].token_ids == tokens:
-                self.duplicate_cache_registrations += 1
-            block.update(h, tokens)
-            self.hash_to_block_id[h] = block.block_id
-
-    def _hash_units(self, seq: Sequence) -> None:
-        unit = self.prefix_match_unit
-        done = (seq.num_cached_tokens + seq.num_scheduled_tokens) // unit
-        first_new = seq.num_cached_tokens // unit
-        h = -1
-        for u in range(done):
-            s, e = u * unit, (u + 1) * unit
-            toks = tuple(seq.token_ids[s:e])
-            h = chain_hash(toks, h)
-            if u < first_new:
-                continue
-            bidx = (e - 1) // self.block_size
-            bid = seq.block_table[bidx]
-            entry = PrefixIndexEntry(h, toks, bid, e % self.block_size or self.block_size)
-            prev = self.hash_to_prefix_entry.get(h)
-            if prev is not None and prev.tail_block_id != bid:
-                self.duplicate_cache_registrations += 1
-            self.hash_to_prefix_entry[h] = entry
-            self.blocks[bid].prefix_hashes.add(h)
-            if e % self.block_size == 0:
-                self.blocks[bid].update(h, seq.block(bidx))
-                self.hash_to_block_id[h] = bid
-
-    @property
-    def num_cached_blocks(self) -> int:
-        return sum(b.hash != -1 for b in self.blocks)
-
-    @property
-    def num_reachable_cached_blocks(self) -> int:
-        if self.fine_grained:
-            return len({e.tail_block_id for e in self.hash_to_prefix_entry.values()})
-        return len(set(self.hash_to_block_id.values()))
+            self._drop(p)

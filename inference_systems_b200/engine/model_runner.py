@@ -54,6 +54,20 @@ def count_graph_kernels(handle: int) -> int:
         return -1
 
 
+class DeviceErrorStatus(RuntimeError):
+    """A kernel of the last step reported an error (a bounded wait ran out or an index was out of
+    range): its outputs, and possibly the state it wrote, are not valid."""
+
+
+ERROR_WORD_MODULES = ("gemm", "attention", "tp-communication", "tensor-core attention", "gdn")
+
+
+def describe_error_word(word: int) -> str:
+    parts = [f"{name}={(word >> (8 * i)) & 0xFF:#x}" for i, name in enumerate(ERROR_WORD_MODULES)
+             if (word >> (8 * i)) & 0xFF]
+    return ", ".join(parts) or f"{word:#x}"
+
+
 def _bucket_sizes(max_bs: int) -> list[int]:
     sizes = [1, 2, 4, 8, 16, 24, 32, 48, 64, 80, 96, 112, 128, 160, 192, 224, 256, 320, 384, 448, 512]
     out = [s for s in sizes if s < max_bs] + [max_bs]
@@ -114,6 +128,14 @@ class ModelRunner:
         else:
             self.comm = None
 
+        # Device addresses of every kernel module's error word: each step appends their state to
+        # the sampled tokens (``step_status``), so the one device->host copy per step carries it.
+        if self.device.type == "cuda":
+            from inference_systems_b200 import ops
+            self.error_addrs = ops.cuda_ops().error_word_addresses().to(self.device)
+        else:
+            self.error_addrs = None
+        self.device_errors = 0
         if self.device.type == "cuda":
             spec_rows = config.max_num_seqs * (self.num_speculative_tokens + 1)
             self.model.set_accumulator(max(config.max_num_batched_tokens, config.max_num_seqs, spec_rows), self.device)
@@ -333,10 +355,43 @@ class ModelRunner:
         self._last_hidden = hidden
         return self.model.sample(last, temps, rng)
 
+    def with_status(self, toks: torch.Tensor) -> torch.Tensor:
+        """``[toks | status]`` on GPUs: the last int32 has bit i set when kernel module i's error
+        word is nonzero (``ERROR_WORD_MODULES`` order); unchanged on CPU."""
+        if self.error_addrs is None:
+            return toks
+        from inference_systems_b200 import ops
+        return ops.cuda_ops().step_status(toks.to(torch.int32).contiguous(), self.error_addrs)
+
+    def check_status(self, host: torch.Tensor) -> None:
+        """Raise ``DeviceErrorStatus`` (rank 0) when the step's status word is nonzero.  The detailed
+        words are read (and cleared) first so the message names the failing kernels; workers only
+        count the error, rank 0 fails the step for every request."""
+        if self.error_addrs is None or int(host[-1]) == 0:
+            return
+        self.device_errors += 1
+        word = self._read_error_words()
+        if self.rank == 0:
+            raise DeviceErrorStatus(f"device error in the last step ({describe_error_word(word)}); "
+                                    "its outputs are not valid")
+
+    def last_hidden_host(self) -> torch.Tensor | None:
+        """Final-norm hidden states ``[T, H]`` (fp32, CPU) of the last eagerly run forward pass
+        (prefill chunks always run eagerly); used by tests that score tokens against logits."""
+        h = getattr(self, "_last_hidden", None)
+        return None if h is None else h.float().cpu()
+
+    @staticmethod
+    def _read_error_words() -> int:
+        """Every module's error word, packed 8 bits per module and cleared (synchronous)."""
+        return int(torch.ops.isb.error_word())
+
     def _tokens_to_host(self, toks: torch.Tensor, n: int) -> list[int]:
-        out = toks[:n].to("cpu", non_blocking=False)
-        self.d2h_bytes += out.numel() * out.element_size()
-        return out.tolist()
+        """Copy the sampled tokens (and, on GPUs, the status word after them) to the host."""
+        host = toks.to("cpu", non_blocking=False)
+        self.d2h_bytes += host.numel() * host.element_size()
+        self.check_status(host)
+        return host[:n].tolist()
 
     @torch.inference_mode()
     def run(self, seqs: list[Sequence], is_prefill: bool, internal_boundaries: dict | None = None):
@@ -364,6 +419,7 @@ class ModelRunner:
                 self.mtp_driver.after_prefill(seqs, batch, self._last_hidden, toks, rng)
             if marks:
                 self._capture_internal_states(batch, marks)
+            toks = self.with_status(toks)
         self.sample_step += 1
         out = self._tokens_to_host(toks, b)
         self.forward_calls += 1
@@ -435,7 +491,7 @@ class ModelRunner:
             torch.cuda.synchronize(self.device)
             g = torch.cuda.CUDAGraph(keep_graph=True)
             with torch.cuda.graph(g, pool=pool):
-                toks = self._forward_sample(batch, rng, temps)
+                toks = self.with_status(self._forward_sample(batch, rng, temps))
             g.instantiate()
             if pool is None:
                 pool = g.pool()
@@ -521,6 +577,7 @@ class ModelRunner:
             "kv_cow_bytes": self.cow_bytes,
             "h2d_bytes": self.h2d_bytes,
             "d2h_bytes": self.d2h_bytes,
+            "device_errors": self.device_errors,
             "num_kvcache_blocks": self.config.num_kvcache_blocks,
             "phase_profile": self.profiler.metrics(),
         }
@@ -558,6 +615,20 @@ class ModelRunner:
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             ms = float(t.item())
         return ms
+
+    @torch.inference_mode()
+    def breakdown_replays(self, batch_size: int, path: str, n: int = 3) -> None:
+        """Kernel-time table of ``n`` decode-graph replays, profiled on every rank at once (the
+        tensor-parallel exchanges need every rank replaying); rank 0 writes ``path``."""
+        from inference_systems_b200.engine.profiler import kernel_time_table
+        g = self.graphs[self._graph_bucket(batch_size)]
+        if self.world_size > 1:
+            dist.barrier()
+        text = kernel_time_table(g.replay, n)
+        if self.rank == 0:
+            os.makedirs(os.path.dirname(path) or ".", exist_ok=True)
+            with open(path, "w") as f:
+                f.write(text)
 
     def graph_kernel_count(self, batch_size: int) -> int:
         return self.graph_kernels.get(self._graph_bucket(batch_size), -1)

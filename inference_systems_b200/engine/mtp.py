@@ -303,7 +303,7 @@ class MTPDriver:
             new = self._draft_steps(tok, m_sel, (pos_d + acc).to(torch.int32), bt_d, caps_d, st_d, rng_d,
                                     slots_host or [], max_k)
             self.drafts.index_copy_(0, st_d.long(), new)
-        return torch.cat((v.reshape(-1).to(torch.int32), acc))
+        return r.with_status(torch.cat((v.reshape(-1).to(torch.int32), acc)))
 
     # ---------------------------------------------------------- graphs
     def _bucket(self, b: int) -> int | None:
@@ -355,9 +355,10 @@ class MTPDriver:
             self.graph_replays += 1
             tb = bucket * (k + 1)
             host = out_dev.to("cpu")
+            r.d2h_bytes += host.numel() * 4
+            r.check_status(host)
             vals = host[:tb].view(bucket, k + 1)[:b].tolist()
             accs = host[tb:tb + b].tolist()
-            r.d2h_bytes += host.numel() * 4
         else:
             flat = self._pack(seqs, b)
             meta = r._upload(flat)
@@ -365,6 +366,7 @@ class MTPDriver:
             max_k = max(len(s) for s in seqs) + k
             host = self._round_device(meta, b, slots_host, max_k).to("cpu")
             r.d2h_bytes += host.numel() * 4
+            r.check_status(host)
             t = b * (k + 1)
             vals = host[:t].view(b, k + 1).tolist()
             accs = host[t:].tolist()

@@ -1,41 +1,62 @@
-"""GDN recurrent/conv state slots, prefix checkpoints and all-rank transactions.
+"""GDN recurrent/conv state slots, prefix checkpoints and all-rank checkpoint transactions.
 
-Parity: ``nanovllm/engine/state_manager.py``:
+Behavioural parity with ``nanovllm/engine/state_manager.py``: a fixed pool of
+per-request recurrent (fp32) and conv states with one extra scratch slot for
+CUDA-graph padding rows (``:17-325``); a memory-budgeted pool of immutable
+prefix checkpoints stored as fp32, bf16 or int8 with fp32 scales per
+(layer, head, key channel) (``:328-546``); capture and restore as all-rank
+transactions that either happen on every tensor-parallel rank or on none, with
+only rank 0 raising (``:549-640``).
 
-* ``HybridStateManager`` (``:17-325``): fixed pools
-  ``recurrent [L_gdn, slots+1, Hv, Dk, Dv] fp32`` and
-  ``conv [L_gdn, slots+1, conv_dim, K-1]``; the extra slot is a scratch slot
-  that padded CUDA-graph rows point at; allocate/free zero the slot;
-  snapshot/restore; ReplaySSM commit.
-* ``HybridPrefixCheckpointPool`` (``:328-546``): budgeted immutable copies in
-  fp32 / bf16 / int8 (fp32 scale per (layer, head, key-channel)); capture,
-  restore (dequantise once), free, rollback.
-* ``transactional_capture/restore_prefix_checkpoint`` (``:549-640``): local
-  prepare, all-reduce MIN of success, slot-id agreement (MIN == MAX), roll
-  back everywhere on failure, only rank 0 raises.
-
-Design difference: there is no gather/scatter around a forward pass -- the
-kernels read and write the pools in place by slot id (the reference copies
-the batch's states out and back every step, ``state_manager.py:99-143``).
+Design (this module's own):
+* Kernels read and write the state pools in place by slot id; nothing is
+  gathered into or scattered out of a batch tensor around a forward pass.
+* ``SlotAllocator`` hands out the smallest free id (a heap), so every rank
+  allocates the same ids in the same order and a rolled-back capture simply
+  returns its id -- no queue order to restore.
+* Checkpoint storage formats are codec objects (``Fp32Codec``, ``Bf16Codec``,
+  ``Int8Codec``) that own their tensors; the pool only manages slots and budget.
+* ``RankVote`` wraps the consensus collectives (all-reduce MIN for "everyone
+  succeeded", MIN == MAX for "everyone chose the same slot"), on the NCCL group
+  when it is the default, else on CPU tensors over gloo.
 """
 
 from __future__ import annotations
 
-from collections import deque
-from dataclasses import dataclass
+import heapq
 
 import torch
 import torch.distributed as dist
 
 
-@dataclass(frozen=True, slots=True)
-class HybridStateSnapshot:
-    slot_ids: torch.Tensor
-    recurrent_states: torch.Tensor
-    conv_states: torch.Tensor
+class SlotAllocator:
+    """Ids ``0..n-1``; allocation takes the smallest free id."""
+
+    def __init__(self, n: int):
+        self._free = list(range(n))
+        self.used: set[int] = set()
+
+    def __len__(self) -> int:
+        return len(self._free)
+
+    def take(self) -> int:
+        if not self._free:
+            raise RuntimeError("no free slots")
+        slot = heapq.heappop(self._free)
+        self.used.add(slot)
+        return slot
+
+    def give_back(self, slot: int) -> None:
+        if slot not in self.used:
+            raise ValueError(f"slot {slot} is not allocated")
+        self.used.remove(slot)
+        heapq.heappush(self._free, slot)
 
 
 class HybridStateManager:
+    """``recurrent [L_gdn, slots + 1, Hv, Dk, Dv]`` fp32 and ``conv [L_gdn, slots + 1, conv_dim, K - 1]``
+    pools; slot ``slots`` is the scratch slot that padded rows of a captured batch point at."""
+
     def __init__(self, *, max_num_seqs: int, num_linear_layers: int, num_value_heads: int, key_head_dim: int,
                  value_head_dim: int, conv_dim: int, conv_kernel_size: int, conv_dtype: torch.dtype,
                  device: torch.device | str):
@@ -46,299 +67,271 @@ class HybridStateManager:
         self.max_num_seqs = max_num_seqs
         self.num_linear_layers = num_linear_layers
         self.scratch_slot_id = max_num_seqs
-        n = max_num_seqs + 1
-        self.recurrent_states = torch.zeros(num_linear_layers, n, num_value_heads, key_head_dim, value_head_dim,
-                                            dtype=torch.float32, device=device)
-        self.conv_states = torch.zeros(num_linear_layers, n, conv_dim, conv_kernel_size - 1, dtype=conv_dtype,
-                                       device=device)
-        self.free_slot_ids: deque[int] = deque(range(max_num_seqs))
-        self.used_slot_ids: set[int] = set()
+        self.recurrent_states = torch.zeros(num_linear_layers, max_num_seqs + 1, num_value_heads, key_head_dim,
+                                            value_head_dim, dtype=torch.float32, device=device)
+        self.conv_states = torch.zeros(num_linear_layers, max_num_seqs + 1, conv_dim, conv_kernel_size - 1,
+                                       dtype=conv_dtype, device=device)
+        self.slots = SlotAllocator(max_num_seqs)
 
     @property
     def can_allocate(self) -> bool:
-        return bool(self.free_slot_ids)
+        return len(self.slots) > 0
+
+    @property
+    def used_slot_ids(self) -> set[int]:
+        return self.slots.used
 
     def layer_pools(self, j: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.recurrent_states[j], self.conv_states[j]
 
-    def _zero_slot(self, slot: int) -> None:
+    def clear_slot(self, slot: int) -> None:
         self.recurrent_states[:, slot].zero_()
         self.conv_states[:, slot].zero_()
 
     def allocate(self, sequence=None) -> int:
-        if not self.free_slot_ids:
-            raise RuntimeError("no free GDN state slots")
+        """A zeroed slot (assigned to ``sequence.state_slot`` when given)."""
         if sequence is not None and getattr(sequence, "state_slot", None) is not None:
             raise ValueError("sequence already owns a state slot")
-        slot = self.free_slot_ids.popleft()
-        self._zero_slot(slot)
-        self.used_slot_ids.add(slot)
+        if not self.can_allocate:
+            raise RuntimeError("no free GDN state slots")
+        slot = self.slots.take()
+        self.clear_slot(slot)
         if sequence is not None:
             sequence.state_slot = slot
         return slot
 
     def free(self, sequence_or_slot) -> None:
-        if isinstance(sequence_or_slot, int):
-            slot, seq = sequence_or_slot, None
-        else:
-            seq = sequence_or_slot
-            slot = getattr(seq, "state_slot", None)
-            if slot is None:
-                return
-        if slot not in self.used_slot_ids:
+        """Zero and release a slot (given directly or as ``sequence.state_slot``)."""
+        seq = None if isinstance(sequence_or_slot, int) else sequence_or_slot
+        slot = sequence_or_slot if seq is None else getattr(seq, "state_slot", None)
+        if slot is None:
+            return
+        if slot not in self.slots.used:
             raise ValueError(f"state slot {slot} is not allocated")
-        self._zero_slot(slot)
-        self.used_slot_ids.remove(slot)
-        self.free_slot_ids.append(slot)
+        self.clear_slot(slot)
+        self.slots.give_back(slot)
         if seq is not None:
             seq.state_slot = None
 
     def reset_scratch(self) -> None:
-        self._zero_slot(self.scratch_slot_id)
-
-    def snapshot(self, slot_ids: torch.Tensor) -> HybridStateSnapshot:
-        idx = slot_ids.to(self.recurrent_states.device, torch.long)
-        return HybridStateSnapshot(idx.clone(), self.recurrent_states.index_select(1, idx).clone(),
-                                   self.conv_states.index_select(1, idx).clone())
-
-    def restore(self, snap: HybridStateSnapshot) -> None:
-        idx = snap.slot_ids.to(self.recurrent_states.device, torch.long)
-        self.recurrent_states.index_copy_(1, idx, snap.recurrent_states.to(self.recurrent_states.dtype))
-        self.conv_states.index_copy_(1, idx, snap.conv_states.to(self.conv_states.dtype))
-
-    def restore_accepted_prefixes(self, snapshots: list[HybridStateSnapshot], accepted_lengths: torch.Tensor) -> None:
-        """Row ``b`` gets ``snapshots[accepted_lengths[b]]`` (``snapshots[0]`` = pre-draft)."""
-        if not snapshots:
-            raise ValueError("at least the pre-draft snapshot is required")
-        base = snapshots[0].slot_ids
-        if accepted_lengths.numel() != base.numel():
-            raise ValueError("accepted_lengths must have one value per snapshotted slot")
-        for s in snapshots:
-            if not torch.equal(s.slot_ids, base):
-                raise ValueError("all speculative snapshots must use the same slot order")
-        acc = accepted_lengths.to(torch.long).tolist()
-        if any(a < 0 or a >= len(snapshots) for a in acc):
-            raise ValueError("accepted length has no matching state snapshot")
-        rec = torch.stack([snapshots[a].recurrent_states[:, b] for b, a in enumerate(acc)], dim=1)
-        conv = torch.stack([snapshots[a].conv_states[:, b] for b, a in enumerate(acc)], dim=1)
-        self.restore(HybridStateSnapshot(base, rec, conv))
-
-    def replay_recurrent(self, slot_ids: torch.Tensor, keys: torch.Tensor, deltas: torch.Tensor,
-                         log_decays: torch.Tensor, commit_lengths: torch.Tensor, *, num_steps: int) -> None:
-        """Fold the accepted prefix of compact transitions into each slot's state.
-
-        ``keys [L, B*steps, Hv, Dk]``, ``deltas [L, B*steps, Hv, Dv]``,
-        ``log_decays [L, B*steps, Hv]``; row ``b`` folds its first
-        ``commit_lengths[b]`` steps: ``S <- exp(g) S + k delta^T``.
-        """
-        from inference_systems_b200 import ops
-        if num_steps <= 0:
-            raise ValueError("replay requires at least one transition")
-        b = slot_ids.numel()
-        if commit_lengths.shape != (b,):
-            raise ValueError("commit_lengths must have one value per slot")
-        for t, name in ((keys, "key"), (deltas, "delta"), (log_decays, "decay")):
-            if tuple(t.shape[:2]) != (self.num_linear_layers, b * num_steps):
-                raise ValueError(f"replay {name} shape does not match layers x batch x steps")
-        if not commit_lengths.is_cuda and bool(((commit_lengths < 1) | (commit_lengths > num_steps)).any()):
-            raise ValueError("commit length is outside the replay window")
-        ops.gdn_replay_commit(self.recurrent_states, slot_ids, keys, deltas, log_decays, commit_lengths, num_steps)
-
-    def commit_conv_history(self, slot_ids: torch.Tensor, conv_history: torch.Tensor, boundaries: torch.Tensor, *,
-                            num_steps: int) -> None:
-        """``conv[l, slot_b] <- conv_history[l, b*steps + boundaries[b]]``."""
-        from inference_systems_b200 import ops
-        if conv_history.shape[0] != self.num_linear_layers:
-            raise ValueError("conv history layer count does not match state pool")
-        ops.gdn_conv_commit(self.conv_states, conv_history, slot_ids, boundaries, num_steps)
+        self.clear_slot(self.scratch_slot_id)
 
     def memory_bytes(self) -> int:
-        return (self.recurrent_states.numel() * self.recurrent_states.element_size()
-                + self.conv_states.numel() * self.conv_states.element_size())
+        return sum(t.numel() * t.element_size() for t in (self.recurrent_states, self.conv_states))
 
     def bytes_per_slot(self) -> int:
-        return (self.recurrent_states[:, 0].numel() * self.recurrent_states.element_size()
-                + self.conv_states[:, 0].numel() * self.conv_states.element_size())
+        return sum(t[:, 0].numel() * t.element_size() for t in (self.recurrent_states, self.conv_states))
+
+
+# -------------------------------------------------------------------- checkpoint codecs
+
+
+class Fp32Codec:
+    name, dtype = "fp32", torch.float32
+
+    def __init__(self, capacity: int, shape: tuple[int, ...], device):
+        self.data = torch.zeros(capacity, *shape, dtype=self.dtype, device=device)
+
+    @classmethod
+    def bytes_per(cls, shape: tuple[int, ...]) -> int:
+        n = 1
+        for d in shape:
+            n *= d
+        return n * torch.tensor([], dtype=cls.dtype).element_size()
+
+    def encode(self, slot: int, state: torch.Tensor) -> None:
+        self.data[slot].copy_(state)
+
+    def decode(self, slot: int, out: torch.Tensor) -> None:
+        out.copy_(self.data[slot])
+
+    def clear(self, slot: int) -> None:
+        self.data[slot].zero_()
+
+    def nbytes(self) -> int:
+        return self.data.numel() * self.data.element_size()
+
+
+class Bf16Codec(Fp32Codec):
+    name, dtype = "bf16", torch.bfloat16
+
+
+class Int8Codec(Fp32Codec):
+    """int8 values with one fp32 scale per (layer, head, key channel): quantised along Dv."""
+
+    name, dtype = "int8", torch.int8
+
+    def __init__(self, capacity: int, shape: tuple[int, ...], device):
+        super().__init__(capacity, shape, device)
+        self.scales = torch.zeros(capacity, *shape[:-1], 1, dtype=torch.float32, device=device)
+
+    @classmethod
+    def bytes_per(cls, shape: tuple[int, ...]) -> int:
+        rows = 1
+        for d in shape[:-1]:
+            rows *= d
+        return rows * shape[-1] + rows * 4
+
+    def encode(self, slot: int, state: torch.Tensor) -> None:
+        from inference_systems_b200 import ops
+        ops.quantize_state_int8(state, self.data[slot], self.scales[slot])
+
+    def decode(self, slot: int, out: torch.Tensor) -> None:
+        from inference_systems_b200 import ops
+        ops.dequantize_state_int8(self.data[slot], self.scales[slot], out)
+
+    def clear(self, slot: int) -> None:
+        super().clear(slot)
+        self.scales[slot].zero_()
+
+    def nbytes(self) -> int:
+        return super().nbytes() + self.scales.numel() * 4
+
+
+_CODECS = {c.name: c for c in (Fp32Codec, Bf16Codec, Int8Codec)}
 
 
 class HybridPrefixCheckpointPool:
-    """Fixed-budget checkpoint copies of request states (fp32 / bf16 / int8)."""
-
-    _DTYPES = ("fp32", "bf16", "int8")
+    """Immutable checkpoint copies of request states within a memory budget."""
 
     def __init__(self, state_manager: HybridStateManager, memory_budget_bytes: int, checkpoint_dtype: str = "fp32"):
-        if checkpoint_dtype not in self._DTYPES:
-            raise ValueError(f"checkpoint dtype must be one of {self._DTYPES}, got {checkpoint_dtype}")
-        sm = state_manager
-        self.state_manager = sm
+        if checkpoint_dtype not in _CODECS:
+            raise ValueError(f"checkpoint dtype must be one of {tuple(_CODECS)}, got {checkpoint_dtype}")
+        sm = self.state_manager = state_manager
         self.checkpoint_dtype = checkpoint_dtype
-        rs, cs = sm.recurrent_states.shape, sm.conv_states.shape
-        self.recurrent_shape = (rs[0], *rs[2:])
-        self.conv_shape = (cs[0], *cs[2:])
-        rec_elems = sm.recurrent_states[:, 0].numel()
+        self.recurrent_shape = (sm.recurrent_states.shape[0], *sm.recurrent_states.shape[2:])
+        self.conv_shape = (sm.conv_states.shape[0], *sm.conv_states.shape[2:])
+        codec = _CODECS[checkpoint_dtype]
         conv_bytes = sm.conv_states[:, 0].numel() * sm.conv_states.element_size()
-        self.scale_shape = None
-        scale_bytes = 0
-        if checkpoint_dtype == "fp32":
-            store, rec_bytes = torch.float32, rec_elems * 4
-        elif checkpoint_dtype == "bf16":
-            store, rec_bytes = torch.bfloat16, rec_elems * 2
-        else:
-            store, rec_bytes = torch.int8, rec_elems
-            # one fp32 scale per (layer, head, key channel): quantise along Dv
-            self.scale_shape = (*self.recurrent_shape[:3], 1)
-            scale_bytes = self.scale_shape[0] * self.scale_shape[1] * self.scale_shape[2] * 4
-        self.recurrent_bytes_per_checkpoint = rec_bytes
-        self.scale_bytes_per_checkpoint = scale_bytes
-        self.conv_bytes_per_checkpoint = conv_bytes
-        self.bytes_per_checkpoint = rec_bytes + scale_bytes + conv_bytes
+        self.bytes_per_checkpoint = codec.bytes_per(self.recurrent_shape) + conv_bytes
         self.capacity = memory_budget_bytes // self.bytes_per_checkpoint
         if self.capacity <= 0:
             raise ValueError("hybrid prefix checkpoint budget is smaller than one checkpoint: "
                              f"budget={memory_budget_bytes}, required={self.bytes_per_checkpoint}")
         dev = sm.recurrent_states.device
-        self.recurrent_checkpoints = torch.zeros(self.capacity, *self.recurrent_shape, dtype=store, device=dev)
-        self.recurrent_scales = (torch.zeros(self.capacity, *self.scale_shape, dtype=torch.float32, device=dev)
-                                 if self.scale_shape is not None else None)
-        self.conv_checkpoints = torch.zeros(self.capacity, *self.conv_shape, dtype=sm.conv_states.dtype, device=dev)
-        self.free_checkpoint_slots: deque[int] = deque(range(self.capacity))
-        self.used_checkpoint_slots: set[int] = set()
+        self.recurrent = codec(self.capacity, self.recurrent_shape, dev)
+        self.conv = torch.zeros(self.capacity, *self.conv_shape, dtype=sm.conv_states.dtype, device=dev)
+        self.slots = SlotAllocator(self.capacity)
 
     @property
     def can_allocate(self) -> bool:
-        return bool(self.free_checkpoint_slots)
+        return len(self.slots) > 0
 
-    def _store(self, ck: int, rec: torch.Tensor, conv: torch.Tensor) -> None:
-        from inference_systems_b200 import ops
-        if self.checkpoint_dtype == "int8":
-            ops.quantize_state_int8(rec, self.recurrent_checkpoints[ck], self.recurrent_scales[ck])
-        else:
-            self.recurrent_checkpoints[ck].copy_(rec)
-        self.conv_checkpoints[ck].copy_(conv)
+    @property
+    def used_checkpoint_slots(self) -> set[int]:
+        return self.slots.used
 
-    def _zero(self, ck: int) -> None:
-        self.recurrent_checkpoints[ck].zero_()
-        if self.recurrent_scales is not None:
-            self.recurrent_scales[ck].zero_()
-        self.conv_checkpoints[ck].zero_()
-
-    def _take(self) -> int:
-        if not self.free_checkpoint_slots:
-            raise RuntimeError("no free hybrid prefix checkpoint slots")
-        return self.free_checkpoint_slots.popleft()
+    @property
+    def free_checkpoint_slots(self) -> int:
+        return len(self.slots)
 
     def capture(self, request_state_slot: int) -> int:
+        """Checkpoint the current state of a request's slot; returns the checkpoint slot."""
         sm = self.state_manager
         if request_state_slot not in sm.used_slot_ids:
             raise ValueError("cannot checkpoint an unallocated request state slot")
         return self.capture_tensors(sm.recurrent_states[:, request_state_slot], sm.conv_states[:, request_state_slot])
 
     def capture_tensors(self, recurrent_state: torch.Tensor, conv_state: torch.Tensor) -> int:
-        if tuple(recurrent_state.shape) != tuple(self.recurrent_shape):
+        """Checkpoint explicit state tensors (states recorded inside a prefill chunk)."""
+        if tuple(recurrent_state.shape) != self.recurrent_shape:
             raise ValueError(f"internal recurrent checkpoint must have shape {self.recurrent_shape}")
-        if tuple(conv_state.shape) != tuple(self.conv_shape):
+        if tuple(conv_state.shape) != self.conv_shape:
             raise ValueError(f"internal conv checkpoint must have shape {self.conv_shape}")
-        ck = self._take()
+        if not self.can_allocate:
+            raise RuntimeError("no free hybrid prefix checkpoint slots")
+        ck = self.slots.take()
         try:
-            self._store(ck, recurrent_state, conv_state)
+            self.recurrent.encode(ck, recurrent_state)
+            self.conv[ck].copy_(conv_state)
         except Exception:
-            self._zero(ck)
-            self.free_checkpoint_slots.appendleft(ck)
+            self._clear(ck)
+            self.slots.give_back(ck)
             raise
-        self.used_checkpoint_slots.add(ck)
         return ck
 
     def restore(self, checkpoint_slot: int, request_state_slot: int) -> None:
-        from inference_systems_b200 import ops
         sm = self.state_manager
-        if checkpoint_slot not in self.used_checkpoint_slots:
+        if checkpoint_slot not in self.slots.used:
             raise ValueError("hybrid prefix checkpoint slot is not allocated")
         if request_state_slot not in sm.used_slot_ids:
             raise ValueError("request state slot is not allocated")
-        dst = sm.recurrent_states[:, request_state_slot]
-        if self.checkpoint_dtype == "int8":
-            ops.dequantize_state_int8(self.recurrent_checkpoints[checkpoint_slot],
-                                      self.recurrent_scales[checkpoint_slot], dst)
-        else:
-            dst.copy_(self.recurrent_checkpoints[checkpoint_slot])
-        sm.conv_states[:, request_state_slot].copy_(self.conv_checkpoints[checkpoint_slot])
+        self.recurrent.decode(checkpoint_slot, sm.recurrent_states[:, request_state_slot])
+        sm.conv_states[:, request_state_slot].copy_(self.conv[checkpoint_slot])
+
+    def _clear(self, ck: int) -> None:
+        self.recurrent.clear(ck)
+        self.conv[ck].zero_()
 
     def free(self, checkpoint_slot: int) -> None:
-        if checkpoint_slot not in self.used_checkpoint_slots:
+        if checkpoint_slot not in self.slots.used:
             raise ValueError("hybrid prefix checkpoint slot is not allocated")
-        self._zero(checkpoint_slot)
-        self.used_checkpoint_slots.remove(checkpoint_slot)
-        self.free_checkpoint_slots.append(checkpoint_slot)
+        self._clear(checkpoint_slot)
+        self.slots.give_back(checkpoint_slot)
 
-    def rollback_capture(self, checkpoint_slot: int) -> None:
-        """Undo an unpublished capture and restore the deterministic free order."""
-        if checkpoint_slot not in self.used_checkpoint_slots:
-            raise ValueError("hybrid prefix checkpoint slot is not allocated")
-        self._zero(checkpoint_slot)
-        self.used_checkpoint_slots.remove(checkpoint_slot)
-        self.free_checkpoint_slots = deque(sorted([*self.free_checkpoint_slots, checkpoint_slot]))
+    # an unpublished capture is undone exactly like an eviction (the allocator keeps the order)
+    rollback_capture = free
 
     def memory_bytes(self) -> int:
-        n = self.recurrent_checkpoints.numel() * self.recurrent_checkpoints.element_size()
-        if self.recurrent_scales is not None:
-            n += self.recurrent_scales.numel() * 4
-        return n + self.conv_checkpoints.numel() * self.conv_checkpoints.element_size()
+        return self.recurrent.nbytes() + self.conv.numel() * self.conv.element_size()
 
 
-# ------------------------------------------------------------ transactions
-def _consensus_device(ref: torch.Tensor) -> torch.device:
-    if dist.is_initialized() and dist.get_backend() == "nccl":
-        return ref.device
-    return torch.device("cpu")
+# ------------------------------------------------------------------------ transactions
 
 
-def _multi_rank() -> bool:
-    return dist.is_initialized() and dist.get_world_size() > 1
+class RankVote:
+    """Consensus over the default process group (a no-op with one rank)."""
 
+    def __init__(self, like: torch.Tensor):
+        self.active = dist.is_initialized() and dist.get_world_size() > 1
+        nccl = self.active and dist.get_backend() == "nccl"
+        self.device = like.device if nccl else torch.device("cpu")
+        self.rank = dist.get_rank() if dist.is_initialized() else 0
 
-def _all_ok(ok: bool, ref: torch.Tensor) -> bool:
-    flag = torch.tensor(1 if ok else 0, dtype=torch.int32, device=_consensus_device(ref))
-    dist.all_reduce(flag, op=dist.ReduceOp.MIN)
-    return int(flag.item()) == 1
+    def all_ok(self, ok: bool) -> bool:
+        if not self.active:
+            return ok
+        t = torch.tensor(int(ok), dtype=torch.int32, device=self.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        return bool(t.item())
 
-
-def _same_everywhere(value: int, ref: torch.Tensor) -> bool:
-    dev = _consensus_device(ref)
-    lo = torch.tensor(value, dtype=torch.int64, device=dev)
-    hi = lo.clone()
-    dist.all_reduce(lo, op=dist.ReduceOp.MIN)
-    dist.all_reduce(hi, op=dist.ReduceOp.MAX)
-    return int(lo.item()) == int(hi.item())
+    def all_equal(self, value: int) -> bool:
+        if not self.active:
+            return True
+        lo = torch.tensor(value, dtype=torch.int64, device=self.device)
+        hi = lo.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        return int(lo.item()) == int(hi.item())
 
 
 def transactional_capture_prefix_checkpoint(pool: HybridPrefixCheckpointPool, request_state_slot: int, *,
                                             recurrent_state: torch.Tensor | None = None,
                                             conv_state: torch.Tensor | None = None) -> int:
-    """Capture on every rank or on none; returns the agreed slot (-1 on non-zero ranks after failure)."""
-    slot, err = None, None
+    """Capture on every rank or on none.  Every rank votes before anyone raises; on failure every
+    rank rolls back and rank 0 raises (other ranks return -1).  Ranks must agree on the slot id."""
+    vote = RankVote(pool.conv)
+    slot, error = None, None
     try:
-        if recurrent_state is None and conv_state is None:
-            slot = pool.capture(request_state_slot)
-        elif recurrent_state is not None and conv_state is not None:
-            slot = pool.capture_tensors(recurrent_state, conv_state)
-        else:
+        if (recurrent_state is None) != (conv_state is None):
             raise ValueError("both internal checkpoint tensors are required")
-    except Exception as exc:  # join the vote before raising
-        err = exc
-    if not _multi_rank():
-        if err is not None:
-            raise err
+        slot = (pool.capture(request_state_slot) if recurrent_state is None
+                else pool.capture_tensors(recurrent_state, conv_state))
+    except Exception as exc:  # noqa: BLE001 - voted on below
+        error = exc
+    if not vote.active:
+        if error is not None:
+            raise error
         return slot
-    ref = pool.recurrent_checkpoints
-    if not _all_ok(err is None, ref):
+    if not vote.all_ok(error is None):
         if slot is not None:
             pool.rollback_capture(slot)
-        if dist.get_rank() == 0:
-            raise RuntimeError("hybrid prefix capture rolled back on all ranks")
+        if vote.rank == 0:
+            raise RuntimeError("hybrid prefix capture rolled back on all ranks") from error
         return -1
-    if not _same_everywhere(slot, ref):
+    if not vote.all_equal(slot):
         pool.rollback_capture(slot)
-        if dist.get_rank() == 0:
+        if vote.rank == 0:
             raise RuntimeError("hybrid prefix checkpoint slot IDs diverged across ranks")
         return -1
     return slot
@@ -346,18 +339,18 @@ def transactional_capture_prefix_checkpoint(pool: HybridPrefixCheckpointPool, re
 
 def transactional_restore_prefix_checkpoint(pool: HybridPrefixCheckpointPool, checkpoint_slot: int,
                                             request_state_slot: int) -> None:
-    """Restore on every rank or roll every rank back to the pre-restore state."""
+    """Restore on every rank, or put every rank's slot back as it was (rank 0 raises)."""
     sm = pool.state_manager
-    rec_backup = sm.recurrent_states[:, request_state_slot].clone()
-    conv_backup = sm.conv_states[:, request_state_slot].clone()
-    err = None
+    vote = RankVote(pool.conv)
+    saved = (sm.recurrent_states[:, request_state_slot].clone(), sm.conv_states[:, request_state_slot].clone())
+    error = None
     try:
         pool.restore(checkpoint_slot, request_state_slot)
-    except Exception as exc:
-        err = exc
-    ok = _all_ok(err is None, pool.recurrent_checkpoints) if _multi_rank() else err is None
-    if not ok:
-        sm.recurrent_states[:, request_state_slot].copy_(rec_backup)
-        sm.conv_states[:, request_state_slot].copy_(conv_backup)
-        if not dist.is_initialized() or dist.get_rank() == 0:
-            raise RuntimeError("hybrid prefix restore rolled back on all ranks")
+    except Exception as exc:  # noqa: BLE001 - voted on below
+        error = exc
+    if vote.all_ok(error is None):
+        return
+    sm.recurrent_states[:, request_state_slot].copy_(saved[0])
+    sm.conv_states[:, request_state_slot].copy_(saved[1])
+    if vote.rank == 0:
+        raise RuntimeError("hybrid prefix restore rolled back on all ranks") from error

@@ -27,7 +27,6 @@ import torch
 from torch import nn
 
 from inference_systems_b200 import ops
-from inference_systems_b200.parallel.comm import ShardedActivation
 from inference_systems_b200.models.registry import ModelCapabilities
 from inference_systems_b200.ops.reference import pack_gate_up
 from inference_systems_b200.utils.context import ForwardBatch
@@ -65,19 +64,15 @@ class ColumnScratch:
 
     def project(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor | None:
         t, n = x.shape[0], w.shape[0]
-        if (self.buf is None or isinstance(x, ShardedActivation) or not x.is_cuda or t > self.rows
-                or t * n > self.buf.numel()):
+        if self.buf is None or not x.is_cuda or t > self.rows or t * n > self.buf.numel():
             return None
         acc = self.buf[: t * n].view(t, n)
         ops.linear_accumulate(x, w, acc)
         return acc
 
 
-def _col_linear(x, w: torch.Tensor, silu_mul: bool = False) -> torch.Tensor:
-    """Column-parallel projection of a replicated ``[T, H]`` tensor or of a token-sharded
-    activation (all-gather fused into the GEMM)."""
-    if isinstance(x, ShardedActivation):
-        return x.comm.sp_linear(x, w, silu_mul)
+def _col_linear(x: torch.Tensor, w: torch.Tensor, silu_mul: bool = False) -> torch.Tensor:
+    """Column-parallel projection of a replicated ``[T, H]`` activation."""
     return ops.linear_silu_mul(x, w) if silu_mul else ops.linear(x, w)
 
 
@@ -410,10 +405,6 @@ class HybridCausalLM(nn.Module):
         """
         cos_sin = self.cos_sin(batch.input_ids.device)
         layers = self.layers
-        T = batch.input_ids.shape[0]
-        S = self.comm.sp_rows(T) if self.comm is not None and self.tp.size > 1 else 0
-        if S:
-            return self._forward_sharded(batch, kv_caches, state_pools, cos_sin, T, S)
         residual, x = ops.embed_rmsnorm(batch.input_ids, self.embed_tokens, layers[0].input_layernorm, self.eps,
                                         self.hybrid)
         attn_j = gdn_j = 0
@@ -434,40 +425,6 @@ class HybridCausalLM(nn.Module):
             next_norm = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm
             x = self._row_parallel(y, layer.mlp.down, residual, next_norm)
         return x
-
-    def _forward_sharded(self, batch: ForwardBatch, kv_caches: list, state_pools: list | None,
-                         cos_sin: torch.Tensor, T: int, S: int) -> torch.Tensor:
-        """The same layers with the residual stream split by tokens over the TP group: each
-        row-parallel GEMM ends in a reduce-scatter + residual + RMSNorm on this rank's rows, and
-        each column-parallel GEMM gathers its input rows from their owners."""
-        comm, layers = self.comm, self.layers
-        lo, hi = comm.sp_range(T, S)
-        if hi > lo:
-            residual, x0 = ops.embed_rmsnorm(batch.input_ids[lo:hi], self.embed_tokens, layers[0].input_layernorm,
-                                             self.eps, self.hybrid)
-        else:
-            residual = torch.empty(0, self.hidden_size, dtype=self.embed_tokens.dtype, device=batch.input_ids.device)
-            x0 = torch.empty_like(residual)
-        x = comm.sp_publish(x0, T, S)
-        attn_j = gdn_j = 0
-        for i, layer in enumerate(layers):
-            if layer.is_linear:
-                rec = batch.gdn_verify[gdn_j] if batch.gdn_verify is not None else None
-                hist = None
-                if batch.gdn_history is not None:
-                    h = batch.gdn_history
-                    hist = (h["rows"], h["rec"][gdn_j], h["conv"][gdn_j])
-                y = layer.mixer(x, batch, state_pools[gdn_j], rec, hist)
-                gdn_j += 1
-            else:
-                y = layer.mixer(x, batch, kv_caches[attn_j], cos_sin)
-                attn_j += 1
-            x = comm.sp_row_parallel_norm(y, layer.mixer_out_weight(), residual, layer.post_attention_layernorm,
-                                          self.eps, self.hybrid, T, S)
-            y = layer.mlp.forward_pre_down(x)
-            next_norm = layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm
-            x = comm.sp_row_parallel_norm(y, layer.mlp.down, residual, next_norm, self.eps, self.hybrid, T, S)
-        return comm.sp_gather(x)
 
     def sample(self, hidden: torch.Tensor, temperatures: torch.Tensor, rng: torch.Tensor) -> torch.Tensor:
         """Vocab-parallel LM head fused with greedy / Gumbel-max sampling -> token ids ``[B]`` int32."""

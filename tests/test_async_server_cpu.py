@@ -105,6 +105,44 @@ def test_async_failure_fails_streams_and_rejects_new(ckpt):
     asyncio.run(main())
 
 
+def test_device_error_status_fails_the_step_and_the_streams(ckpt):
+    """A nonzero status word after a step (a kernel's bounded wait ran out) makes
+    ``LLMEngine.step`` raise ``DeviceErrorStatus`` naming the module; the async engine's failure
+    latch then fails every open stream with it.  The status word is faked on the CPU runner: the
+    GPU test ``tests/test_engine_errors_gpu.py`` drives the same path from a real kernel."""
+    from inference_systems_b200.engine.model_runner import DeviceErrorStatus
+
+    d, cfg = ckpt
+    prompts = _prompts(2, 10, cfg["vocab_size"], seed=4)
+
+    def poison(runner):
+        runner.error_addrs = "fake"   # any non-None value: the runner appends and checks a status word
+        runner.with_status = lambda toks: torch.cat((toks.to(torch.int32), torch.tensor([1 << 2], dtype=torch.int32)))
+        runner._read_error_words = lambda: 0x2 << 16
+
+    llm = LLM(d, **KW)
+    poison(llm.model_runner)
+    llm.add_request(prompts[0], SamplingParams(temperature=0.0, max_tokens=4))
+    with pytest.raises(DeviceErrorStatus, match="tp-communication=0x2"):
+        llm.step()
+    assert llm.model_runner.get_metrics()["device_errors"] == 1
+    llm.exit()
+
+    async def main():
+        eng = AsyncLLMEngine(d, **KW)
+        poison(eng.engine.model_runner)
+        streams = [await eng.submit(p, SamplingParams(temperature=0.0, max_tokens=4)) for p in prompts]
+        for s in streams:
+            with pytest.raises(RuntimeError) as info:
+                async for _ in s:
+                    pass
+            assert isinstance(info.value.__cause__, DeviceErrorStatus)
+        with pytest.raises(RuntimeError):
+            await eng.close()
+
+    asyncio.run(main())
+
+
 def test_server_completions_stream_and_metrics(ckpt):
     from fastapi.testclient import TestClient
 

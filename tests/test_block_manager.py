@@ -31,9 +31,9 @@ def test_allocate_and_free_roundtrip():
     s = seq(range(600))
     assert bm.can_allocate(s) == 0
     bm.allocate(s, 0)
-    assert len(s.block_table) == 3 and len(bm.free_block_ids) == 5
+    assert len(s.block_table) == 3 and bm.num_free_blocks == 5
     bm.deallocate(s)
-    assert len(bm.free_block_ids) == 8 and not s.block_table
+    assert bm.num_free_blocks == 8 and not s.block_table
 
 
 def test_full_block_prefix_hit_reuses_pages():
@@ -47,7 +47,7 @@ def test_full_block_prefix_hit_reuses_pages():
     bm.allocate(b, cached)
     assert b.block_table[:2] == a.block_table[:2]
     assert b.num_cached_tokens == 512
-    assert bm.blocks[a.block_table[0]].ref_count == 2
+    assert bm.ref_count(a.block_table[0]) == 2
 
 
 def test_freed_cached_pages_stay_reusable_until_reassigned():

@@ -38,24 +38,3 @@ def test_tensor_parallel_engine_matches_oracle(tmp_path, name, tp):
     llm.exit()
     for o, p in zip(out, prompts):
         assert o["token_ids"] == reference_greedy(sd, cfg, p, 5)
-
-
-def test_token_sharded_prefill_matches_oracle(tmp_path, monkeypatch):
-    """Prefill chunks above the fused-row limit run token-sharded (reduce-scatter + RMSNorm on
-    each rank's rows, all-gather in front of every column-parallel projection) and must give
-    the oracle's tokens."""
-    monkeypatch.setenv("ISB_TP_SP", "1")
-    monkeypatch.setenv("ISB_TP_MAX_ROWS", "16")
-    cfg = preset("tiny", linear_num_value_heads=4)
-    sd = random_state_dict(cfg, seed=3, std=0.25)
-    d = str(tmp_path)
-    write_config(d, cfg)
-    save_file({k: v.contiguous() for k, v in sd.items()}, os.path.join(d, "model.safetensors"))
-    g = torch.Generator().manual_seed(9)
-    prompts = [torch.randint(0, cfg["vocab_size"], (n,), generator=g).tolist() for n in (37, 21)]
-    llm = LLM(d, device="cpu", tensor_parallel_size=2, max_num_seqs=2, max_num_state_slots=2, max_model_len=128,
-              dist_port=_free_port(), max_num_batched_tokens=64)
-    out = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=4, ignore_eos=True), use_tqdm=False)
-    llm.exit()
-    for o, p in zip(out, prompts):
-        assert o["token_ids"] == reference_greedy(sd, cfg, p, 4)

@@ -62,13 +62,13 @@ def _worker(rank: int, world: int, port: int, scenario: str, out_dir: str) -> No
             res["used"] = sorted(pool.used_checkpoint_slots)
         elif scenario == "slot_ids_diverge":
             if rank == 1:
-                pool._take()  # rank 1's next capture gets a different slot id
+                pool.slots.take()  # rank 1's next capture gets a different slot id
             try:
                 res["slot"] = transactional_capture_prefix_checkpoint(pool, slot)
             except RuntimeError as e:
                 res["raised"] = str(e)
             res["used"] = sorted(pool.used_checkpoint_slots)
-            res["free"] = len(pool.free_checkpoint_slots)
+            res["free"] = pool.free_checkpoint_slots
             res["capacity"] = pool.capacity
         elif scenario == "restore_fails_on_rank0":
             ck = transactional_capture_prefix_checkpoint(pool, slot)
@@ -134,7 +134,7 @@ def test_diverging_slot_ids_roll_back(tmp_path):
     out = _run("slot_ids_diverge", tmp_path)
     assert "diverged" in out[0]["raised"]
     assert out[1].get("slot") == -1
-    assert out[0]["used"] == [] and out[1]["used"] == []
+    assert out[0]["used"] == [] and out[1]["used"] == [0]  # rank 1 keeps only the slot taken outside
     assert out[0]["free"] == out[0]["capacity"]
     assert out[1]["free"] == out[1]["capacity"] - 1  # only the slot taken before the transaction is gone
 
