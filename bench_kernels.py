@@ -358,7 +358,56 @@ def tp_bench(batches=(1, 8, 128)) -> None:
     assert err == 0, f"device error word {err:#x}"
 
 
+def tp_emulated_bench() -> None:
+    """The tensor-parallel exchange kernels on ONE GPU with W ranks laid out as local buffers.
+
+    Times, per launch inside a CUDA graph: the row-parallel GEMM with the reduce-scatter epilogue
+    (``tp_gemm_rs``) next to the same GEMM accumulating locally (``gemm_accum``), and the owner
+    kernel (``tp_norm_allgather``, final wait off: nothing on one GPU waits for a later launch).
+    Isolates the kernels' own cost from cross-GPU latency."""
+    from inference_systems_b200.parallel.comm import shard_rows
+
+    c = ops.cuda_ops()
+    dev, bf = "cuda", torch.bfloat16
+    rows = []
+    for world, b, hh, inter in ((2, 1, 1024, 3584), (2, 128, 1024, 3584), (8, 128, 1024, 3584),
+                                (2, 64, 5120, 17408), (2, 2048, 1024, 3584)):
+        k = inter // world
+        s = shard_rows(b, world)
+        one = b * hh <= 256 * 1024
+        srows = b if one else s
+        slots = [torch.zeros(world, srows, hh, dtype=bf, device=dev) for _ in range(world)]
+        xs = [torch.zeros(b, hh, dtype=bf, device=dev) for _ in range(world)]
+        ctl = [torch.zeros(8, dtype=torch.int32, device=dev) for _ in range(world)]
+        staging = torch.zeros(b, hh, device=dev)
+        tab = lambda ts, off=0: torch.tensor([t.data_ptr() + off for t in ts], dtype=torch.int64, device=dev)  # noqa: E731
+        slot_ptrs, rs_ptrs, ag_ptrs, x_ptrs = tab(slots), tab(ctl), tab(ctl, 4), tab(xs)
+        x = torch.randn(b, k, device=dev).to(bf)
+        w = (torch.randn(hh, k, device=dev) * 0.02).to(bf)
+        res = torch.randn(b, hh, device=dev).to(bf)
+        nw = torch.zeros(hh, device=dev).to(bf)
+        acc = torch.zeros(b, hh, device=dev)
+        ctas = c.tp_gemm_rs(x, w, slot_ptrs, srows, staging, rs_ptrs, 0, s, 0, one)
+        t_rs = graph_time_us([lambda: c.tp_gemm_rs(x, w, slot_ptrs, srows, staging, rs_ptrs, 0, s, 0, one)] * 20)
+        t_acc = graph_time_us([lambda: c.gemm_accum(x, w, acc, 0)] * 20)
+        t_norm = graph_time_us([lambda: c.tp_norm_allgather(slots[0], res, nw, x_ptrs, ag_ptrs, ctl[0], b, s, 0, 0,
+                                                            1e-6, True, False, one)] * 20)
+        t_accnorm = graph_time_us([lambda: ops.add_rmsnorm_acc(acc, res, nw, 1e-6, True)] * 20)
+        torch.cuda.synchronize()
+        row = {"path": "exchange kernels on one GPU (emulated ranks)", "one_shot": one, "tp": world, "tokens": b,
+               "hidden": hh,
+               "inter_per_rank": k, "gemm_ctas": ctas, "gemm_rs_us": round(t_rs, 2), "gemm_accum_us": round(t_acc, 2),
+               "owner_norm_allgather_us": round(t_norm, 2), "local_add_norm_us": round(t_accnorm, 2)}
+        rows.append(row)
+        print(json.dumps(row), flush=True)
+    assert torch.ops.isb.error_word() == 0
+
+
 def main():
+    if "--tp-emulated" in sys.argv:
+        load_extension()
+        tp_emulated_bench()
+        return
     if "--tp" in sys.argv:
         load_extension()
         tp_bench()

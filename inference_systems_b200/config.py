@@ -118,7 +118,7 @@ class Config:
     speculative_parallel_verify: bool = True
     enable_mtp_phase_profiling: bool = False
     enable_mtp_replay_ssm: bool = False
-    gdn_decode_backend: str = "torch"
+    gdn_decode_backend: str = "auto"
     enable_hybrid_prefix_cache: bool = False
     hybrid_prefix_checkpoint_interval_blocks: int = 8
     hybrid_prefix_checkpoint_interval_tokens: int | None = None
@@ -183,6 +183,17 @@ class Config:
         assert 0 <= self.num_speculative_tokens <= 8
         if self.gdn_decode_backend not in ("torch", "cuda", "auto"):
             raise ValueError("gdn_decode_backend must be torch, cuda, or auto")
+        # GDN runs on this engine's sm_100a kernels on GPUs and on the PyTorch recurrence on CPUs;
+        # there is no second implementation to switch to on either device.
+        on_cuda = (self.device or ("cuda" if torch.cuda.is_available() else "cpu")) == "cuda"
+        if on_cuda and self.gdn_decode_backend == "torch":
+            raise ValueError("gdn_decode_backend='torch' is not available on GPUs: GDN runs on the sm_100a "
+                             "kernels (use 'auto' or 'cuda')")
+        if not on_cuda and self.gdn_decode_backend == "cuda":
+            raise ValueError("gdn_decode_backend='cuda' needs a CUDA device (use 'auto' or 'torch' on CPU)")
+        if not self.speculative_parallel_verify:
+            raise ValueError("sequential speculative verification is not provided: the one-pass verify "
+                             "(speculative_parallel_verify=True) is lossless and does strictly less work")
         assert self.hybrid_prefix_checkpoint_interval_blocks > 0
         if self.hybrid_prefix_checkpoint_interval_tokens is not None:
             if self.hybrid_prefix_checkpoint_interval_tokens <= 0:

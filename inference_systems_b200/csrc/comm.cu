@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
     const __nv_bfloat16* __restrict__ slots, int slot_rows, __nv_bfloat16* __restrict__ residual,
     const __nv_bfloat16* __restrict__ w, const unsigned long long* __restrict__ xdst,
     const unsigned long long* __restrict__ ag_flags, unsigned int* ctl, int lo, int rows, int H, float eps,
-    bool zc, int world, bool wait_gather, unsigned int rs_incr, unsigned int ag_incr) {
+    bool zc, int world, bool wait_gather, unsigned int rs_incr, unsigned int ag_incr, int one_shot_rank) {
   pdl_trigger();
   pdl_wait();
   __shared__ int s_ok;
@@ -184,6 +184,10 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
       __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll
       for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+      if (one_shot_rank >= 0) {  // one-shot: every rank normalises every row itself
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xdst[one_shot_rank]) + r * H + c) = out;
+        continue;
+      }
       // the all-gather: the row goes to every rank's activation buffer (staggered start)
       for (int q = 0; q < world; ++q) {
         const int dst = (i + q) % world;
@@ -196,15 +200,17 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
   // waits until every owner's rows have arrived, so the grid completes with the full activation.
   __syncthreads();
   if (tid == 0) {
-    for (int q = 0; q < world; ++q) {
-      unsigned int* f = reinterpret_cast<unsigned int*>(ag_flags[q]);
-      asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
+    if (one_shot_rank < 0) {
+      for (int q = 0; q < world; ++q) {
+        unsigned int* f = reinterpret_cast<unsigned int*>(ag_flags[q]);
+        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
+      }
     }
     unsigned int prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctl + 4) : "memory");
     if (prev == gridDim.x - 1) {
       ctl[4] = 0u;
-      if (wait_gather) wait_geq(ctl + 1, ag_target, 4u);
+      if (wait_gather && one_shot_rank < 0) wait_geq(ctl + 1, ag_target, 4u);
       ctl[2] = rs_target;
       ctl[3] = ag_target;
     }
@@ -310,24 +316,26 @@ static int norm_ctas(int64_t rows) { return int(std::max<int64_t>(std::min<int64
 
 void tp_norm_allgather(const at::Tensor& slots, at::Tensor residual, const at::Tensor& w, const at::Tensor& xdst,
                        const at::Tensor& ag_flags, at::Tensor ctl, int64_t T, int64_t own_rows, int64_t rank,
-                       int64_t rs_incr, double eps, bool zc, bool wait_gather) {
+                       int64_t rs_incr, double eps, bool zc, bool wait_gather, bool one_shot) {
   TORCH_CHECK(residual.is_contiguous() && residual.scalar_type() == at::kBFloat16 && residual.dim() == 2 &&
                   residual.size(0) >= T, "residual must be contiguous bf16 [>= T, H]");
   const int H = residual.size(1);
   const int W = xdst.numel();
   TORCH_CHECK(xdst.scalar_type() == at::kLong && ag_flags.scalar_type() == at::kLong && ag_flags.numel() == W &&
                   W >= 1 && W <= kMaxWorld, "one activation buffer and counter per rank (<= 8)");
-  TORCH_CHECK(own_rows >= 1 && own_rows * W >= T && rank >= 0 && rank < W, "every token row needs an owner");
+  TORCH_CHECK(rank >= 0 && rank < W && (one_shot || (own_rows >= 1 && own_rows * W >= T)),
+              "every token row needs an owner");
   TORCH_CHECK(slots.scalar_type() == at::kBFloat16 && slots.is_contiguous() && slots.dim() == 3 &&
-                  slots.size(0) == W && slots.size(2) == H && slots.size(1) >= own_rows,
-              "slots: contiguous bf16 [W, >= own_rows, H]");
+                  slots.size(0) == W && slots.size(2) == H && slots.size(1) >= (one_shot ? T : own_rows),
+              "slots: contiguous bf16 [W, >= rows, H]");
   TORCH_CHECK(H % 8 == 0 && H <= 16384, "hidden size must be a multiple of 8 and at most 16384");
   TORCH_CHECK(ctl.scalar_type() == at::kInt && ctl.numel() >= 5 && ctl.is_contiguous(), "int32 control words");
   auto owned = [&](int64_t r) { return std::max<int64_t>(0, std::min<int64_t>(own_rows, T - r * own_rows)); };
-  int64_t ag_incr = 0;  // every CTA of every rank's owner kernel signals every rank once
-  for (int64_t r = 0; r < W; ++r) ag_incr += norm_ctas(owned(r));
-  const int64_t rows = owned(rank);
-  const int64_t lo = std::min<int64_t>(rank * own_rows, T);
+  int64_t ag_incr = 0;  // every CTA of every rank's owner kernel signals every rank once (two-shot)
+  if (!one_shot)
+    for (int64_t r = 0; r < W; ++r) ag_incr += norm_ctas(owned(r));
+  const int64_t rows = one_shot ? T : owned(rank);
+  const int64_t lo = one_shot ? 0 : std::min<int64_t>(rank * own_rows, T);
   const int threads = std::min(512, ((H / 8 + 31) / 32) * 32);
   launch_pdl(tp_norm_ag_kernel, dim3(norm_ctas(rows)), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<const __nv_bfloat16*>(slots.data_ptr()), int(slots.size(1)),
@@ -335,7 +343,8 @@ void tp_norm_allgather(const at::Tensor& slots, at::Tensor residual, const at::T
              reinterpret_cast<const unsigned long long*>(xdst.data_ptr<int64_t>()),
              reinterpret_cast<const unsigned long long*>(ag_flags.data_ptr<int64_t>()),
              reinterpret_cast<unsigned int*>(ctl.data_ptr<int>()), int(lo), int(rows), H, float(eps), zc, W,
-             wait_gather, static_cast<unsigned int>(rs_incr), static_cast<unsigned int>(ag_incr));
+             wait_gather, static_cast<unsigned int>(rs_incr), static_cast<unsigned int>(ag_incr),
+             one_shot ? int(rank) : -1);
 }
 
 at::Tensor xrank_argmax(const at::Tensor& val, const at::Tensor& idx, const at::Tensor& xbufs,

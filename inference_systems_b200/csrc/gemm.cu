@@ -76,6 +76,7 @@ struct GemmArgs {
   int ndst;
   int own_rows;                    // token rows owned by each rank
   int slot_rows;                   // rows of one source slot (>= own_rows)
+  bool bcast;                      // one-shot: every row goes to every rank (slot row = token)
   const unsigned long long* peer_flags;  // [ndst] address of each rank's arrival counter
   int rank;
   // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
@@ -117,15 +118,24 @@ ISB_DEVICE void acc_add1(const GemmArgs& args, size_t off, float a) {
   atomicAdd(args.acc + off, a);
 }
 
-// kRsPush: store 4 features of token ``tok`` (bf16) into the owner rank's slot for this rank.
+// kRsPush: store 4 features of token ``tok`` (bf16) into the owner rank's slot for this rank, or
+// (one-shot) into every rank's slot for this rank.
 ISB_DEVICE void rs_push4(const GemmArgs& args, int tok, int f, float a, float b, float c, float d) {
-  const int owner = tok / args.own_rows;
-  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dsts[owner]) +
-                       (size_t(args.rank) * args.slot_rows + (tok - owner * args.own_rows)) * args.ldo + f;
   uint2 raw;
   __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
   h[0] = __floats2bfloat162_rn(a, b);
   h[1] = __floats2bfloat162_rn(c, d);
+  if (args.bcast) {
+    const size_t off = (size_t(args.rank) * args.slot_rows + tok) * args.ldo + f;
+    for (int q = 0; q < args.ndst; ++q) {
+      const int r = (args.rank + q) % args.ndst;  // own copy first, then the peers in turn
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(args.dsts[r]) + off) = raw;
+    }
+    return;
+  }
+  const int owner = tok / args.own_rows;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(args.dsts[owner]) +
+                       (size_t(args.rank) * args.slot_rows + (tok - owner * args.own_rows)) * args.ldo + f;
   *reinterpret_cast<uint2*>(dst) = raw;
 }
 
@@ -1184,7 +1194,8 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }
 
-// Tensor-parallel row-parallel GEMM fused with the reduce-scatter.  ``a`` [T, K/W] . ``b`` [H, K/W]^T
+// Tensor-parallel row-parallel GEMM fused with the reduce-scatter (or, ``one_shot``, with the
+// all-to-all push of a one-shot all-reduce: every row to every rank).  ``a`` [T, K/W] . ``b`` [H, K/W]^T
 // is this rank's partial product.  Token rows [r*own_rows, (r+1)*own_rows) belong to rank r: each
 // complete bf16 row goes straight into rank r's slot for this rank (``slots``: int64 [W] device
 // table of the ranks' slot arrays [W][slot_rows][H] bf16, peer memory included), so a partial
@@ -1193,7 +1204,8 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
 // last CTA then bumps every rank's arrival counter (``flags``: int64 [W] device addresses), which
 // the owner's ``tp_norm_allgather`` waits for.
 int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
-                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits) {
+                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits,
+                   bool one_shot) {
   at::Tensor a = a_in.contiguous();
   check_operands(a, b);
   const int M = a.size(0), N = b.size(0);
@@ -1201,8 +1213,10 @@ int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
                   slots.is_cuda() && flags.is_cuda(), "slots / flags: int64 device tables, one entry per rank");
   TORCH_CHECK(staging.scalar_type() == at::kFloat && staging.is_contiguous() && staging.size(0) >= M &&
                   staging.size(1) == N, "staging accumulator must be contiguous fp32 [>= T, H]");
-  TORCH_CHECK(own_rows > 0 && own_rows <= slot_rows && int64_t(own_rows) * slots.numel() >= M && rank >= 0 &&
-                  rank < slots.numel(), "every token row needs an owner rank and a slot row");
+  TORCH_CHECK(rank >= 0 && rank < slots.numel(), "rank out of range");
+  TORCH_CHECK(one_shot ? M <= slot_rows
+                       : own_rows > 0 && own_rows <= slot_rows && int64_t(own_rows) * slots.numel() >= M,
+              "every token row needs an owner rank and a slot row");
   TORCH_CHECK(N % 4 == 0, "output features must be a multiple of 4");
   if (M == 0) return 0;
   const int kb_total = (int(a.size(1)) + BK - 1) / BK;
@@ -1223,8 +1237,9 @@ int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
   args.counters = p.splits > 1 ? counter_slot() : nullptr;
   args.dsts = reinterpret_cast<const unsigned long long*>(slots.data_ptr<int64_t>());
   args.ndst = int(slots.numel());
-  args.own_rows = int(own_rows);
+  args.own_rows = one_shot ? M : int(own_rows);
   args.slot_rows = int(slot_rows);
+  args.bcast = one_shot;
   args.peer_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
   args.rank = int(rank);
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }

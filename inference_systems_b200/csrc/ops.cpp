@@ -66,10 +66,11 @@ void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_
 int64_t attn_error_word();
 int64_t comm_error_word();
 int64_t tp_gemm_rs(const at::Tensor& a, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
-                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits);
+                   at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits,
+                   bool one_shot);
 void tp_norm_allgather(const at::Tensor& slots, at::Tensor residual, const at::Tensor& w, const at::Tensor& xdst,
                        const at::Tensor& ag_flags, at::Tensor ctl, int64_t T, int64_t own_rows, int64_t rank,
-                       int64_t rs_incr, double eps, bool zc, bool wait_gather);
+                       int64_t rs_incr, double eps, bool zc, bool wait_gather, bool one_shot);
 std::tuple<at::Tensor, at::Tensor> symm_alloc(int64_t nbytes);
 int64_t symm_open(const at::Tensor& handle);
 void symm_close(int64_t ptr);
@@ -150,10 +151,10 @@ TORCH_LIBRARY(isb, m) {
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
   m.def("tp_gemm_rs(Tensor a, Tensor b, Tensor slots, int slot_rows, Tensor(a!) staging, Tensor flags, "
-        "int rank, int own_rows, int splits=0) -> int");
+        "int rank, int own_rows, int splits=0, bool one_shot=False) -> int");
   m.def("tp_norm_allgather(Tensor slots, Tensor(b!) residual, Tensor w, Tensor xdst, Tensor ag_flags, "
         "Tensor(c!) ctl, int T, int own_rows, int rank, int rs_incr, float eps, bool zero_centered, "
-        "bool wait_gather) -> ()");
+        "bool wait_gather, bool one_shot=False) -> ()");
   m.def("comm_set_wait_timeout(int ns) -> ()");
   m.def("step_status(Tensor toks, Tensor words) -> Tensor");
   m.def("error_word_addresses() -> Tensor");

@@ -66,6 +66,10 @@ class TPComm:
         tokens = getattr(config, "max_num_batched_tokens", 8192) if config is not None else 8192
         self.max_tokens = int(os.environ.get("ISB_TP_MAX_TOKENS", max_tokens or max(tokens, seqs * (spec + 1), 256)))
         self.max_sample_rows = max_sample_rows or max(512, seqs * (spec + 1))
+        # Exchanges of up to this many activation elements (T x H) run one-shot: every rank pushes
+        # its whole bf16 partial to every rank and normalises every row itself -- one cross-GPU
+        # hop instead of two, at W/2 times the bytes; larger ones (prefill) run two-shot.
+        self.one_shot_elems = int(os.environ.get("ISB_TP_ONE_SHOT_ELEMS", 256 * 1024))
         self.xpar = 0
         self.fused = device.type == "cuda"
         self._peer_ptrs: list[int] = []
@@ -78,7 +82,7 @@ class TPComm:
         w, h, t = self.world, self.hidden, self.max_tokens
         off = 0
         layout = {}
-        self.slot_rows = shard_rows(t, w)
+        self.slot_rows = max(shard_rows(t, w), min(t, self.one_shot_elems // h))
         for name, nbytes in (("slots", w * self.slot_rows * h * 2), ("x0", t * h * 2), ("x1", t * h * 2),
                              ("ctl", 32), ("xbuf", w * self.max_sample_rows * 8), ("xflag", w * 4)):
             layout[name] = off
@@ -141,16 +145,18 @@ class TPComm:
                                    norm_w: torch.Tensor, eps: float, zero_centered: bool) -> torch.Tensor:
         """``residual += sum_ranks(x @ w^T)``; return RMSNorm(residual) (all rows, on every rank).
 
-        On GPUs only the rows this rank owns are updated in ``residual``."""
+        On GPUs a two-shot exchange (large ``T``) updates only the rows this rank owns in
+        ``residual``; a one-shot exchange updates all of them."""
         t = x.shape[0]
         if self.fused and t <= self.max_tokens:
             c = ops.cuda_ops()
             s = shard_rows(t, self.world)
-            ctas = c.tp_gemm_rs(x, w, self.slot_ptrs, self.slot_rows, self.staging, self.rs_ptrs, self.rank, s, 0)
+            one = t * self.hidden <= self.one_shot_elems and t <= self.slot_rows
+            ctas = c.tp_gemm_rs(x, w, self.slot_ptrs, self.slot_rows, self.staging, self.rs_ptrs, self.rank, s, 0, one)
             p = self.xpar
             self.xpar ^= 1
             c.tp_norm_allgather(self.slots_local, residual, norm_w, self.x_ptrs[p], self.ag_ptrs, self.ctl, t, s,
-                                self.rank, self.world * ctas, eps, zero_centered, True)
+                                self.rank, self.world * ctas, eps, zero_centered, True, one)
             return self.x_local[p][:t]
         y = ops.linear(x, w)
         dist.all_reduce(y, group=self.group)

@@ -33,9 +33,9 @@ def _addr_table(tensors, offset_bytes=0):
 class EmulatedRanks:
     """W ranks' symmetric buffers as local tensors (NaN where nothing may be read)."""
 
-    def __init__(self, w, t, h):
-        self.w, self.t, self.h = w, t, h
-        self.slot_rows = max((t + w - 1) // w, 1)
+    def __init__(self, w, t, h, one_shot=False):
+        self.w, self.t, self.h, self.one_shot = w, t, h, one_shot
+        self.slot_rows = t if one_shot else max((t + w - 1) // w, 1)
         self.slots = [torch.full((w, self.slot_rows, h), float("nan"), dtype=torch.bfloat16, device=DEV)
                       for _ in range(w)]
         self.staging = [torch.zeros(t, h, device=DEV) for _ in range(w)]
@@ -48,6 +48,8 @@ class EmulatedRanks:
 
     def owned(self, r, t):
         s = max((t + self.w - 1) // self.w, 1)
+        if self.one_shot:  # every rank normalises every row
+            return s, 0, t
         lo = min(r * s, t)
         return s, lo, min(s, t - lo)
 
@@ -56,23 +58,27 @@ def _exchange(ranks, xs, ws, res, nw, t, zc=True, splits=0):
     """One exchange on every emulated rank; returns (GEMM CTAs per rank, owner CTAs over all ranks)."""
     c = ops.cuda_ops()
     s = ranks.owned(0, t)[0]
-    ctas = [c.tp_gemm_rs(xs[r], ws[r], ranks.slot_ptrs, ranks.slot_rows, ranks.staging[r], ranks.rs_ptrs, r, s, splits)
-            for r in range(ranks.w)]
+    one = ranks.one_shot
+    ctas = [c.tp_gemm_rs(xs[r], ws[r], ranks.slot_ptrs, ranks.slot_rows, ranks.staging[r], ranks.rs_ptrs, r, s, splits,
+                         one) for r in range(ranks.w)]
     assert len(set(ctas)) == 1
     for r in range(ranks.w):
         c.tp_norm_allgather(ranks.slots[r], res[r], nw, ranks.x_ptrs, ranks.ag_ptrs, ranks.ctl[r], t, s, r,
-                            ranks.w * ctas[0], 1e-6, zc, False)
+                            ranks.w * ctas[0], 1e-6, zc, False, one)
     torch.cuda.synchronize()
-    owners = sum(max(min(ranks.owned(r, t)[2], 296), 1) for r in range(ranks.w))
+    owners = 0 if one else sum(max(min(ranks.owned(r, t)[2], 296), 1) for r in range(ranks.w))
     return ctas[0], owners
 
 
+@pytest.mark.parametrize("one_shot", [False, True])
 @pytest.mark.parametrize("w,t,h,k,splits", [(2, 128, 1024, 1792, 0), (2, 128, 1024, 1792, 1), (4, 128, 1024, 512, 0),
                                             (8, 128, 1024, 256, 0), (8, 5, 1024, 448, 0), (2, 300, 5120, 1024, 0),
                                             (2, 300, 1024, 2048, 4), (4, 1, 1024, 512, 0)])
-def test_reduce_scatter_norm_allgather(w, t, h, k, splits):
+def test_reduce_scatter_norm_allgather(w, t, h, k, splits, one_shot):
+    """Two-shot (reduce-scatter to the owner, owner normalises and pushes its rows to every rank)
+    and one-shot (every rank pushes its whole partial to every rank and normalises every row)."""
     g = torch.Generator(device=DEV).manual_seed(w * 100 + t)
-    ranks = EmulatedRanks(w, t, h)
+    ranks = EmulatedRanks(w, t, h, one_shot)
     xs = [torch.randn(t, k, device=DEV, generator=g).to(torch.bfloat16) for _ in range(w)]
     ws = [(torch.randn(h, k, device=DEV, generator=g) * 0.05).to(torch.bfloat16) for _ in range(w)]
     res0 = torch.randn(t, h, device=DEV, generator=g).to(torch.bfloat16)
@@ -90,7 +96,7 @@ def test_reduce_scatter_norm_allgather(w, t, h, k, splits):
             _, lo, rows = ranks.owned(r, t)
             assert _rel(res[r][lo:lo + rows], want_res[lo:lo + rows]) < 1e-2 if rows else True
             assert torch.count_nonzero(ranks.staging[r]) == 0      # split-K staging re-zeroed
-            rs, ag = w * ctas * (step + 1), owners * (step + 1)
+            rs, ag = w * ctas * (step + 1), owners * (step + 1)   # one-shot: no owner arrivals
             assert ranks.ctl[r].tolist() == [rs, ag, rs, ag, 0, 0, 0, 0]
         res0 = res[0].clone()
         for r in range(w):  # every rank's residual view, as the next layer would see its own rows
