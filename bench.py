@@ -171,8 +171,13 @@ def _serve_batch(llm, runner, cfg, b: int, args, clk) -> dict:
         llm.step()
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
+    first_tokens = sum(s.num_completion_tokens for s in llm.scheduler.running)
+    gen0 = torch.cuda.Event(enable_timing=True)
+    gen0.record()
+    gen_steps = 0
     for _ in range(args.warmup):
         llm.step()
+        gen_steps += 1
     torch.cuda.synchronize()
     h2d0, d2h0 = runner.h2d_bytes, runner.d2h_bytes
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -189,8 +194,15 @@ def _serve_batch(llm, runner, cfg, b: int, args, clk) -> dict:
     e2e_ms = ev0.elapsed_time(ev1)
     h2d = (runner.h2d_bytes - h2d0) / args.steps
     d2h = (runner.d2h_bytes - d2h0) / args.steps
+    gen_steps += args.steps
     while not llm.is_finished():  # finish the requests: TTFT / TPOT of complete requests
         llm.step()
+        gen_steps += 1
+    gen1 = torch.cuda.Event(enable_timing=True)
+    gen1.record()
+    torch.cuda.synchronize()
+    gen_ms = gen0.elapsed_time(gen1)
+    gen_tokens = b * out_len - first_tokens
     # device-timed: K decode-graph replays of this batch bucket, max over ranks
     dev_ms = runner.call("bench_replay", b, args.warmup, args.steps)
     clk_on.__exit__(None, None, None)
@@ -207,6 +219,11 @@ def _serve_batch(llm, runner, cfg, b: int, args, clk) -> dict:
         "tpot_p50_ms": _p50(m.get("tpot_ms") for m in req),
         "prefill_s": round(prefill_s, 3),
         "output_len": out_len,
+        # the whole decode phase (context 513 .. 512 + output_len) through LLMEngine.step, not just
+        # the timed window at its start
+        "full_generation": {"decode_tokens": gen_tokens, "steps": gen_steps,
+                            "e2e_tok_s": round(gen_tokens / (gen_ms / 1e3), 1),
+                            "mean_step_ms": round(gen_ms / max(gen_steps, 1), 4)},
     }
 
 
@@ -294,6 +311,7 @@ def run_isb(args, rank: int, world: int) -> dict | None:
         "ttft_p50_ms": head["ttft_p50_ms"],
         "tpot_p50_ms": head["tpot_p50_ms"],
         "prefill_s": head["prefill_s"],
+        "full_generation": head["full_generation"],
         "impl": "isb",
     }
     if len(batches) > 1:

@@ -117,7 +117,7 @@ class Config:
     num_speculative_tokens: int = 0
     speculative_parallel_verify: bool = True
     enable_mtp_phase_profiling: bool = False
-    enable_mtp_replay_ssm: bool = False
+    enable_mtp_replay_ssm: bool | None = None  # None: replay records whenever MTP is on
     gdn_decode_backend: str = "auto"
     enable_hybrid_prefix_cache: bool = False
     hybrid_prefix_checkpoint_interval_blocks: int = 8
@@ -227,7 +227,7 @@ class Config:
                 raise ValueError("native MTP currently requires Qwen3.5 hybrid state")
             if caps.mtp_num_hidden_layers != 1:
                 raise ValueError("native MTP requires exactly one checkpoint MTP layer")
-        if self.enable_mtp_replay_ssm:
+        if self.enable_mtp_replay_ssm is True:
             if not self.num_speculative_tokens:
                 raise ValueError("MTP ReplaySSM requires speculative decoding")
             if not self.speculative_parallel_verify:

@@ -315,7 +315,12 @@ __global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int
   const int tid = threadIdx.x, kr = tid >> 5, vc = (tid & 31) * 4;
   const int n = min(max(lens[b], 0), steps);
   if (n == 0) return;
-  float* S = rec + (((size_t(l) * pool_slots + slots[b]) * Hv + h) * D) * D;
+  const int slot = slots[b];
+  if (slot < 0 || slot >= pool_slots) {  // never write outside the pool: flag the batch as invalid
+    if (tid == 0) atomicOr(&g_gdn_err, 4u);
+    return;
+  }
+  float* S = rec + (((size_t(l) * pool_slots + slot) * Hv + h) * D) * D;
   float4 st[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) st[i] = *reinterpret_cast<const float4*>(S + (kr * 16 + i) * D + vc);
@@ -339,9 +344,14 @@ __global__ void __launch_bounds__(kThreads) replay_commit_kernel(float* rec, int
 __global__ void conv_commit_kernel(__nv_bfloat16* conv, int pool_slots, const __nv_bfloat16* hist, int hist_rows,
                                    const int* slots, const int* bounds, int steps, int elems) {
   const int b = blockIdx.x, l = blockIdx.y;
-  const int row = b * steps + bounds[b];
+  const int slot = slots[b], bound = bounds[b];
+  if (slot < 0 || slot >= pool_slots || bound < 0 || bound >= steps) {  // out of range: flag, write nothing
+    if (threadIdx.x == 0) atomicOr(&g_gdn_err, 8u);
+    return;
+  }
+  const int row = b * steps + bound;
   const __nv_bfloat16* src = hist + (size_t(l) * hist_rows + row) * elems;
-  __nv_bfloat16* dst = conv + (size_t(l) * pool_slots + slots[b]) * elems;
+  __nv_bfloat16* dst = conv + (size_t(l) * pool_slots + slot) * elems;
   for (int i = threadIdx.x; i < elems; i += blockDim.x) dst[i] = src[i];
 }
 

@@ -97,15 +97,24 @@ class MTPDriver:
         self.drafts = torch.zeros(n_slots, self.k, dtype=torch.int32, device=dev)
         self.max_rows = cfg.max_num_seqs * (self.k + 1)
         geo = runner.model.gdn_geometry()
+        # verify records: compact replay terms folded at commit (default), or full state snapshots
+        # after every verify row copied at commit (``enable_mtp_replay_ssm=False``)
+        self.replay = getattr(cfg, "enable_mtp_replay_ssm", None) is not False
+        self.rec_k = self.hist_rec = None
         if geo is not None:
             L, hv, dk, dv = geo["num_layers"], geo["hv"], geo["dk"], geo["dv"]
             rows = self.max_rows
-            self.rec_k = torch.zeros(L, rows, hv, dk, dtype=torch.float32, device=dev)
-            self.rec_delta = torch.zeros(L, rows, hv, dv, dtype=torch.float32, device=dev)
-            self.rec_g = torch.zeros(L, rows, hv, dtype=torch.float32, device=dev)
+            if self.replay:
+                self.rec_k = torch.zeros(L, rows, hv, dk, dtype=torch.float32, device=dev)
+                self.rec_delta = torch.zeros(L, rows, hv, dv, dtype=torch.float32, device=dev)
+                self.rec_g = torch.zeros(L, rows, hv, dtype=torch.float32, device=dev)
+            else:
+                need = L * rows * hv * dk * dv * 4
+                if dev.type == "cuda" and need > torch.cuda.mem_get_info(dev)[0] // 4:
+                    raise ValueError(f"MTP state snapshots need {need / 2**30:.1f} GiB for {rows} verify rows; "
+                                     "use enable_mtp_replay_ssm=True or fewer max_num_seqs")
+                self.hist_rec = torch.zeros(L, rows, hv, dk, dv, dtype=torch.float32, device=dev)
             self.conv_hist = torch.zeros(L, rows, geo["conv_dim"], geo["kernel"] - 1, dtype=runner.dtype, device=dev)
-        else:
-            self.rec_k = None
         n_attn = len(runner.model.attn_layer_ids)
         self.kv_index = n_attn  # the MTP layer is the last layer of the KV cache
         self.before_round = None  # test hook: callable(seqs, driver) run before each verify pass
@@ -141,6 +150,7 @@ class MTPDriver:
             "accepted_length_histogram": list(self.accept_hist),
             "prefill_catchups": self.prefill_catchups,
             "synthetic_acceptance": self.synthetic,
+            "verify_records": "replay" if self.replay else "snapshot",
             "cudagraph_buckets": sorted(self.graphs),
             "cudagraph_replays": self.graph_replays,
         }
@@ -149,10 +159,12 @@ class MTPDriver:
         self.drafts[state_slot] = torch.as_tensor(tokens, dtype=torch.int32, device=self.drafts.device)
 
     def _gdn_records(self, t: int):
-        if self.rec_k is None:
-            return None
-        return [(self.rec_k[j, :t], self.rec_delta[j, :t], self.rec_g[j, :t], self.conv_hist[j, :t])
-                for j in range(self.rec_k.shape[0])]
+        if self.rec_k is not None:
+            return [(self.rec_k[j, :t], self.rec_delta[j, :t], self.rec_g[j, :t], self.conv_hist[j, :t])
+                    for j in range(self.rec_k.shape[0])]
+        if self.hist_rec is not None:
+            return [(self.hist_rec[j, :t], self.conv_hist[j, :t]) for j in range(self.hist_rec.shape[0])]
+        return None
 
     def _sample(self, hidden: torch.Tensor, rng: torch.Tensor) -> torch.Tensor:
         temps = torch.zeros(hidden.shape[0], dtype=torch.float32, device=hidden.device)
@@ -291,6 +303,11 @@ class MTPDriver:
         sm_mgr = r.state_manager
         if sm_mgr is not None and self.rec_k is not None:
             ops.gdn_replay_commit(sm_mgr.recurrent_states, st_d, self.rec_k, self.rec_delta, self.rec_g, acc + 1, k + 1)
+            ops.gdn_conv_commit(sm_mgr.conv_states, self.conv_hist, st_d, acc, k + 1)
+        elif sm_mgr is not None and self.hist_rec is not None:
+            # the snapshot after the last accepted row becomes the slot's state, in every GDN layer
+            accepted_row = (torch.arange(b, device=dev) * (k + 1) + acc).long()
+            sm_mgr.recurrent_states[:, st_d.long()] = self.hist_rec[:, accepted_row]
             ops.gdn_conv_commit(sm_mgr.conv_states, self.conv_hist, st_d, acc, k + 1)
 
         # ---- MTP catch-up over the verified rows, then the next drafts

@@ -46,6 +46,13 @@ class CommandChannel:
                     if time.monotonic() > deadline:
                         raise
                     time.sleep(0.01)
+            # Attaching registers the segment with this process's resource tracker, which would
+            # unlink (or report as leaked) a segment that rank 0 owns and unlinks itself.
+            try:
+                from multiprocessing import resource_tracker
+                resource_tracker.unregister(self.shm._name, "shared_memory")
+            except Exception:  # noqa: BLE001 - tracker internals differ across Python versions
+                pass
         self.owner = create
         self.seq = 0
 

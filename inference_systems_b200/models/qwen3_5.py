@@ -220,8 +220,10 @@ class GDNMixer(nn.Module):
                                         conv_pool, *history, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv,
                                         eps=self.eps)
         if records is not None:
-            return ops.gdn_verify(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool,
-                                  conv_pool, *records, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
+            # (k, delta, log decay, conv window) replay records, or (state, conv window) snapshots
+            verify = ops.gdn_verify if len(records) == 4 else ops.gdn_verify_snapshots
+            return verify(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool, conv_pool,
+                          *records, hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
         return ops.gdn(proj, batch, self.conv_w, self.A_log, self.dt_bias, self.norm_w, rec_pool, conv_pool,
                        hk=self.hk, hv=self.hv, dk=self.dk, dv=self.dv, eps=self.eps)
 

@@ -217,6 +217,33 @@ def gdn_verify(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, 
     return out
 
 
+def gdn_verify_snapshots(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool,
+                         conv_pool, hist_rec: torch.Tensor, conv_hist: torch.Tensor, *, hk: int, hv: int, dk: int,
+                         dv: int, eps: float) -> torch.Tensor:
+    """GDN mixer over speculative rows without touching the slot pools, keeping the full state after
+    every row (``hist_rec[t]``, ``conv_hist[t]``): the accepted row's state is then copied into the
+    pool.  The snapshot alternative to replay records (more memory, no fold at commit); parity: the
+    reference's minimal-snapshot verify (``nanovllm/engine/model_runner.py:1570-1652``)."""
+    if proj.is_cuda:
+        rows = torch.arange(proj.shape[0], device=proj.device, dtype=torch.int32)
+        return cuda_ops().gdn_scan_history(proj, batch.cu_seqlens_q, batch.state_slots, conv_w, a_log, dt_bias,
+                                           norm_w, rec_pool, conv_pool, hk, hv, eps, False, rows, hist_rec, conv_hist,
+                                           None, None, None)
+    out = torch.empty(proj.shape[0], hv * dv, dtype=proj.dtype, device=proj.device)
+    cu = batch.cu_seqlens_host
+    for i, slot in enumerate(batch.slots_host):
+        s, e = cu[i], cu[i + 1]
+        if e == s:
+            continue
+        y, _, _, rh, ch, _ = ref.gdn_sequence(proj[s:e], conv_w, a_log, dt_bias, norm_w, rec_pool[slot],
+                                              conv_pool[slot], hk=hk, hv=hv, dk=dk, dv=dv, eps=eps,
+                                              history_at=list(range(e - s)))
+        out[s:e] = y
+        hist_rec[s:e] = torch.stack(rh)
+        conv_hist[s:e] = torch.stack(ch)
+    return out
+
+
 def gdn_with_history(proj: torch.Tensor, batch: ForwardBatch, conv_w, a_log, dt_bias, norm_w, rec_pool, conv_pool,
                      rows: torch.Tensor, hist_rec: torch.Tensor, hist_conv: torch.Tensor, *, hk: int, hv: int, dk: int,
                      dv: int, eps: float) -> torch.Tensor:

@@ -53,8 +53,10 @@ def test_mtp_with_model_drafts_is_lossless(tmp_path):
     assert mtp["rounds"] > 0 and mtp["prefill_catchups"] > 0
 
 
-@pytest.mark.parametrize("k", [1, 3])
-def test_mtp_oracle_drafts_cover_every_accept_length(tmp_path, k):
+@pytest.mark.parametrize("k,replay", [(1, None), (3, None), (3, False)])
+def test_mtp_oracle_drafts_cover_every_accept_length(tmp_path, k, replay):
+    """Every accepted length 0..K occurs; with ``enable_mtp_replay_ssm=False`` the commit copies the
+    state snapshot of the accepted row instead of folding replay records, with the same tokens."""
     d, cfg = _ckpt(tmp_path)
     prompts = _prompts(3, 17, cfg["vocab_size"], seed=2)
     n = 14
@@ -73,10 +75,12 @@ def test_mtp_oracle_drafts_cover_every_accept_length(tmp_path, k):
             driver.set_drafts(s.state_slot, drafts)
         rounds[0] += 1
 
-    got, m = _generate(d, prompts, n, hook=hook, num_speculative_tokens=k, max_num_batched_tokens=64)
+    got, m = _generate(d, prompts, n, hook=hook, num_speculative_tokens=k, max_num_batched_tokens=64,
+                       enable_mtp_replay_ssm=replay)
     assert got == [w[:n] for w in want]
     hist = m["model_runner"]["mtp"]["accepted_length_histogram"]
     assert all(c > 0 for c in hist), hist
+    assert m["model_runner"]["mtp"]["verify_records"] == ("snapshot" if replay is False else "replay")
 
 
 def test_mtp_synthetic_full_acceptance_emits_k_plus_one(tmp_path):

@@ -55,8 +55,8 @@ def _prefix(a, b):
     return n
 
 
-@pytest.mark.parametrize("k,eager", [(1, True), (3, True), (2, False)])
-def test_mtp_oracle_drafts_match_target_only(ckpt, k, eager):
+@pytest.mark.parametrize("k,eager,replay", [(1, True, None), (3, True, None), (2, False, None), (2, False, False)])
+def test_mtp_oracle_drafts_match_target_only(ckpt, k, eager, replay):
     d, cfg = ckpt
     prompts = _prompts(3, 40, cfg["vocab_size"], seed=5)
     n = 12
@@ -75,7 +75,7 @@ def test_mtp_oracle_drafts_match_target_only(ckpt, k, eager):
             driver.set_drafts(s.state_slot, drafts)
         rounds[0] += 1
 
-    got, m = _generate(d, prompts, n, hook=hook, eager=eager, num_speculative_tokens=k)
+    got, m = _generate(d, prompts, n, hook=hook, eager=eager, num_speculative_tokens=k, enable_mtp_replay_ssm=replay)
     prefixes = [_prefix(g, w) for g, w in zip(got, want)]
     assert sum(p == n for p in prefixes) >= 2 and min(prefixes) >= 4, (got, want)
     mtp = m["model_runner"]["mtp"]
