@@ -79,31 +79,6 @@ ISB_DEVICE bool wait_geq(const unsigned int* cnt, unsigned int target, unsigned 
   return true;
 }
 
-struct Vec8 {
-  float v[8];
-};
-
-__device__ __forceinline__ Vec8 load8(const __nv_bfloat16* p) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  Vec8 r;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    r.v[2 * i] = f.x;
-    r.v[2 * i + 1] = f.y;
-  }
-  return r;
-}
-
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
-  uint4 raw;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = raw;
-}
-
 constexpr int kMaxWorld = 8;
 constexpr int kMaxChunks = 4;  // columns per thread / 8: H <= 4 * 8 * 512
 
@@ -175,11 +150,8 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
       const int c = (tid + k * nt) * 8;
       if (c >= H) break;
       store8(res + c, v[k]);
-      const Vec8 wv = load8(w + c);
       float y[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e)
-        y[e] = zc ? v[k][e] * rs * (1.f + wv.v[e]) : __bfloat162float(__float2bfloat16(v[k][e] * rs)) * wv.v[e];
+      norm8(y, v[k], w + c, rs, zc);
       uint4 out;
       __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&out);
 #pragma unroll

@@ -248,4 +248,45 @@ ISB_DEVICE float warp_max(float v) {
   return v;
 }
 
+// ------------------------------------------------------- bf16 x 8 vectors (RMSNorm family)
+struct Vec8 {
+  float v[8];
+};
+
+ISB_DEVICE Vec8 load8(const __nv_bfloat16* p) {
+  const uint4 raw = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  Vec8 r;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 f = __bfloat1622float2(h[i]);
+    r.v[2 * i] = f.x;
+    r.v[2 * i + 1] = f.y;
+  }
+  return r;
+}
+
+ISB_DEVICE void store8(__nv_bfloat16* p, const float* v) {
+  uint4 raw;
+  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+// RMSNorm output of 8 features of the fp32 sum ``s`` with reciprocal RMS ``rs``:
+// zero-centred (Qwen3.5) s * rs * (1 + w); plain (Qwen3) bf16(s * rs) * w.
+ISB_DEVICE void norm8(float* y, const float* s, const __nv_bfloat16* w, float rs, bool zc) {
+  const Vec8 wv = load8(w);
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    y[i] = zc ? s[i] * rs * (1.0f + wv.v[i]) : __bfloat162float(__float2bfloat16(s[i] * rs)) * wv.v[i];
+}
+
+ISB_DEVICE void norm_store8(__nv_bfloat16* o, const float* s, const __nv_bfloat16* w, float rs, bool zc) {
+  float y[8];
+  norm8(y, s, w, rs, zc);
+  store8(o, y);
+}
+
 }  // namespace isb

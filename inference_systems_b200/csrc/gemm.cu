@@ -20,6 +20,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cstdlib>
 #include <vector>
 #include <torch/extension.h>
@@ -29,6 +30,8 @@
 
 namespace isb {
 
+// Sticky error bits of the GEMM kernels (bounded waits that gave up); 128 = the fused add+RMSNorm
+// grid barrier.
 __device__ unsigned int g_gemm_err;
 
 constexpr int BM = 128;
@@ -82,6 +85,16 @@ struct GemmArgs {
   // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
   // CTA and the accumulator is zero between uses, so plain stores replace the atomics
   bool acc_plain;
+  // kRedAdd followed, in the same kernel, by residual add + RMSNorm of the accumulated rows: after
+  // a grid-wide barrier (every CTA resident: the host only asks for it when the grid fits) each CTA
+  // normalises rows blockIdx, blockIdx + grid, ...: residual <- bf16(acc + residual),
+  // norm_out <- RMSNorm(acc + residual), acc <- 0.  ``counters`` holds the barrier's two words.
+  __nv_bfloat16* norm_out;
+  __nv_bfloat16* norm_res;
+  const __nv_bfloat16* norm_w;
+  float norm_eps;
+  int norm_rows;           // token rows of the accumulator
+  bool norm_zc;
 };
 
 // Arrival counters of split-K tiles.  A launch uses one of kCounterSlots
@@ -161,6 +174,73 @@ ISB_DEVICE float gumbel_noise(int seed, int step, int row, int col) {
   h = fmix32(h ^ (uint32_t(col) * 0x165667B1u));
   const float u = (float(h >> 8) + 0.5f) * (1.0f / 16777216.0f);
   return -logf(-logf(u));
+}
+
+// Tail of an accumulating GEMM that also applies the residual add + RMSNorm (128 epilogue threads
+// of every CTA): a bounded grid barrier, then rows round-robin over the CTAs.
+__device__ __noinline__ void fused_add_norm(const GemmArgs& args) {
+  __shared__ float red[4];
+  const int tid = threadIdx.x - 64;
+  const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+  const unsigned int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  unsigned int* arrive = args.counters;
+  unsigned int* depart = args.counters + 1;
+  __threadfence();
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  if (tid == 0) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(arrive) : "memory");
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(arrive) : "memory");
+      if (v >= total) break;
+      if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(&g_gemm_err, 128u);  // rows are still normalised; the step reports the error
+        break;
+      }
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  const int T = args.norm_rows, H = args.ldo;
+  for (int row = int(cta); row < T; row += int(total)) {
+    float* a = args.acc + size_t(row) * H;
+    __nv_bfloat16* res = args.norm_res + size_t(row) * H;
+    float ss = 0.f;
+    for (int c = tid * 8; c < H; c += 128 * 8) {
+      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
+      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
+      const Vec8 r = load8(res + c);
+      const float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
+                          x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const float rs = rsqrtf((red[0] + red[1] + red[2] + red[3]) / float(H) + args.norm_eps);
+    for (int c = tid * 8; c < H; c += 128 * 8) {
+      const float4 x0 = __ldcg(reinterpret_cast<const float4*>(a + c));
+      const float4 x1 = __ldcg(reinterpret_cast<const float4*>(a + c + 4));
+      const Vec8 r = load8(res + c);
+      const float v[8] = {x0.x + r.v[0], x0.y + r.v[1], x0.z + r.v[2], x0.w + r.v[3],
+                          x1.x + r.v[4], x1.y + r.v[5], x1.z + r.v[6], x1.w + r.v[7]};
+      store8(res + c, v);
+      norm_store8(args.norm_out + size_t(row) * H + c, v, args.norm_w + c, rs, args.norm_zc);
+      *reinterpret_cast<float4*>(a + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<float4*>(a + c + 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // ``red`` is reused by the next row
+  }
+  if (tid == 0) {  // the last CTA out resets the barrier for the next launch on this counter slot
+    unsigned int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(depart) : "memory");
+    if (prev == total - 1) {
+      *arrive = 0u;
+      *depart = 0u;
+    }
+  }
 }
 
 template <int BN, bool SWAP, int EPI, bool CL = false>
@@ -637,6 +717,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   if (dbg && threadIdx.x == 64) dbg[6] = globaltimer_ns();
+  if constexpr (EPI == kRedAdd) {
+    if (args.norm_out != nullptr && epi) fused_add_norm(args);
+  }
   if constexpr (EPI == kRsPush) {
     // Every CTA counts itself in on every rank once its pushes are issued: the release at system
     // scope by one thread after the epilogue barrier orders all 128 epilogue threads' stores (and,
@@ -1192,6 +1275,58 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+}
+
+at::Tensor add_rmsnorm_acc(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
+
+// ``out = RMSNorm(residual + a . b^T)`` with ``residual`` updated and ``acc`` (fp32 [>= M, N], zero
+// between uses) re-zeroed, in ONE kernel when the split-K grid fits on the SMs at once (the add and
+// the norm run after an in-kernel grid barrier); otherwise the accumulate GEMM and the separate
+// add + RMSNorm kernel.
+at::Tensor gemm_accum_norm(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, at::Tensor residual,
+                           const at::Tensor& w, double eps, bool zc) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) >= M && acc.size(1) == N,
+              "accumulator must be contiguous fp32 [>= M, N]");
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() && residual.size(0) == M &&
+                  residual.size(1) == N && N % 8 == 0, "residual must be contiguous bf16 [M, N], N % 8 == 0");
+  at::Tensor out = at::empty_like(residual);
+  if (M == 0) return out;
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  Plan p = plan_gemm(a, b, false, 1);
+  const int tiles = p.tiles_p * p.tiles_q;
+  static const bool enabled = [] {
+    const char* e = std::getenv("ISB_FUSED_NORM");
+    return !(e && e[0] == '0');
+  }();
+  if (!enabled || tiles > num_sms()) {  // the grid barrier needs every CTA resident
+    gemm_accum(a, b, acc, 0);
+    return add_rmsnorm_acc(acc, residual, w, eps, zc);
+  }
+  // one wave: as many K splits as fit next to the tiles (each split keeps >= 2 k-blocks)
+  const int sp = std::max(1, std::min({16, num_sms() / tiles, kb_total / 2}));
+  p.kb_per = (kb_total + sp - 1) / sp;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  GemmArgs args = {};
+  args.acc = acc.data_ptr<float>();
+  args.K = a.size(1);
+  args.ldo = N;
+  args.kb_per_split = p.kb_per;
+  args.acc_plain = p.splits == 1;
+  args.counters = counter_slot();
+  args.norm_out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  args.norm_res = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  args.norm_w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  args.norm_eps = float(eps);
+  args.norm_zc = zc;
+  args.norm_rows = M;
+  if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  return out;
 }
 
 // Tensor-parallel row-parallel GEMM fused with the reduce-scatter (or, ``one_shot``, with the

@@ -17,46 +17,6 @@ namespace isb {
 
 namespace {
 
-struct Vec8 {
-  float v[8];
-};
-
-__device__ __forceinline__ Vec8 load8(const __nv_bfloat16* p) {
-  const uint4 raw = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-  Vec8 r;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __bfloat1622float2(h[i]);
-    r.v[2 * i] = f.x;
-    r.v[2 * i + 1] = f.y;
-  }
-  return r;
-}
-
-__device__ __forceinline__ void store8(__nv_bfloat16* p, const float* v) {
-  uint4 raw;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&raw);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(p) = raw;
-}
-
-__device__ __forceinline__ void norm_store8(__nv_bfloat16* o, const float* s, const __nv_bfloat16* w, float rs,
-                                            bool zc) {
-  const Vec8 wv = load8(w);
-  float y[8];
-#pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    if (zc) {
-      y[i] = s[i] * rs * (1.0f + wv.v[i]);
-    } else {
-      y[i] = __bfloat162float(__float2bfloat16(s[i] * rs)) * wv.v[i];
-    }
-  }
-  store8(o, y);
-}
-
 // MODE 3: s = acc (fp32) + residual; residual <- bf16(s); out = norm(s); acc <- 0
 __global__ void acc_norm_kernel(float* __restrict__ acc, __nv_bfloat16* __restrict__ residual,
                                 const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ out, int rows, int H,

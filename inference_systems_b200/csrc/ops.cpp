@@ -13,6 +13,8 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h, const at:
 int64_t gemm_error_word();
 at::Tensor gemm_timeline(const at::Tensor& a, const at::Tensor& b, int64_t splits);
 void gemm_accum(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, int64_t splits);
+at::Tensor gemm_accum_norm(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, at::Tensor residual,
+                           const at::Tensor& w, double eps, bool zc);
 at::Tensor add_rmsnorm_acc(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
 at::Tensor silu_mul_acc(at::Tensor acc, int64_t rows);
 at::Tensor rmsnorm(const at::Tensor& x, const at::Tensor& w, double eps, bool zc);
@@ -148,6 +150,8 @@ TORCH_LIBRARY(isb, m) {
   m.def("error_word() -> int");
   m.def("gemm_timeline(Tensor a, Tensor b, int splits) -> Tensor");
   m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
+  m.def("gemm_accum_norm(Tensor a, Tensor b, Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, "
+        "bool zero_centered) -> Tensor");
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
   m.def("tp_gemm_rs(Tensor a, Tensor b, Tensor slots, int slot_rows, Tensor(a!) staging, Tensor flags, "
@@ -188,6 +192,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("copy_kv_page", &isb::copy_kv_page);
   m.impl("gemm_timeline", &isb::gemm_timeline);
   m.impl("gemm_accum", &isb::gemm_accum);
+  m.impl("gemm_accum_norm", &isb::gemm_accum_norm);
   m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);
   m.impl("silu_mul_acc", &isb::silu_mul_acc);
   m.impl("tp_gemm_rs", &isb::tp_gemm_rs);

@@ -394,8 +394,7 @@ class HybridCausalLM(nn.Module):
             return self.comm.row_parallel_residual_norm(x, w, residual, norm_w, self.eps, self.hybrid)
         acc = getattr(self, "acc", None)
         if x.is_cuda and acc is not None and x.shape[0] <= acc.shape[0]:
-            ops.linear_accumulate(x, w, acc)
-            return ops.add_rmsnorm_acc(acc, residual, norm_w, self.eps, self.hybrid)
+            return ops.linear_add_rmsnorm(x, w, acc, residual, norm_w, self.eps, self.hybrid)
         y = ops.linear(x, w)
         return ops.add_rmsnorm(y, residual, norm_w, self.eps, self.hybrid)
 

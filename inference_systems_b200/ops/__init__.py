@@ -61,6 +61,17 @@ def add_rmsnorm_acc(acc: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, 
     return out
 
 
+def linear_add_rmsnorm(x: torch.Tensor, w: torch.Tensor, acc: torch.Tensor, residual: torch.Tensor,
+                       norm_w: torch.Tensor, eps: float, zero_centered: bool) -> torch.Tensor:
+    """``residual += x @ w^T``; return RMSNorm(residual).  On CUDA one kernel when its split-K grid
+    fits on the SMs (the add + norm run behind an in-kernel grid barrier), else the accumulate GEMM
+    and ``add_rmsnorm_acc``.  ``acc`` is the fp32 scratch, zero between uses."""
+    if x.is_cuda:
+        return cuda_ops().gemm_accum_norm(x, w, acc, residual, norm_w, eps, zero_centered)
+    linear_accumulate(x, w, acc)
+    return add_rmsnorm_acc(acc, residual, norm_w, eps, zero_centered)
+
+
 def silu_mul_acc(acc: torch.Tensor, rows: int) -> torch.Tensor:
     """Consume a packed fp32 gate/up accumulator ``[>=rows, 2I]``: return ``SiLU(gate) * up`` (bf16), re-zero it."""
     if acc.is_cuda:

@@ -406,6 +406,28 @@ def test_gemm_accumulate_and_norm(m, n, k):
     assert torch.count_nonzero(acc) == 0, "consumer must re-zero the accumulator"
 
 
+@pytest.mark.parametrize("m,n,k,zc", [(1, 1024, 2048, True), (37, 1024, 3584, False), (128, 1024, 2048, True),
+                                      (128, 1024, 3584, True), (300, 1024, 3584, True), (96, 5120, 17408, True)])
+def test_gemm_accum_norm_fused(m, n, k, zc):
+    """One kernel: split-K accumulate, in-kernel grid barrier, residual add + RMSNorm (grids that
+    fit on the SMs; larger ones take the two-kernel path).  Repeated calls cycle the barrier's
+    counter slots, which must come back to zero."""
+    g = torch.Generator(device=DEV).manual_seed(m + k + n)
+    a = torch.randn(m, k, device=DEV, generator=g).to(torch.bfloat16)
+    b = (torch.randn(n, k, device=DEV, generator=g) * 0.05).to(torch.bfloat16)
+    w = (torch.randn(n, device=DEV, generator=g) * 0.1).to(torch.bfloat16)
+    acc = torch.zeros(m + 3, n, device=DEV)
+    exp = a.float() @ b.float().t()
+    for it in range(10):
+        resid = torch.randn(m, n, device=DEV, generator=g).to(torch.bfloat16)
+        r_ref = resid.cpu().clone()
+        exp_out = ref.add_rmsnorm(exp.cpu(), r_ref, w.cpu(), 1e-6, zc)
+        out = ops.linear_add_rmsnorm(a, b, acc, resid, w, 1e-6, zc)
+        assert _rel(out, exp_out) < 1e-2, it
+        assert _rel(resid, r_ref) < 1e-2, it
+        assert torch.count_nonzero(acc) == 0, "the fused tail must re-zero the accumulator"
+
+
 def test_silu_mul_acc():
     acc = torch.randn(9, 2 * 448, device=DEV)
     exp = ref.silu_mul_packed(acc.cpu())
