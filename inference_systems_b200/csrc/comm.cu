@@ -167,15 +167,16 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
       }
     }
   }
-  // Count this CTA in on every rank (a system-scope release after the CTA barrier orders all its
+  // Count this CTA in on every rank (a system-scope fence after the CTA barrier orders all its
   // threads' pushes); the last CTA here then moves the targets on and, unless told otherwise,
   // waits until every owner's rows have arrived, so the grid completes with the full activation.
   __syncthreads();
   if (tid == 0) {
     if (one_shot_rank < 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");  // one fence orders the pushes before every count
       for (int q = 0; q < world; ++q) {
         unsigned int* f = reinterpret_cast<unsigned int*>(ag_flags[q]);
-        asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
+        asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(f) : "memory");
       }
     }
     unsigned int prev;

@@ -689,13 +689,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tok0 = SWAP ? q0 : p0, ntok = SWAP ? BN : BM;
             const int f0 = SWAP ? p0 : q0, nf = SWAP ? BM : BN;
             const int T = SWAP ? args.Q_rows : args.P_rows, F = SWAP ? args.P_rows : args.Q_rows;
-            for (int i = tid; i < ntok * (nf / 4); i += 128) {
-              const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
-              if (tok >= T || f >= F) continue;
-              float* a = args.acc + size_t(tok) * args.ldo + f;
-              const float4 w = __ldcg(reinterpret_cast<const float4*>(a));
-              *reinterpret_cast<float4*>(a) = make_float4(0.f, 0.f, 0.f, 0.f);
-              rs_push4(args, tok, f, w.x, w.y, w.z, w.w);
+            // 8 independent L2 reads in flight per thread before any store: a store to the
+            // staging rows or to a slot could alias the next read, so one read per iteration
+            // would pay a full L2 round trip each (32 of them per thread for a 128 x 128 tile)
+            constexpr int UN = 8;
+            const int total = ntok * (nf / 4);
+            for (int base = tid; base < total; base += 128 * UN) {
+              float4 w[UN];
+              float* ap[UN];
+#pragma unroll
+              for (int u = 0; u < UN; ++u) {
+                const int i = base + u * 128;
+                const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
+                ap[u] = (i < total && tok < T && f < F) ? args.acc + size_t(tok) * args.ldo + f : nullptr;
+                if (ap[u]) w[u] = __ldcg(reinterpret_cast<const float4*>(ap[u]));
+              }
+#pragma unroll
+              for (int u = 0; u < UN; ++u) {
+                if (!ap[u]) continue;
+                const int i = base + u * 128;
+                const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
+                *reinterpret_cast<float4*>(ap[u]) = make_float4(0.f, 0.f, 0.f, 0.f);
+                rs_push4(args, tok, f, w[u].x, w[u].y, w[u].z, w[u].w);
+              }
             }
           }
         }
@@ -721,16 +737,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (args.norm_out != nullptr && epi) fused_add_norm(args);
   }
   if constexpr (EPI == kRsPush) {
-    // Every CTA counts itself in on every rank once its pushes are issued: the release at system
-    // scope by one thread after the epilogue barrier orders all 128 epilogue threads' stores (and,
-    // for the tile's last split, the staged sums it read) before the count; the owners wait for
+    // Every CTA counts itself in on every rank once its pushes are issued: one system-scope fence
+    // by one thread after the epilogue barrier orders all 128 epilogue threads' stores (and, for
+    // the tile's last split, the staged sums it read) before the counts; the owners wait for
     // world x gridDim CTAs.  No CTA waits for another, no fence drains the whole grid.
     if (epi) {
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
+        asm volatile("fence.acq_rel.sys;" ::: "memory");  // one fence orders the stores before every count
         for (int r = 0; r < args.ndst; ++r) {
           unsigned int* flag = reinterpret_cast<unsigned int*>(args.peer_flags[(args.rank + r) % args.ndst]);
-          asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
+          asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
         }
       }
     }

