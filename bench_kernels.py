@@ -177,27 +177,35 @@ def cases(b: int) -> dict:
         return [fn], (q.numel() * 2 * 3 + kc.numel() * 4), flops
     out["attention_prefill_tc"] = attention_prefill
 
-    def gdn_chunked():
-        # chunked GDN prefill: one 8192-token sequence, 16 key / 16 value heads
+    def gdn_chunked(nseq: int, n: int):
+        # chunked GDN prefill: nseq sequences of n tokens, 16 key / 16 value heads (0.8B shape)
         hk = hv = 16
         d = 128
-        n = 8192
         c = 2 * hk * d + hv * d
         p = c + hv * d + 2 * hv
-        proj = torch.randn(n, p, device=dev).to(bf)
+        t = nseq * n
+        proj = torch.randn(t, p, device=dev).to(bf)
         conv_w = (torch.randn(c, 4, device=dev) * 0.5).to(bf)
         a_log, dt = torch.zeros(hv, device=dev), torch.ones(hv, device=dev)
         nw = torch.ones(d, device=dev).to(bf)
-        slots = torch.zeros(1, device=dev, dtype=torch.int32)
-        rec = torch.zeros(2, hv, d, d, device=dev)
-        conv = torch.zeros(2, c, 3, device=dev).to(bf)
-        nc = n // 64
-        info = torch.tensor([0] * nc + list(range(0, n, 64)) + [64] * nc + [0, nc], dtype=torch.int32, device=dev)
-        cu = torch.tensor([0, n], dtype=torch.int32, device=dev)
+        slots = torch.arange(nseq, device=dev, dtype=torch.int32)
+        rec = torch.zeros(nseq + 1, hv, d, d, device=dev)
+        conv = torch.zeros(nseq + 1, c, 3, device=dev).to(bf)
+        per = (n + 63) // 64
+        seq, t0, nn = [], [], []
+        for i in range(nseq):
+            for st in range(0, n, 64):
+                seq.append(i)
+                t0.append(i * n + st)
+                nn.append(min(64, n - st))
+        nc = len(seq)
+        info = torch.tensor(seq + t0 + nn + [i * per for i in range(nseq + 1)], dtype=torch.int32, device=dev)
+        cu = torch.arange(nseq + 1, dtype=torch.int32, device=dev) * n
         fn = lambda: torch.ops.isb.gdn_prefill_chunked(proj, cu, slots, info, nc, conv_w, a_log, dt, nw, rec,  # noqa
                                                        conv, hk, hv, 1e-6)
-        return [fn], proj.numel() * 2 + n * hv * d * 2, 0
-    out["gdn_prefill_chunked"] = gdn_chunked
+        return [fn], proj.numel() * 2 + t * hv * d * 2, 0
+    out["gdn_prefill_chunked"] = lambda: gdn_chunked(1, 8192)
+    out["gdn_prefill_chunked_32x512"] = lambda: gdn_chunked(32, 512)
 
     def acc_norm():
         resid = torch.randn(b, 1024, device=dev).to(bf)
@@ -403,7 +411,45 @@ def tp_emulated_bench() -> None:
     assert torch.ops.isb.error_word() == 0
 
 
+def split_sweep_bench() -> None:
+    """Split-K factor of the accumulating decode GEMM (``gemm_accum``) and of the reduce-scatter
+    GEMM (``tp_gemm_rs``, one-shot, 2 emulated ranks): time per launch with the weights cycled
+    through enough copies to exceed L2, so each launch streams its weights from HBM."""
+    c = ops.cuda_ops()
+    dev, bf = "cuda", torch.bfloat16
+    hh = 1024
+    for k in (3584, 2048, 1792, 448):
+        copies = max(2, (300 << 20) // (hh * k * 2))
+        ws = [(torch.randn(hh, k, device=dev) * 0.02).to(bf) for _ in range(copies)]
+        for b in (1, 128):
+            x = torch.randn(b, k, device=dev).to(bf)
+            acc = torch.zeros(b, hh, device=dev)
+            slots = [torch.zeros(2, b, hh, dtype=bf, device=dev) for _ in range(2)]
+            ctl = [torch.zeros(8, dtype=torch.int32, device=dev) for _ in range(2)]
+            staging = torch.zeros(b, hh, device=dev)
+            tab = lambda ts: torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=dev)  # noqa: E731
+            slot_ptrs, rs_ptrs = tab(slots), tab(ctl)
+            row = {"path": "split-K sweep (weights from HBM)", "tokens": b, "N": hh, "K": k,
+                   "weight_mb": round(hh * k * 2 / 1e6, 2)}
+            for sp in (1, 2, 4, 8, 16, 0):
+                if sp > (k + 63) // 64:
+                    continue
+                t_acc = graph_time_us([lambda w=w: c.gemm_accum(x, w, acc, sp) for w in ws])
+                t_rs = graph_time_us([lambda w=w: c.tp_gemm_rs(x, w, slot_ptrs, b, staging, rs_ptrs, 0, b, sp, True)
+                                      for w in ws])
+                key = "auto" if sp == 0 else str(sp)
+                row[f"accum_us_s{key}"] = round(t_acc, 2)
+                row[f"rs_us_s{key}"] = round(t_rs, 2)
+            torch.cuda.synchronize()
+            print(json.dumps(row), flush=True)
+    assert torch.ops.isb.error_word() == 0
+
+
 def main():
+    if "--split-sweep" in sys.argv:
+        load_extension()
+        split_sweep_bench()
+        return
     if "--tp-emulated" in sys.argv:
         load_extension()
         tp_emulated_bench()

@@ -6,12 +6,15 @@
 //   S  = Q K^T           tcgen05.mma M=128, N=64,  K=256  -> TMEM (double-buffered)
 //   softmax (online)     warps 4-7, one TMEM lane (= query row) per thread
 //   O += P V             tcgen05.mma M=128, N=256, K=64   -> TMEM
-// Q and K arrive by TMA (128-byte swizzle, K-major).  V is the B operand of the
-// second MMA with the key dimension as K, so it must be key-contiguous: warps
-// 2-3 load each V block and write its transpose into shared memory in the same
-// swizzled K-major layout (8x8 register transposes, 16-byte stores).  P is
-// written by the softmax threads in that layout too.  Every wait is bounded
-// (globaltimer): on expiry the kernel records an error, stops and frees TMEM.
+// Q, K and V arrive by TMA (128-byte swizzle).  K is the K-major B operand of the first MMA;
+// V is the B operand of the second in MN-major form, read straight from its tile (a swizzled
+// [64 keys][64 dims] box is the canonical MN-major layout: dim blocks one box apart, key
+// groups of 8 one 1024-byte atom apart), so no transpose is needed.  P is written by the
+// softmax threads (K-major, swizzled) into one of two buffers, so the softmax of block j+1
+// overlaps P V of block j.  The running maximum is raised only when a row's block maximum
+// exceeds it by more than 8 (log2 units): P entries stay <= 2^8, and O is rescaled in tensor
+// memory only on those raises.  Every wait is bounded (globaltimer): on expiry the kernel
+// records an error, stops and frees TMEM.
 // Parity (behaviour): flash-attn varlen prefill with a block table and the
 // sigmoid output gate (``nanovllm/layers/attention.py:59-75``,
 // ``nanovllm/models/qwen3_5.py:86,95``).
@@ -32,16 +35,16 @@ constexpr int MR = 128;     // MMA rows (tokens x heads)
 constexpr int PAGE = 256;   // KV page
 constexpr int Q_BYTES = MR * HD * 2;    // 4 swizzle-atom columns of 16 KB
 constexpr int K_BYTES = KB * HD * 2;    // 4 atom columns of 8 KB
-constexpr int VT_BYTES = HD * KB * 2;   // 256 rows x 128 B
+constexpr int V_BYTES = KB * HD * 2;    // 4 boxes of [64 keys x 128 B]
 constexpr int P_BYTES = MR * KB * 2;    // 128 rows x 128 B
 constexpr int BAR_BYTES = 256;
-constexpr int SMEM_BYTES = Q_BYTES + 2 * K_BYTES + 2 * VT_BYTES + P_BYTES + BAR_BYTES + 1024;
+constexpr int SMEM_BYTES = Q_BYTES + 2 * K_BYTES + 2 * V_BYTES + 2 * P_BYTES + BAR_BYTES + 1024;
+constexpr float kRescaleLog2 = 8.f;     // lazy-rescale threshold of the running maximum
 constexpr uint32_t TMEM_COLS = 512;     // S0 [0,64) S1 [64,128) O [256,512)
 
 __device__ unsigned int g_attn_tc_err;
 
 struct TcArgs {
-  const __nv_bfloat16* v_cache;  // [blocks, Hkv, 256, HD]
   const int* cu_q;
   const int* ctx_lens;
   const int* block_tables;
@@ -57,26 +60,39 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<const uint32_t*>(&h);
 }
 
+// MN-major operand, 128-byte swizzle: 64-element blocks along M/N are ``lbo`` bytes apart,
+// groups of 8 rows along K are 1024 bytes apart.
+__device__ __forceinline__ uint64_t smem_desc_mn_sw128(const void* tile, uint32_t lbo) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= (1024ull >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
 template <int G>
 __global__ void __launch_bounds__(256, 1)
-    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK, TcArgs a) {
+    attn_prefill_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, TcArgs a) {
   constexpr int QT = MR / G;          // tokens per tile; G * QT <= 128 rows are used
   constexpr int QROWS = G * QT;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* q_s = smem;
   uint8_t* k_s = q_s + Q_BYTES;
-  uint8_t* vt_s = k_s + 2 * K_BYTES;
-  uint8_t* p_s = vt_s + 2 * VT_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + P_BYTES);
+  uint8_t* v_s = k_s + 2 * K_BYTES;
+  uint8_t* p_s = v_s + 2 * V_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(p_s + 2 * P_BYTES);
   uint64_t* qfull = bars;
   uint64_t* kfull = bars + 1;    // [2]
   uint64_t* vfull = bars + 3;    // [2]
   uint64_t* kvfree = bars + 5;   // [2]
   uint64_t* sfull = bars + 7;    // [2]
   uint64_t* sfree = bars + 9;    // [2]
-  uint64_t* pready = bars + 11;
-  uint64_t* pvdone = bars + 12;
+  uint64_t* pready = bars + 11;  // [2]
+  uint64_t* pvdone = bars + 13;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   pdl_trigger();
@@ -95,16 +111,17 @@ __global__ void __launch_bounds__(256, 1)
     mbar_init(qfull, 1);
     for (int s = 0; s < 2; ++s) {
       mbar_init(&kfull[s], 1);
-      mbar_init(&vfull[s], 64);
+      mbar_init(&vfull[s], 1);
       mbar_init(&kvfree[s], 1);
       mbar_init(&sfull[s], 1);
       mbar_init(&sfree[s], 128);
+      mbar_init(&pready[s], 128);
+      mbar_init(&pvdone[s], 1);
     }
-    mbar_init(pready, 128);
-    mbar_init(pvdone, 1);
     fence_mbar_init();
     prefetch_tmap(&tmQ);
     prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
   }
   if (warp == 1) tmem_alloc(tmem_slot, TMEM_COLS);
   tc_fence_before();
@@ -114,7 +131,7 @@ __global__ void __launch_bounds__(256, 1)
   const uint32_t tO = tmem + 256;
 
   if (warp == 0) {
-    // ---------------------------------------------------- TMA: Q once, K blocks
+    // ---------------------------------------------------- TMA: Q once, K and V blocks
     if (lane == 0) {
       mbar_arrive_expect_tx(qfull, QROWS * HD * 2);  // rows past QROWS stay unused
       for (int c = 0; c < 4; ++c) tma_load_3d(q_s + c * (Q_BYTES / 4), &tmQ, qfull, c * 64, kvh * G, q_start + q0);
@@ -125,12 +142,15 @@ __global__ void __launch_bounds__(256, 1)
         const int row = (bt[key0 / PAGE] * a.Hkv + kvh) * PAGE + key0 % PAGE;
         mbar_arrive_expect_tx(&kfull[s], K_BYTES);
         for (int c = 0; c < 4; ++c) tma_load_2d(k_s + s * K_BYTES + c * (K_BYTES / 4), &tmK, &kfull[s], c * 64, row);
+        mbar_arrive_expect_tx(&vfull[s], V_BYTES);
+        for (int c = 0; c < 4; ++c) tma_load_2d(v_s + s * V_BYTES + c * (V_BYTES / 4), &tmV, &vfull[s], c * 64, row);
       }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------- MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idS = idesc_bf16_f32(MR, KB), idO = idesc_bf16_f32(MR, HD);
+      constexpr uint32_t idS = idesc_bf16_f32(MR, KB);
+      constexpr uint32_t idO = idesc_bf16_f32(MR, HD) | (1u << 16);  // B = V, MN-major
       bool ok = mbar_wait(qfull, 0);
       auto issue_s = [&](int j) -> bool {
         const int s = j & 1;
@@ -150,54 +170,21 @@ __global__ void __launch_bounds__(256, 1)
       for (int j = 0; ok && j < nkb; ++j) {
         if (j + 1 < nkb && !issue_s(j + 1)) { ok = false; break; }
         const int s = j & 1;
-        if (!mbar_wait(pready, j & 1) || !mbar_wait(&vfull[s], (j >> 1) & 1)) { ok = false; break; }
+        if (!mbar_wait(&pready[s], (j >> 1) & 1) || !mbar_wait(&vfull[s], (j >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < KB / 16; ++k) {
-          const uint64_t ad = smem_desc_sw128(p_s) + 2 * k;
-          const uint64_t bd = smem_desc_sw128(vt_s + s * VT_BYTES) + 2 * k;
+          const uint64_t ad = smem_desc_sw128(p_s + s * P_BYTES) + 2 * k;
+          const uint64_t bd = smem_desc_mn_sw128(v_s + s * V_BYTES + k * 2048, V_BYTES / 4);
           mma_bf16(tO, ad, bd, idO, (j > 0 || k > 0) ? 1u : 0u);
         }
         mma_commit(&kvfree[s]);
-        mma_commit(pvdone);
+        mma_commit(&pvdone[s]);
       }
       if (!ok) atomicOr(&g_attn_tc_err, 2u);
     }
   } else if (warp < 4) {
-    // ---------------------------------------------------- V^T producers (64 threads)
-    const int vt = threadIdx.x - 64;
-    for (int j = 0; j < nkb; ++j) {
-      const int s = j & 1;
-      if (j >= 2 && !mbar_wait(&kvfree[s], ((j >> 1) - 1) & 1)) { atomicOr(&g_attn_tc_err, 4u); break; }
-      const int key0 = j * KB;
-      const __nv_bfloat16* vsrc =
-          a.v_cache + ((size_t(bt[key0 / PAGE]) * a.Hkv + kvh) * PAGE + key0 % PAGE) * HD;
-      uint8_t* dst = vt_s + s * VT_BYTES;
-      // 8 keys x 8 dims micro-tiles; V^T row d holds 64 keys (128 B, swizzled 16-byte chunks)
-      for (int m = vt; m < (KB / 8) * (HD / 8); m += 64) {
-        const int kc = m & 7, dc = m >> 3;
-        uint4 in[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) in[i] = *reinterpret_cast<const uint4*>(vsrc + size_t(kc * 8 + i) * HD + dc * 8);
-        // element (key i, dim x) of the micro-tile; x is a compile-time constant after unrolling
-        auto e = [&](int i, int x) -> uint32_t {
-          const uint32_t w = x < 2 ? in[i].x : x < 4 ? in[i].y : x < 6 ? in[i].z : in[i].w;
-          return (x & 1) ? (w >> 16) : (w & 0xFFFFu);
-        };
-#pragma unroll
-        for (int x = 0; x < 8; ++x) {
-          const int d = dc * 8 + x;
-          uint4 o;
-          o.x = e(0, x) | (e(1, x) << 16);
-          o.y = e(2, x) | (e(3, x) << 16);
-          o.z = e(4, x) | (e(5, x) << 16);
-          o.w = e(6, x) | (e(7, x) << 16);
-          *reinterpret_cast<uint4*>(dst + d * 128 + ((kc ^ (d & 7)) * 16)) = o;
-        }
-      }
-      fence_proxy_async_smem();
-      mbar_arrive(&vfull[s]);
-    }
+    // warps 2-3: idle (K and V both arrive by TMA)
   } else {
     // ---------------------------------------------------- softmax + epilogue (warps 4..7)
     const int r = threadIdx.x - 128;                       // query row == TMEM lane
@@ -226,8 +213,11 @@ __global__ void __launch_bounds__(256, 1)
         sc[c] = x;
         mx = fmaxf(mx, x);
       }
-      const float m_new = fmaxf(m, mx);  // finite: key 0 is visible to every row
-      const float alpha = exp2f(m - m_new);
+      // the running maximum moves only when this block's exceeds it by more than 2^8 (the first
+      // block always sets it: key 0 is visible to every row, so it is finite from then on)
+      const bool raise = mx > m + kRescaleLog2;
+      const float m_new = raise ? mx : m;
+      const float alpha = raise ? exp2f(m - m_new) : 1.f;
       float sum = 0.f;
       uint32_t pk[KB / 2];
 #pragma unroll
@@ -238,11 +228,13 @@ __global__ void __launch_bounds__(256, 1)
       }
       l = l * alpha + sum;
       m = m_new;
+      const int pb = j & 1;
       if (j > 0) {
-        // P(j-1) and O must be free: the previous P V has completed
-        if (!mbar_wait(pvdone, (j - 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, alpha < 1.f)) {
+        const bool rescale = __any_sync(0xffffffffu, alpha < 1.f);
+        if (rescale) {
+          // O is rescaled in place: every earlier P V (the last one, j-1, included) has completed
+          if (!mbar_wait(&pvdone[(j - 1) & 1], ((j - 1) >> 1) & 1)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < HD; c += 32) {
             float o[32];
@@ -251,18 +243,22 @@ __global__ void __launch_bounds__(256, 1)
             for (int i = 0; i < 32; ++i) o[i] *= alpha;
             tmem_st32(tO + c + lane_base, o);
           }
+        } else if (j > 1) {
+          // P buffer pb is free once P V of block j-2 has completed
+          if (!mbar_wait(&pvdone[pb], ((j - 2) >> 1) & 1)) { ok = false; break; }
+          tc_fence_after();
         }
       }
-      uint8_t* prow = p_s + r * 128;
+      uint8_t* prow = p_s + pb * P_BYTES + r * 128;
 #pragma unroll
       for (int c = 0; c < 8; ++c)
         *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) * 16)) =
             make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(pready);
+      mbar_arrive(&pready[pb]);
     }
-    if (ok && !mbar_wait(pvdone, (nkb - 1) & 1)) ok = false;
+    if (ok && !mbar_wait(&pvdone[(nkb - 1) & 1], ((nkb - 1) >> 1) & 1)) ok = false;
     if (!ok) atomicOr(&g_attn_tc_err, 8u);
     tc_fence_after();
     const float inv_l = (ok && l > 0.f) ? 1.f / l : 0.f;
@@ -333,18 +329,6 @@ struct DecArgs {
   int max_chunks;
   int nitems;       // max_chunks * B * Hkv
 };
-
-// MN-major operand, 128-byte swizzle: 64-element blocks along M/N are ``lbo`` bytes apart,
-// groups of 8 rows along K are 1024 bytes apart.
-__device__ __forceinline__ uint64_t smem_desc_mn_sw128(const void* tile, uint32_t lbo) {
-  const uint64_t addr = smem_u32(tile);
-  uint64_t d = (addr >> 4) & 0x3FFFull;
-  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
-  d |= (1024ull >> 4) << 32;
-  d |= 1ull << 46;
-  d |= 2ull << 61;
-  return d;
-}
 
 __device__ __forceinline__ void bar_sync_consumers() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
@@ -608,10 +592,11 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn_tc() {
 }
 
 template <int G>
-void launch_tc(const at::Tensor& q, const at::Tensor& kc, const TcArgs& a, int B, int max_seqlen_q, cudaStream_t st) {
+void launch_tc(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const TcArgs& a, int B,
+               int max_seqlen_q, cudaStream_t st) {
   constexpr int QT = MR / G;
   const int T = q.size(0);
-  CUtensorMap tq, tk;
+  CUtensorMap tq, tk, tv;
   {
     cuuint64_t dims[3] = {cuuint64_t(HD), cuuint64_t(a.Hq), cuuint64_t(T)};
     cuuint64_t strides[2] = {cuuint64_t(HD) * 2, cuuint64_t(a.Hq) * HD * 2};
@@ -632,6 +617,10 @@ void launch_tc(const at::Tensor& q, const at::Tensor& kc, const TcArgs& a, int B
                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (k) failed: ", int(r));
+    r = encode_fn_tc()(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, vc.data_ptr(), dims, strides, box, es,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (v) failed: ", int(r));
   }
   auto kern = attn_prefill_tc_kernel<G>;
   static bool attr = false;
@@ -641,7 +630,7 @@ void launch_tc(const at::Tensor& q, const at::Tensor& kc, const TcArgs& a, int B
     attr = true;
   }
   const dim3 grid((max_seqlen_q + QT - 1) / QT, a.Hkv, B);
-  launch_pdl(kern, grid, dim3(256), SMEM_BYTES, st, tq, tk, a);
+  launch_pdl(kern, grid, dim3(256), SMEM_BYTES, st, tq, tk, tv, a);
 }
 
 template <int G>
@@ -746,7 +735,6 @@ at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, con
   at::Tensor out = at::empty({T, Hq * HD}, q.options());
   if (T == 0 || B == 0) return out;
   TcArgs a = {};
-  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(vc.data_ptr());
   a.cu_q = cu_q.data_ptr<int>();
   a.ctx_lens = ctx_lens.data_ptr<int>();
   a.block_tables = block_tables.data_ptr<int>();
@@ -758,12 +746,12 @@ at::Tensor attention_prefill_tc(const at::Tensor& q, const at::Tensor& gate, con
   a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   auto st = at::cuda::getCurrentCUDAStream();
   switch (Hq / Hkv) {
-    case 1: launch_tc<1>(q, kc, a, B, int(max_seqlen_q), st); break;
-    case 2: launch_tc<2>(q, kc, a, B, int(max_seqlen_q), st); break;
-    case 3: launch_tc<3>(q, kc, a, B, int(max_seqlen_q), st); break;
-    case 4: launch_tc<4>(q, kc, a, B, int(max_seqlen_q), st); break;
-    case 6: launch_tc<6>(q, kc, a, B, int(max_seqlen_q), st); break;
-    case 8: launch_tc<8>(q, kc, a, B, int(max_seqlen_q), st); break;
+    case 1: launch_tc<1>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
+    case 2: launch_tc<2>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
+    case 3: launch_tc<3>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
+    case 4: launch_tc<4>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
+    case 6: launch_tc<6>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
+    case 8: launch_tc<8>(q, kc, vc, a, B, int(max_seqlen_q), st); break;
     default: TORCH_CHECK(false, "unsupported GQA group");
   }
   return out;

@@ -17,17 +17,21 @@
 //               O = (e^{G} * Q) S0 + P D,   P_tj = e^{G_t - G_j} (q_t . k_j)  (j <= t)
 //               S_n = e^{G_n} S0 + (e^{G_n - G} * K)^T D
 //
-// gdn_chunk_prep_kernel: one CTA per (chunk, value head), all chunks in
-//   parallel: causal conv + SiLU, L2 norms, beta/decay, and everything above
-//   that does not depend on S0 (W, U, e^G Q, e^{G_n-G} K, P, e^{G_n}).
-// gdn_chunk_state_kernel: one CTA per (32 value columns, value head, sequence)
-//   carries its slice of S through the sequence's chunks in order (value
-//   columns of the state evolve independently), writes the pre-norm output
-//   and the final state, and commits the new conv window.
+// Two implementations of the chunk form (ISB_GDN_CHUNK_TC=0 selects the second):
+// gdn_chunk_tc_kernel (default): one CTA per (value head, sequence) carries the state in tensor
+//   memory and runs every product above on the tensor cores (details at the kernel).
+// gdn_chunk_prep_kernel + gdn_chunk_state_kernel: SIMT fp32; one CTA per (chunk, value head)
+//   computes everything that does not depend on S0 (W, U, e^G Q, e^{G_n-G} K, P, e^{G_n}) for
+//   all chunks in parallel, then one CTA per (32 value columns, value head, sequence) carries
+//   its slice of S through the chunks in order and commits the new conv window.
+// gdn_chunk_conv_commit_kernel (tensor-core path): the new conv windows.
 // gdn_chunk_norm_kernel: gated RMSNorm of each (token, head) row.
-// All arithmetic is fp32; the projection input is bf16 as in the scan.
+// SIMT arithmetic is fp32, tensor-core products tf32 x tf32 -> fp32; the projection input is
+// bf16 as in the scan.
 
 #include <ATen/cuda/CUDAContext.h>
+
+#include <cstdlib>
 #include <torch/extension.h>
 
 #include "common.cuh"
@@ -71,6 +75,8 @@ struct ChunkArgs {
   __nv_bfloat16* out;     // [T, Hv * D]
   int Hk, Hv, C, T;
   float eps;
+  unsigned int* err;      // the GDN kernels' sticky error word
+  float* dbg;             // optional: intermediates of the first chunk of CTA (0, 0) (tests only)
 };
 
 constexpr int kPrepSmemFloats = 3 * CL * LDR + 2 * CL * LDC + 3 * CL;
@@ -365,6 +371,576 @@ __global__ void __launch_bounds__(256) gdn_chunk_state_kernel(ChunkArgs a) {
   }
 }
 
+// ------------------------------------------------------------------ tensor-core form
+// gdn_chunk_tc_kernel: one CTA per (value head, sequence) walks the sequence's chunks in order
+// with the state held TRANSPOSED in tensor memory, S^T [value lanes][key columns] (fp32), and
+// every product of the chunk form on the tensor cores (tcgen05.mma kind::tf32, fp32
+// accumulators in TMEM; operands are fp32 in shared memory, read as tf32):
+//
+//   M1  [K;Q] K^T        M=128 (64 k rows, 64 q rows)  N=64   K=128 keys   -> k.k, q.k
+//       (threads: A = decayed strict-lower b * k.k, P = decayed causal q.k; T = (I+A)^-1 by
+//        16 x 16 blocks in fp32; Tb = T diag(b), Tbe = T diag(b e^G))
+//   M2  [Tbe;Tb] K       M=128 (64 used)  N=128 keys  K=64 tokens           -> W = Tbe K
+//   M3  V^T Tb^T         M=128 values  N=64 tokens  K=64 tokens             -> U^T
+//   M4  + S^T (-W)^T     A = S^T from TMEM, K=128 keys                      -> D^T = U^T - S^T W^T
+//   M5  S^T (e^G Q)^T    A = S^T from TMEM                                 -> O^T (inter-chunk part)
+//       (threads: S^T *= e^{G_n} in TMEM)
+//   M6  + D^T P^T        A = D^T from TMEM, K=64 tokens                    -> O^T
+//   M7  + D^T K'         A = D^T from TMEM, B = e^{G_n - G} K               -> S^T (next chunk's state)
+//
+// Shared-memory tiles use the 128-byte swizzle with 32-float (128-byte) rows; one tile serves
+// as a K-major operand (rows = M/N) and as an MN-major one (rows = K) of the same bytes: the
+// k rows are the B of M1 (K-major over keys) and the B of M2 / M7 (MN-major over keys, K =
+// tokens).  V is stored [token][value] and read MN-major as V^T.  Every wait is bounded; on
+// expiry the CTA records an error, stops and frees its tensor memory.
+constexpr int TC_THREADS = 256;
+constexpr int KQ_SLAB = 128 * 128;            // bytes: 128 rows (k 0-63, q 64-127) x 32 floats
+constexpr int KQ_BYTES = 4 * KQ_SLAB;         // 4 key slabs: 64 KB
+constexpr int MN_BLOCK = 64 * 128;            // MN-major tiles: 64 token rows x 32 floats per block
+constexpr int MN_BYTES = 4 * MN_BLOCK;        // 128 values (V) or keys (K): 32 KB
+constexpr int W_SLAB = 64 * 128;
+constexpr int W_BYTES = 4 * W_SLAB;           // 32 KB
+constexpr int TT_SLAB = 128 * 128;            // rows 0-63 Tbe, 64-127 Tb; 32 tokens per slab
+constexpr int TT_BYTES = 2 * TT_SLAB;         // 32 KB
+constexpr int P_SLAB = 64 * 128;
+constexpr int P_BYTES_TC = 2 * P_SLAB;        // 16 KB
+// kq | V (MN) | K (MN) | W (also: raw inputs, then A and T of the solve) | T stack (also: raw
+// inputs, then the solve's block products) | P | scalars | barrier
+constexpr int TC_SMEM = KQ_BYTES + 2 * MN_BYTES + W_BYTES + TT_BYTES + P_BYTES_TC + 4 * 64 * 4 + 64 + 1024;
+constexpr uint32_t TC_TMEM_COLS = 512;
+constexpr uint32_t CS = 0, C1 = 128, C2 = 192, C3 = 320, C4 = 384;  // S^T, k.k|q.k, W, D^T, O^T
+
+// K-major tiles (128-byte swizzle, 16-byte granules): byte offset of float (r, c) in a tile of
+// 128-byte rows whose 32-float slabs are ``slab`` bytes apart
+__device__ __forceinline__ uint32_t swz(int r, int c, int slab) {
+  return uint32_t((c >> 5) * slab + r * 128 + ((((c & 31) >> 2) ^ (r & 7)) << 4) + (c & 3) * 4);
+}
+
+// MN-major tf32 tiles use the 128-byte swizzle with 32-byte granules (the only MN-major layout
+// the tensor core takes for 32-bit operands): rows along K are 128 bytes (32 floats along M/N)
+// apart, the four 32-byte granules of a row XOR-permuted by (row mod 4), 4-row atoms of 512
+// bytes, 32-float M/N blocks ``MN_BLOCK`` bytes apart.  Byte offset of float (K row r, M/N c).
+__device__ __forceinline__ uint32_t swz_mn(int r, int c) {
+  return uint32_t((c >> 5) * MN_BLOCK + r * 128 + ((((c & 31) >> 3) ^ (r & 3)) << 5) + (c & 7) * 4);
+}
+
+// kind::tf32 instruction descriptor: fp32 accumulate, tf32 A and B
+__host__ __device__ constexpr uint32_t idesc_tf32(int m, int n, bool a_mn = false, bool b_mn = false,
+                                                  bool neg_b = false) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | (neg_b ? 1u << 14 : 0u) | (a_mn ? 1u << 15 : 0u) |
+         (b_mn ? 1u << 16 : 0u) | (uint32_t(n >> 3) << 17) | (uint32_t(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_tf32_ss(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// A operand from tensor memory (M lanes x K columns, K-major)
+__device__ __forceinline__ void mma_tf32_ts(uint32_t d, uint32_t a_tmem, uint64_t b, uint32_t idesc, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d),
+      "r"(a_tmem), "l"(b), "r"(idesc), "r"(acc));
+}
+
+// MN-major tf32 operand descriptor (layout type 1: 128-byte swizzle, 32-byte granules):
+// LBO = M/N block stride, SBO = 512 (4-row atoms along K)
+__device__ __forceinline__ uint64_t desc_mn(const void* tile) {
+  const uint64_t addr = smem_u32(tile);
+  uint64_t d = (addr >> 4) & 0x3FFFull;
+  d |= uint64_t((MN_BLOCK >> 4) & 0x3FFF) << 16;
+  d |= (512ull >> 4) << 32;
+  d |= 1ull << 46;
+  d |= 1ull << 61;
+  return d;
+}
+
+__global__ void __launch_bounds__(TC_THREADS, 1) gdn_chunk_tc_kernel(ChunkArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* kq = smem;
+  uint8_t* vt = kq + KQ_BYTES;     // V [token][value], MN-major
+  uint8_t* km = vt + MN_BYTES;     // K [token][key], MN-major (K' = e^{G_n - G} K after M2)
+  uint8_t* wt = km + MN_BYTES;
+  uint8_t* tt = wt + W_BYTES;
+  uint8_t* pt = tt + TT_BYTES;
+  // the solve's scratch lives in tiles that are free between the conv and M2
+  float* A_s = reinterpret_cast<float*>(wt);  // [64][64] strict-lower A, column index XOR (row & 31)
+  float* T_s = A_s + 64 * 64;                  // [64][64] T = (I + A)^-1
+  float* M_s = reinterpret_cast<float*>(tt);   // [3][16][17] block products
+  float* beta_s = reinterpret_cast<float*>(pt + P_BYTES_TC);
+  float* g_s = beta_s + 64;
+  float* G_s = g_s + 64;
+  float* eG_s = G_s + 64;
+  uint64_t* bar = reinterpret_cast<uint64_t*>(eG_s + 64);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar + 1);
+  int* s_ok = reinterpret_cast<int*>(bar + 2);
+
+  const int h = blockIdx.x, s = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  pdl_trigger();
+  pdl_wait();  // proj, the chunk table and the pools come from earlier work on the stream
+  const int c0 = a.cu_chunks[s], c1 = a.cu_chunks[s + 1];
+  if (c1 <= c0) return;  // whole CTA, before any TMEM is taken
+  const int seq0 = a.cu_seqlens[s], slot = a.slots[s];
+  const int r = a.Hv / a.Hk, hk = h / r, kd = a.Hk * D;
+
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+    *s_ok = 1;
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, TC_TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int qd = warp & 3, hf = warp >> 2;            // TMEM lane quarter, column half
+  const int lrow = qd * 32 + lane;                    // TMEM lane of this thread
+  const uint32_t lane_addr = tmem + (uint32_t(qd * 32) << 16);
+  uint32_t phase = 0;
+
+  // bounded wait for the last commit, shared by the whole CTA
+  auto wait_mma = [&](unsigned int code) -> bool {
+    if (tid == 0 && *s_ok && !mbar_wait(bar, phase)) {
+      atomicOr(a.err, code);
+      *s_ok = 0;
+    }
+    phase ^= 1u;
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    return *s_ok != 0;
+  };
+  auto commit = [&]() { mma_commit(bar); };
+
+  // ---- state in: S^T lane v = value column v, TMEM column k = key k
+  float* S = a.rec + ((size_t(slot) * a.Hv + h) * D) * D;
+  {
+    float v[32];
+    for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = S[size_t(cb + j) * D + lrow];
+      tmem_st32(lane_addr + CS + cb, v);
+    }
+  }
+  const float inv_sqrt_d = rsqrtf(float(D));
+  // 16-byte staging loads need 16-byte-aligned rows (channel offsets are multiples of 128)
+  const bool vec_ok = (a.proj_stride % 8) == 0 && (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0;
+
+  for (int c = c0; c < c1; ++c) {
+    const int n = a.chunk_n[c], t0 = a.chunk_t0[c];
+    // phase clock of the second chunk of CTA (0, 0) (test hook): dbg[90112 + k] = ns since its start
+    const bool clk = a.dbg != nullptr && h == 0 && s == 0 && c == c0 + 1 && tid == 0;
+    const uint64_t clk0 = clk ? globaltimer_ns() : 0;
+    auto stamp = [&](int k) {
+      if (clk) a.dbg[90112 + k] = float(globaltimer_ns() - clk0);
+    };
+    // ---------------------------------------------------------------- P0: conv, norms, decay
+    // Raw inputs of rows t0-3 .. t0+n-1 for this head's 384 channels ([q | k | v], bf16) are
+    // staged in the W / T tile space (free until M2) with every load in flight at once; the
+    // first chunk's three history rows come from the conv-state pool.
+    {
+      __nv_bfloat16* raw = reinterpret_cast<__nv_bfloat16*>(wt);  // [n + 3][384], row i = token t0 - 3 + i
+      const int nrows = n + KW - 1;
+      auto chan = [&](int j) {  // staged column j -> projection channel
+        return j < 128 ? hk * D + j : j < 256 ? kd + hk * D + (j - 128) : 2 * kd + h * D + (j - 256);
+      };
+      if (vec_ok) {
+        constexpr int PER = 384 / 8;
+        constexpr int UN = 14;  // ceil(67 * 48 / 256)
+        uint4 buf[UN];
+#pragma unroll
+        for (int u = 0; u < UN; ++u) {
+          const int e = tid + u * TC_THREADS, row = e / PER, j = (e % PER) * 8, tok = t0 - (KW - 1) + row;
+          buf[u] = (row < nrows && tok >= seq0)
+                       ? *reinterpret_cast<const uint4*>(a.proj + size_t(tok) * a.proj_stride + chan(j))
+                       : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int u = 0; u < UN; ++u) {  // rows before the sequence start are the history loop's
+          const int e = tid + u * TC_THREADS, row = e / PER, j = (e % PER) * 8;
+          if (row < nrows && t0 - (KW - 1) + row >= seq0) *reinterpret_cast<uint4*>(raw + row * 384 + j) = buf[u];
+        }
+      } else {
+        constexpr int PER = 384 / 2;
+        for (int base = 0; base < nrows * PER; base += 8 * TC_THREADS) {
+          uint32_t buf[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int e = base + tid + u * TC_THREADS, row = e / PER, j = (e % PER) * 2, tok = t0 - (KW - 1) + row;
+            buf[u] = (row < nrows && tok >= seq0)
+                         ? *reinterpret_cast<const uint32_t*>(a.proj + size_t(tok) * a.proj_stride + chan(j))
+                         : 0u;
+          }
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int e = base + tid + u * TC_THREADS, row = e / PER, j = (e % PER) * 2;
+            if (row < nrows && t0 - (KW - 1) + row >= seq0) *reinterpret_cast<uint32_t*>(raw + row * 384 + j) = buf[u];
+          }
+        }
+      }
+      if (t0 - (KW - 1) < seq0) {  // history rows before the sequence start: the conv state
+        for (int e = tid; e < (KW - 1) * 384; e += TC_THREADS) {
+          const int row = e / 384, j = e % 384, tok = t0 - (KW - 1) + row;
+          if (tok < seq0)
+            raw[row * 384 + j] = a.conv[(size_t(slot) * a.C + chan(j)) * (KW - 1) + (KW - 1) - (seq0 - tok)];
+        }
+      }
+      stamp(0);  // staging loads issued and stored
+      __syncthreads();
+      // conv + SiLU: 768 items of (2 adjacent channels, 16 output rows), 3 per thread; the
+      // 4-row window slides in registers (one 32-bit shared load per row)
+#pragma unroll 1
+      for (int item = tid; item < 768; item += TC_THREADS) {
+        const int pair = item % 192, r0 = (item / 192) * 16, j = pair * 2;
+        float w0[KW], w1[KW];
+        {
+          const int ch = chan(j);
+          const uint4 wr = *reinterpret_cast<const uint4*>(a.conv_w + size_t(ch) * KW);  // 2 x 4 taps
+          const __nv_bfloat162* wh = reinterpret_cast<const __nv_bfloat162*>(&wr);
+          const float2 a0 = __bfloat1622float2(wh[0]), a1 = __bfloat1622float2(wh[1]);
+          const float2 b0 = __bfloat1622float2(wh[2]), b1 = __bfloat1622float2(wh[3]);
+          w0[0] = a0.x; w0[1] = a0.y; w0[2] = a1.x; w0[3] = a1.y;
+          w1[0] = b0.x; w1[1] = b0.y; w1[2] = b1.x; w1[3] = b1.y;
+        }
+        auto ld = [&](int row) -> float2 {
+          return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(raw + row * 384 + j));
+        };
+        float2 x0 = ld(r0), x1 = ld(r0 + 1), x2 = ld(r0 + 2);
+#pragma unroll 4
+        for (int i = r0; i < r0 + 16; ++i) {
+          float2 y = make_float2(0.f, 0.f);
+          if (i < n) {
+            const float2 x3 = ld(i + 3);
+            const float u0 = w0[0] * x0.x + w0[1] * x1.x + w0[2] * x2.x + w0[3] * x3.x;
+            const float u1 = w1[0] * x0.y + w1[1] * x1.y + w1[2] * x2.y + w1[3] * x3.y;
+            y = make_float2(__fdividef(u0, 1.f + __expf(-u0)), __fdividef(u1, 1.f + __expf(-u1)));
+            x0 = x1; x1 = x2; x2 = x3;
+          }
+          if (pair < 64) *reinterpret_cast<float2*>(kq + swz(64 + i, j, KQ_SLAB)) = y;            // q
+          else if (pair < 128) *reinterpret_cast<float2*>(kq + swz(i, j - 128, KQ_SLAB)) = y;     // k
+          else *reinterpret_cast<float2*>(vt + swz_mn(i, j - 256)) = y;                            // v
+        }
+      }
+      if (tid < 64) {
+        float b = 0.f, g = 0.f;
+        if (tid < n) {
+          const __nv_bfloat16* row = a.proj + size_t(t0 + tid) * a.proj_stride + a.C + a.Hv * D;
+          b = 1.f / (1.f + __expf(-bf(row[h])));
+          g = -__expf(a.A_log[h]) * softplus_f(bf(row[a.Hv + h]) + a.dt_bias[h]);
+        }
+        beta_s[tid] = b;
+        g_s[tid] = g;
+      }
+    }
+    __syncthreads();
+    stamp(1);  // conv done
+    // L2 norms of the q and k rows (q also scaled by 1/sqrt(D)): lane l holds keys 4l .. 4l+3
+    for (int i = warp; i < 64; i += 8) {
+#pragma unroll
+      for (int which = 0; which < 2; ++which) {
+        const int row = which ? 64 + i : i;
+        float4* p = reinterpret_cast<float4*>(kq + swz(row, lane * 4, KQ_SLAB));
+        float4 x = *p;
+        const float ss = warp_sum(x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w);
+        const float sc = rsqrtf(ss + 1e-6f) * (which ? inv_sqrt_d : 1.f);
+        x.x *= sc; x.y *= sc; x.z *= sc; x.w *= sc;
+        *p = x;
+        if (!which) *reinterpret_cast<float4*>(km + swz_mn(i, lane * 4)) = x;
+      }
+    }
+    if (warp == 0) {  // inclusive prefix sum of g over the 64 rows (2 per lane)
+      const float x0 = g_s[2 * lane], x1 = g_s[2 * lane + 1];
+      float v = x0 + x1;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      const float before = v - (x0 + x1);
+      G_s[2 * lane] = before + x0;
+      G_s[2 * lane + 1] = v;
+      eG_s[2 * lane] = __expf(before + x0);
+      eG_s[2 * lane + 1] = __expf(v);
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    stamp(2);  // norms, decay done
+    // ---------------------------------------------------------------- M1: [K;Q] K^T
+    if (tid == 0 && *s_ok) {
+      tc_fence_after();
+      constexpr uint32_t id = idesc_tf32(128, 64);
+#pragma unroll
+      for (int ks = 0; ks < 16; ++ks) {
+        const uint64_t ad = smem_desc_sw128(kq + (ks >> 2) * KQ_SLAB) + 2 * (ks & 3);
+        mma_tf32_ss(tmem + C1, ad, ad, id, ks > 0 ? 1u : 0u);
+      }
+      commit();
+    }
+    if (!wait_mma(1u << 4)) break;
+    const float Gn = G_s[n - 1];
+    const bool dump = a.dbg != nullptr && h == 0 && s == 0 && c == c0;
+    if (dump) {  // [0, 8192): k.k | q.k rows; [8192, 32768): k, q, v rows
+      float v[32];
+      tmem_ld32(lane_addr + C1 + hf * 32, v);
+      for (int e = 0; e < 32; ++e) a.dbg[lrow * 64 + hf * 32 + e] = v[e];
+      for (int e = tid; e < 128 * 128; e += TC_THREADS)
+        a.dbg[8192 + e] = *reinterpret_cast<const float*>(kq + swz(e >> 7, e & 127, KQ_SLAB));
+      for (int e = tid; e < 64 * 128; e += TC_THREADS)
+        a.dbg[8192 + 16384 + e] = *reinterpret_cast<const float*>(vt + swz_mn(e >> 7, e & 127));
+    }
+    stamp(3);  // M1 complete
+    // ---------------------------------------------------------------- A, P from k.k, q.k
+    {
+      float v[32];
+      tmem_ld32(lane_addr + C1 + hf * 32, v);
+      if (lrow < 64) {
+        const int i = lrow;
+        const float bi = beta_s[i], Gi = G_s[i];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = hf * 32 + e;
+          A_s[i * 64 + (j ^ (i & 31))] = (j < i && i < n) ? bi * __expf(Gi - G_s[j]) * v[e] : 0.f;
+        }
+      } else {
+        const int i = lrow - 64;
+        const float Gi = G_s[i];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = hf * 32 + e;
+          *reinterpret_cast<float*>(pt + swz(i, j, P_SLAB)) = (j <= i && i < n) ? __expf(Gi - G_s[j]) * v[e] : 0.f;
+        }
+      }
+    }
+    __syncthreads();
+    stamp(4);  // A, P written
+    // ---------------------------------------------------------------- T = (I + A)^-1, 16 x 16 blocks
+    if (tid < 64) {  // diagonal blocks: thread = column j, forward substitution down the block
+      const int j = tid, b16 = j & ~15, jj = j & 15;
+      float x[16];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) x[k] = k == jj ? 1.f : 0.f;
+#pragma unroll
+      for (int i = 1; i < 16; ++i) {
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < i; ++k) acc += A_s[(b16 + i) * 64 + ((b16 + k) ^ ((b16 + i) & 31))] * x[k];
+        if (i > jj) x[i] = -acc;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) T_s[(b16 + i) * 64 + j] = x[i];
+    }
+    __syncthreads();
+    for (int d = 1; d < 4; ++d) {  // off-diagonal blocks (I, J = I - d): T_IJ = -T_II sum_K A_IK T_KJ
+      const int nb = 4 - d;
+      for (int e = tid; e < nb * 256; e += TC_THREADS) {
+        const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15, I = d + blk, J = blk;
+        float acc = 0.f;
+        for (int K = J; K < I; ++K)
+#pragma unroll
+          for (int k = 0; k < 16; ++k)
+            acc += A_s[(I * 16 + rr) * 64 + ((K * 16 + k) ^ rr ^ (I & 1) * 16)] * T_s[(K * 16 + k) * 64 + J * 16 + cc];
+        M_s[(blk * 16 + rr) * 17 + cc] = acc;
+      }
+      __syncthreads();
+      for (int e = tid; e < nb * 256; e += TC_THREADS) {
+        const int blk = e >> 8, rr = (e >> 4) & 15, cc = e & 15, I = d + blk, J = blk;
+        float acc = 0.f;
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc += T_s[(I * 16 + rr) * 64 + I * 16 + k] * M_s[(blk * 16 + k) * 17 + cc];
+        T_s[(I * 16 + rr) * 64 + J * 16 + cc] = -acc;
+      }
+      __syncthreads();
+    }
+    stamp(5);  // solve done
+    // Tbe (rows 0-63) and Tb (rows 64-127) of the stacked tile; e^G Q in place of Q
+    for (int e = tid; e < 64 * 64; e += TC_THREADS) {
+      const int i = e >> 6, j = e & 63;
+      const float t = j <= i ? T_s[i * 64 + j] * beta_s[j] : 0.f;
+      *reinterpret_cast<float*>(tt + swz(i, j, TT_SLAB)) = t * eG_s[j];
+      *reinterpret_cast<float*>(tt + swz(64 + i, j, TT_SLAB)) = t;
+    }
+    for (int e = tid; e < 64 * 32; e += TC_THREADS) {
+      const int i = e >> 5, q4 = (e & 31) * 4;
+      float4* p = reinterpret_cast<float4*>(kq + swz(64 + i, q4, KQ_SLAB));
+      float4 x = *p;
+      const float sc = eG_s[i];
+      x.x *= sc; x.y *= sc; x.z *= sc; x.w *= sc;
+      *p = x;
+    }
+    fence_proxy_async_smem();
+    __syncthreads();
+    stamp(6);  // T tiles, e^G Q written
+    // ---------------------------------------------------------------- M2: W = Tbe K
+    if (tid == 0 && *s_ok) {
+      tc_fence_after();
+      constexpr uint32_t id = idesc_tf32(128, 128, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t ad = smem_desc_sw128(tt + (ks >> 2) * TT_SLAB) + 2 * (ks & 3);
+        const uint64_t bd = desc_mn(km + ks * 1024);
+        mma_tf32_ss(tmem + C2, ad, bd, id, ks > 0 ? 1u : 0u);
+      }
+      commit();
+    }
+    if (!wait_mma(1u << 5)) break;
+    if (dump) {  // [32768, 40960): W rows 0-63 of C2; [40960, 49152): T_s
+      float v[32];
+      for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+        tmem_ld32(lane_addr + C2 + cb, v);
+        if (lrow < 64)
+          for (int e = 0; e < 32; ++e) a.dbg[32768 + lrow * 128 + cb + e] = v[e];
+      }
+      for (int e = tid; e < 64 * 64; e += TC_THREADS) a.dbg[40960 + e] = T_s[(e >> 6) * 64 + (e & 63)];
+    }
+    stamp(7);  // M2 complete
+    // W rows (lanes 0-63) into the W tile; K' = e^{G_n - G} K in place of K (MMAs reading K are done)
+    if (lrow < 64) {
+      float v[32];
+#pragma unroll 1
+      for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+        tmem_ld32(lane_addr + C2 + cb, v);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)
+          *reinterpret_cast<float4*>(wt + swz(lrow, cb + e, W_SLAB)) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      }
+    }
+    for (int e = tid; e < 64 * 32; e += TC_THREADS) {
+      const int i = e >> 5, q4 = (e & 31) * 4;
+      float4* p = reinterpret_cast<float4*>(km + swz_mn(i, q4));
+      float4 x = *p;
+      const float sc = i < n ? __expf(Gn - G_s[i]) : 0.f;
+      x.x *= sc; x.y *= sc; x.z *= sc; x.w *= sc;
+      *p = x;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    stamp(8);  // W tile, K' written
+    // ---------------------------------------------------------------- M3-M5: D^T, O^T (S part)
+    if (tid == 0 && *s_ok) {
+      tc_fence_after();
+      constexpr uint32_t idU = idesc_tf32(128, 64, true, false);
+      constexpr uint32_t idW = idesc_tf32(128, 64, false, false, true);
+      constexpr uint32_t idO = idesc_tf32(128, 64);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {  // U^T = V^T Tb^T
+        const uint64_t ad = desc_mn(vt + ks * 1024);
+        const uint64_t bd = smem_desc_sw128(tt + (ks >> 2) * TT_SLAB + 64 * 128) + 2 * (ks & 3);
+        mma_tf32_ss(tmem + C3, ad, bd, idU, ks > 0 ? 1u : 0u);
+      }
+#pragma unroll
+      for (int ks = 0; ks < 16; ++ks) {  // D^T -= S^T W^T ; O^T = S^T (e^G Q)^T
+        const uint64_t bw = smem_desc_sw128(wt + (ks >> 2) * W_SLAB) + 2 * (ks & 3);
+        const uint64_t bq = smem_desc_sw128(kq + (ks >> 2) * KQ_SLAB + 64 * 128) + 2 * (ks & 3);
+        mma_tf32_ts(tmem + C3, tmem + CS + ks * 8, bw, idW, 1u);
+        mma_tf32_ts(tmem + C4, tmem + CS + ks * 8, bq, idO, ks > 0 ? 1u : 0u);
+      }
+      commit();
+    }
+    if (!wait_mma(1u << 6)) break;
+    if (dump) {  // [49152, 57344): D^T; [57344, 65536): O^T (S part)
+      float v[32];
+      tmem_ld32(lane_addr + C3 + hf * 32, v);
+      for (int e = 0; e < 32; ++e) a.dbg[49152 + lrow * 64 + hf * 32 + e] = v[e];
+      tmem_ld32(lane_addr + C4 + hf * 32, v);
+      for (int e = 0; e < 32; ++e) a.dbg[57344 + lrow * 64 + hf * 32 + e] = v[e];
+    }
+    stamp(9);  // M3-M5 complete
+    // S^T *= e^{G_n}
+    {
+      const float gam = __expf(Gn);
+      float v[32];
+#pragma unroll 1
+      for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+        tmem_ld32(lane_addr + CS + cb, v);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) v[e] *= gam;
+        tmem_st32(lane_addr + CS + cb, v);
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+    stamp(10);  // S^T scaled
+    // ---------------------------------------------------------------- M6, M7
+    if (tid == 0 && *s_ok) {
+      tc_fence_after();
+      constexpr uint32_t idP = idesc_tf32(128, 64);
+      constexpr uint32_t idS = idesc_tf32(128, 128, false, true);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint64_t bp = smem_desc_sw128(pt + (ks >> 2) * P_SLAB) + 2 * (ks & 3);
+        const uint64_t bk = desc_mn(km + ks * 1024);
+        mma_tf32_ts(tmem + C4, tmem + C3 + ks * 8, bp, idP, 1u);
+        mma_tf32_ts(tmem + CS, tmem + C3 + ks * 8, bk, idS, 1u);
+      }
+      commit();
+    }
+    if (!wait_mma(1u << 7)) break;
+    if (dump) {  // [65536, 73728): O^T; [73728, 90112): S^T
+      float v[32];
+      tmem_ld32(lane_addr + C4 + hf * 32, v);
+      for (int e = 0; e < 32; ++e) a.dbg[65536 + lrow * 64 + hf * 32 + e] = v[e];
+      for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+        tmem_ld32(lane_addr + CS + cb, v);
+        for (int e = 0; e < 32; ++e) a.dbg[73728 + lrow * 128 + cb + e] = v[e];
+      }
+    }
+    stamp(11);  // M6, M7 complete
+    // ---------------------------------------------------------------- O^T out (pre-norm, fp32)
+    {
+      float v[32];
+      tmem_ld32(lane_addr + C4 + hf * 32, v);
+      const int val = lrow;
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const int i = hf * 32 + e;
+        if (i < n) a.o32[(size_t(t0 + i) * a.Hv + h) * D + val] = v[e];
+      }
+    }
+    stamp(12);  // O written (thread 0's share)
+    tc_fence_before();
+    __syncthreads();  // the next chunk overwrites the tiles and TMEM columns read above
+  }
+  // ---- state out
+  if (*s_ok) {
+    float v[32];
+    for (int cb = hf * 64; cb < hf * 64 + 64; cb += 32) {
+      tmem_ld32(lane_addr + CS + cb, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) S[size_t(cb + j) * D + lrow] = v[j];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc(tmem, TC_TMEM_COLS);
+}
+
+// New conv windows after a chunked prefill: per sequence, the last KW-1 raw inputs of every
+// channel (older window entries where the sequence is shorter).  A kernel of its own because the
+// q / k channels of a key head are read by every value head that shares it.
+__global__ void __launch_bounds__(256) gdn_chunk_conv_commit_kernel(ChunkArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  const int s = blockIdx.x;
+  const int seq0 = a.cu_seqlens[s], L = a.cu_seqlens[s + 1] - seq0, slot = a.slots[s];
+  if (L <= 0) return;
+  for (int ch = blockIdx.y * blockDim.x + threadIdx.x; ch < a.C; ch += gridDim.y * blockDim.x) {
+    __nv_bfloat16* cw = a.conv + (size_t(slot) * a.C + ch) * (KW - 1);
+    __nv_bfloat16 nv[KW - 1];
+#pragma unroll
+    for (int i = 0; i < KW - 1; ++i) {
+      const int pos = L - (KW - 1) + i;
+      nv[i] = pos >= 0 ? a.proj[size_t(seq0 + pos) * a.proj_stride + ch] : cw[(KW - 1) + pos];
+    }
+#pragma unroll
+    for (int i = 0; i < KW - 1; ++i) cw[i] = nv[i];
+  }
+}
+
 // One warp per (token, value head): bf16-rounded output, gated RMSNorm.
 __global__ void __launch_bounds__(256) gdn_chunk_norm_kernel(ChunkArgs a) {
   pdl_trigger();
@@ -391,6 +967,18 @@ __global__ void __launch_bounds__(256) gdn_chunk_norm_kernel(ChunkArgs a) {
 }
 
 }  // namespace
+
+int64_t gdn_error_word_address();
+
+// Test hook: a non-empty fp32 buffer of >= 90128 floats receives the intermediates of the first
+// chunk of CTA (value head 0, sequence 0) of the following tensor-core launches and the phase
+// clock of its second chunk; empty clears it.
+static float* g_chunk_dbg = nullptr;
+void gdn_chunk_debug(const at::Tensor& buf) {
+  TORCH_CHECK(buf.numel() == 0 || (buf.is_cuda() && buf.scalar_type() == at::kFloat && buf.numel() >= 90128),
+              "debug buffer: fp32 CUDA tensor of >= 90128 floats, or empty");
+  g_chunk_dbg = buf.numel() ? buf.data_ptr<float>() : nullptr;
+}
 
 // chunk_info = [chunk_seq (nc) | chunk_t0 (nc) | chunk_n (nc) | cu_chunks (B+1)] int32 on the device.
 at::Tensor gdn_prefill_chunked(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
@@ -434,6 +1022,8 @@ at::Tensor gdn_prefill_chunked(const at::Tensor& proj, const at::Tensor& cu_seql
   a.C = C;
   a.T = T;
   a.eps = float(eps);
+  a.err = reinterpret_cast<unsigned int*>(gdn_error_word_address());
+  a.dbg = g_chunk_dbg;
   auto st = at::cuda::getCurrentCUDAStream();
   const int prep_smem = kPrepSmemFloats * 4, state_smem = kStateSmemFloats * 4;
   static bool attr = false;
@@ -444,8 +1034,23 @@ at::Tensor gdn_prefill_chunked(const at::Tensor& proj, const at::Tensor& cu_seql
                                      state_smem) == cudaSuccess, "chunk state smem attribute");
     attr = true;
   }
-  launch_pdl(gdn_chunk_prep_kernel, dim3(int(nc), int(hv)), dim3(256), prep_smem, st, a);
-  launch_pdl(gdn_chunk_state_kernel, dim3(D / SLICE, int(hv), B), dim3(256), state_smem, st, a);
+  static const bool use_tc = [] {
+    const char* e = std::getenv("ISB_GDN_CHUNK_TC");
+    return !(e && e[0] == '0');
+  }();
+  if (use_tc) {
+    static bool tc_attr = false;
+    if (!tc_attr) {
+      TORCH_CHECK(cudaFuncSetAttribute(gdn_chunk_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM) ==
+                      cudaSuccess, "chunk tc smem attribute");
+      tc_attr = true;
+    }
+    launch_pdl(gdn_chunk_tc_kernel, dim3(int(hv), B), dim3(TC_THREADS), TC_SMEM, st, a);
+    launch_pdl(gdn_chunk_conv_commit_kernel, dim3(B, (C + 255) / 256), dim3(256), 0, st, a);
+  } else {
+    launch_pdl(gdn_chunk_prep_kernel, dim3(int(nc), int(hv)), dim3(256), prep_smem, st, a);
+    launch_pdl(gdn_chunk_state_kernel, dim3(D / SLICE, int(hv), B), dim3(256), state_smem, st, a);
+  }
   launch_pdl(gdn_chunk_norm_kernel, dim3((T * int(hv) + 7) / 8), dim3(256), 0, st, a);
   return out;
 }

@@ -25,6 +25,7 @@ at::Tensor embed(const at::Tensor& ids, const at::Tensor& table, int64_t vocab_s
 at::Tensor gdn_decode(const at::Tensor& proj, const at::Tensor& slots, const at::Tensor& conv_w, const at::Tensor& A_log,
                       const at::Tensor& dt_bias, const at::Tensor& norm_w, at::Tensor rec, at::Tensor conv, int64_t hk,
                       int64_t hv, int64_t dk, int64_t dv, double eps);
+void gdn_chunk_debug(const at::Tensor& buf);
 at::Tensor gdn_prefill_chunked(const at::Tensor& proj, const at::Tensor& cu_seqlens, const at::Tensor& slots,
                                const at::Tensor& chunk_info, int64_t nc, const at::Tensor& conv_w,
                                const at::Tensor& A_log, const at::Tensor& dt_bias, const at::Tensor& norm_w,
@@ -162,6 +163,7 @@ TORCH_LIBRARY(isb, m) {
   m.def("comm_set_wait_timeout(int ns) -> ()");
   m.def("step_status(Tensor toks, Tensor words) -> Tensor");
   m.def("error_word_addresses() -> Tensor");
+  m.def("gdn_chunk_debug(Tensor buf) -> ()");
   m.def("symm_alloc(int nbytes) -> (Tensor, Tensor)");
   m.def("symm_open(Tensor handle) -> int");
   m.def("symm_close(int ptr) -> ()");
@@ -202,6 +204,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
 }
 
 TORCH_LIBRARY_IMPL(isb, CompositeExplicitAutograd, m) {
+  m.impl("gdn_chunk_debug", &isb::gdn_chunk_debug);
   m.impl("error_word", &isb::error_word);
   m.impl("symm_alloc", &isb::symm_alloc);
   m.impl("symm_open", &isb::symm_open);

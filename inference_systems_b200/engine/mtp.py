@@ -386,7 +386,7 @@ class MTPDriver:
             r.check_status(host)
             t = b * (k + 1)
             vals = host[:t].view(b, k + 1).tolist()
-            accs = host[t:].tolist()
+            accs = host[t:t + b].tolist()  # the step's status word follows the accepted counts
         r.sample_step += 1
         out = [row[: a + 1] for row, a in zip(vals, accs)]
         self.rounds += 1

@@ -150,15 +150,16 @@ def gdn_chunk_table(batch: ForwardBatch) -> tuple[torch.Tensor, int]:
 
 
 _SMS: int | None = None
+_CHUNK_US = 10.0  # one 64-token chunk of the tensor-core chunked GDN prefill (B200)
 
 
 def _chunked_is_faster(batch: ForwardBatch, hv: int) -> bool:
     """Pick the chunked prefill or the token scan for this batch from a cost model fitted on B200.
 
     Token scan: one CTA per (value head, sequence), two per SM, about 2.9 us per
-    token step, so waves x longest length.  Chunked: the chunk-parallel prep
-    kernel (one CTA per chunk and head, ~100 us, one per SM) plus the state
-    kernel (4 CTAs per head and sequence, ~21 us per chunk, one per SM).
+    token step, so waves x longest length.  Chunked (tensor-core form): one CTA per
+    (value head, sequence), one per SM, about ``_CHUNK_US`` per 64-token chunk in
+    order, plus a fixed cost for the conv-window and norm kernels.
     """
     global _SMS
     if _SMS is None:
@@ -169,10 +170,9 @@ def _chunked_is_faster(batch: ForwardBatch, hv: int) -> bool:
     lmax = max(lens, default=0)
     if lmax < 2:
         return False
-    nc = sum((n + GDN_CHUNK - 1) // GDN_CHUNK for n in lens)
     ceil = lambda x, y: -(-x // y)  # noqa: E731
     scan = ceil(b * hv, 2 * _SMS) * lmax * 2.9
-    chunked = ceil(nc * hv, _SMS) * 100.0 + ceil(4 * hv * b, _SMS) * ceil(lmax, GDN_CHUNK) * 21.0
+    chunked = ceil(hv * b, _SMS) * ceil(lmax, GDN_CHUNK) * _CHUNK_US + 10.0
     return chunked < scan
 
 
