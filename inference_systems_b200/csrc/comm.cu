@@ -97,7 +97,9 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
   pdl_wait();
   __shared__ int s_ok;
   __shared__ float red[16];
+  __shared__ unsigned long long s_x[kMaxWorld];  // activation buffers, read once
   const int tid = threadIdx.x, nt = blockDim.x;
+  if (tid < world) s_x[tid] = xdst[tid];
   // targets of this exchange; the previous exchange's last CTA wrote the bases before its grid
   // completed (ordered by pdl_wait), and this exchange's last CTA moves them only after every CTA
   // has read them
@@ -157,13 +159,13 @@ __global__ void __launch_bounds__(512) tp_norm_ag_kernel(
 #pragma unroll
       for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
       if (one_shot_rank >= 0) {  // one-shot: every rank normalises every row itself
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xdst[one_shot_rank]) + r * H + c) = out;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(s_x[one_shot_rank]) + r * H + c) = out;
         continue;
       }
       // the all-gather: the row goes to every rank's activation buffer (staggered start)
       for (int q = 0; q < world; ++q) {
         const int dst = (i + q) % world;
-        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(xdst[dst]) + r * H + c) = out;
+        *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(s_x[dst]) + r * H + c) = out;
       }
     }
   }

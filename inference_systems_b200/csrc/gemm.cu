@@ -93,6 +93,8 @@ struct GemmArgs {
   __nv_bfloat16* norm_res;
   const __nv_bfloat16* norm_w;
   float norm_eps;
+  bool acc_direct;         // swap-AB kRedAdd: add straight from TMEM registers (no shared staging)
+  int epi_probe;           // diagnostics of the direct path: 1 = TMEM loads only, 2 = stores only
   int norm_rows;           // token rows of the accumulator
   bool norm_zc;
 };
@@ -104,14 +106,16 @@ constexpr int kCounterSlots = 8;
 constexpr int kCountersPerSlot = 8192;
 __device__ unsigned int g_splitk_counters[kCounterSlots * kCountersPerSlot];
 
+// Fire-and-forget reductions carry no "memory" clobber: a clobber would make the compiler reload
+// every kernel argument from memory after each one (measured: a 128 x 128 fp32 tile took 6 us to
+// leave the CTA instead of 1).  Readers of the reduced values are ordered by fences and barriers,
+// which do clobber memory.
 ISB_DEVICE void red_add_v4(float* p, float a, float b, float c, float d) {
-  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+  asm volatile("red.relaxed.gpu.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 
 ISB_DEVICE void red_add_v4_sys(float* p, float a, float b, float c, float d) {
-  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
+  asm volatile("red.relaxed.sys.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d));
 }
 
 // Add 4 consecutive values at element offset ``off`` of the accumulator.
@@ -158,6 +162,25 @@ ISB_DEVICE void rs_emit4(const GemmArgs& args, bool staged, int tok, int f, floa
   else rs_push4(args, tok, f, a, b, c, d);
 }
 
+// Push 4 features of token ``tok`` (bf16) into the owner rank's slot for this rank, or (one-shot)
+// into every rank's slot; ``dst`` is the destination table (own slot first), the scalars are the
+// kernel arguments hoisted out of the caller's loop.
+ISB_DEVICE void push_rs4(const unsigned long long* dst, bool bcast, int ndst, int rk, int slot_rows, int own_rows,
+                         size_t ldo, int tok, int f, float4 w) {
+  uint2 raw;
+  __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+  hh[0] = __floats2bfloat162_rn(w.x, w.y);
+  hh[1] = __floats2bfloat162_rn(w.z, w.w);
+  if (bcast) {
+    const size_t off = (size_t(rk) * slot_rows + tok) * ldo + f;
+    for (int q = 0; q < ndst; ++q) *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(dst[q]) + off) = raw;
+  } else {
+    const int owner = tok / own_rows;
+    const size_t off = (size_t(rk) * slot_rows + (tok - owner * own_rows)) * ldo + f;
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(dst[(owner - rk + ndst) % ndst]) + off) = raw;
+  }
+}
+
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
   h ^= h >> 16;
   h *= 0x85EBCA6Bu;
@@ -178,7 +201,7 @@ ISB_DEVICE float gumbel_noise(int seed, int step, int row, int col) {
 
 // Tail of an accumulating GEMM that also applies the residual add + RMSNorm (128 epilogue threads
 // of every CTA): a bounded grid barrier, then rows round-robin over the CTAs.
-__device__ __noinline__ void fused_add_norm(const GemmArgs& args) {
+__device__ __forceinline__ void fused_add_norm(const GemmArgs& args) {
   __shared__ float red[4];
   const int tid = threadIdx.x - 64;
   const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
@@ -275,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_mbar_init();
     prefetch_tmap(&tmP);
     prefetch_tmap(&tmQ);
-    if constexpr (SWAP && (EPI == kStore || EPI == kSiluMul)) prefetch_tmap(&tmO);
+    if constexpr (SWAP && (EPI == kStore || EPI == kSiluMul || EPI == kRedAdd || EPI == kRsPush)) prefetch_tmap(&tmO);
   }
   if (warp == 1) tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
   tc_fence_before();
@@ -355,7 +378,64 @@ __global__ void __launch_bounds__(kThreads, 1)
   __nv_bfloat16* ostage = reinterpret_cast<__nv_bfloat16*>(smem + XBUF_BYTES);  // [BN][128] bf16
   __shared__ int s_last;
 
-  if constexpr (CL) {
+  if constexpr (CL && EPI == kRsPush) {
+    // ---- split-K in ONE cluster per weight tile (cluster dims (1, 1, splits), <= 8): every CTA
+    // parks its fp32 partial [tokens][features] in its own shared memory; after the cluster
+    // barrier CTA r sums token rows r, r + splits, ... over the cluster (DSMEM loads) and pushes
+    // them (bf16) to the owner's slot, or to every rank's slot in one-shot mode.  No staging
+    // round trip through L2, no tile counter, and every CTA of the tile pushes a share.  The
+    // partials stay alive until the second cluster barrier.
+    static_assert(SWAP, "cluster reduce-scatter serves swap-AB tiles");
+    float* fstage = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 (token-major)
+    __shared__ unsigned long long s_dst[8];
+    const int tid = threadIdx.x - 64;
+    if (epi) {
+      pdl_wait();  // the slots and counters may still be in use by the previous kernel
+      const bool acc_ok = mbar_wait(acc_full, 0) && nkb > 0;
+      if (!acc_ok && nkb > 0) atomicOr(&g_gemm_err, 8u);
+      tc_fence_after();
+#pragma unroll 1
+      for (int c = 0; c < BN / CH; ++c) {
+        float v[CH];
+        if (acc_ok) {
+          if constexpr (CH == 16) tmem_ld16(lane_addr + c * CH, v); else tmem_ld32(lane_addr + c * CH, v);
+        } else {
+#pragma unroll
+          for (int j = 0; j < CH; ++j) v[j] = 0.f;
+        }
+#pragma unroll
+        for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
+      }
+      if (tid < args.ndst) s_dst[tid] = args.dsts[(args.rank + tid) % args.ndst];
+    }
+    __syncwarp();  // .aligned cluster barrier: the warp reconverges first (lane 0 ran the pipeline)
+    cluster_sync();
+    if (epi) {
+      const uint32_t me = cluster_ctarank(), ns = cluster_nctarank();
+      const int q0 = tile_q * BN, p0 = tile_p * BM;
+      const int ntok = min(BN, args.Q_rows - q0);
+      const int mine = ntok > int(me) ? (ntok - int(me) + int(ns) - 1) / int(ns) : 0;  // rows of this CTA
+      const bool bcast = args.bcast;
+      const int ndst = args.ndst, rk = args.rank, slot_rows = args.slot_rows, own_rows = args.own_rows;
+      const size_t ldo = size_t(args.ldo);
+      const uint32_t base = smem_u32(fstage);
+      for (int i = tid; i < mine * (BM / 4); i += 128) {
+        const int t = int(me) + (i / (BM / 4)) * int(ns), f4 = (i % (BM / 4)) * 4;
+        const uint32_t off = uint32_t((t * BM + f4) * 4);
+        float4 acc4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int z = 0; z < 8; ++z) {
+          if (z < int(ns)) {
+            const float4 x = ld_dsmem_f4(mapa_shared(base + off, uint32_t(z)));
+            acc4.x += x.x; acc4.y += x.y; acc4.z += x.z; acc4.w += x.w;
+          }
+        }
+        push_rs4(s_dst, bcast, ndst, rk, slot_rows, own_rows, ldo, q0 + t, p0 + f4, acc4);
+      }
+    }
+    __syncwarp();  // .aligned cluster barrier: the warp reconverges first (lane 0 ran the pipeline)
+    cluster_sync();  // the peers have finished reading this CTA's partial
+  } else if constexpr (CL) {
     // ---- split-K pair in a 2-CTA cluster (swap-AB store / SiLU*mul): each CTA of the pair
     // multiplied half of K; both park their fp32 partial rows in their own shared memory, then
     // CTA r sums its own and its peer's partials (DSMEM loads) for token columns
@@ -387,6 +467,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           *reinterpret_cast<float4*>(pbuf + row * PSTR + c * CH + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
     }
+    __syncwarp();  // .aligned cluster barrier: the warp reconverges first (lane 0 ran the pipeline)
     cluster_sync();
     if (epi) {
       const uint32_t me = cluster_ctarank();
@@ -427,6 +508,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
       }
     }
+    __syncwarp();  // .aligned cluster barrier: the warp reconverges first (lane 0 ran the pipeline)
     cluster_sync();  // the peer has finished reading this CTA's partials
   }
   if (epi && !CL) {
@@ -437,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (dbg && threadIdx.x == 64) dbg[5] = globaltimer_ns();
 
     auto load_chunk = [&](int c, float* v) {
-      if (!acc_ok) {
+      if (!acc_ok || args.epi_probe == 2) {
 #pragma unroll
         for (int j = 0; j < CH; ++j) v[j] = 0.f;
         return;
@@ -560,9 +642,41 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if constexpr (EPI == kRedAdd) {
           if constexpr (SWAP) {
-            float* fstage = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 (token-major)
+            if (args.acc_direct) {
+              // thread = feature row, v[j] = token c*CH + j: a warp adds 32 consecutive features
+              const int f = p0 + row;
+              if (args.epi_probe == 1) {
+                float sink = 0.f;
 #pragma unroll
-            for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
+                for (int j = 0; j < CH; ++j) sink += v[j];
+                if (sink == 123.456f) args.acc[0] = sink;  // keeps the loads
+              } else if (f < args.P_rows) {
+                // conditions hoisted out of the store loop: full chunks store unpredicated
+                const size_t ldo = size_t(args.ldo);
+                float* dst = args.acc + size_t(q0 + c * CH) * ldo + f;
+                const int nj = min(CH, args.Q_rows - (q0 + c * CH));
+                const int reps = args.epi_probe == 3 ? 17 : 1;  // diagnostics: repeated stores
+                for (int rr = 0; rr < reps; ++rr) {
+                  if (args.acc_plain && nj == CH) {
+#pragma unroll
+                    for (int j = 0; j < CH; ++j) dst[j * ldo] = v[j];
+                  } else if (nj == CH) {
+#pragma unroll
+                    for (int j = 0; j < CH; ++j)
+                      asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(dst + j * ldo), "f"(v[j]));
+                  } else {
+                    for (int j = 0; j < nj; ++j) {
+                      if (args.acc_plain) dst[j * ldo] = v[j];
+                      else asm volatile("red.relaxed.gpu.global.add.f32 [%0], %1;" ::"l"(dst + j * ldo), "f"(v[j]));
+                    }
+                  }
+                }
+              }
+            } else {
+              float* fstage = reinterpret_cast<float*>(smem);  // [BN][BM] fp32 (token-major)
+#pragma unroll
+              for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
+            }
           } else {
             const int t = p0 + row;
             const int col0 = q0 + c * CH;
@@ -640,37 +754,81 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // swap-AB accumulation: 4 consecutive features per vector atomic from the staged tile
-      if constexpr (SWAP && EPI == kRedAdd) {
+      // swap-AB accumulation: the staged [tokens][features] fp32 tile leaves in ONE bulk tensor
+      // reduce-add (a plain bulk store when this CTA is the tile's only producer); the copy
+      // engine clips token rows past the accumulator's extent
+      if (SWAP && EPI == kRedAdd && !args.acc_direct) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        const float* fstage = reinterpret_cast<const float*>(smem);
-        const int tid = threadIdx.x - 64;
-        const bool vec_ok = (args.ldo % 4) == 0;
-        for (int i = tid; i < BN * (BM / 4); i += 128) {
-          const int t = i / (BM / 4), f4 = (i % (BM / 4)) * 4;
-          const int tok = q0 + t, f = p0 + f4;
-          if (tok >= args.Q_rows || f >= args.P_rows) continue;
-          const float4 w = *reinterpret_cast<const float4*>(fstage + t * BM + f4);
-          const size_t off = size_t(tok) * args.ldo + f;
-          if (vec_ok && f + 3 < args.P_rows) {
-            acc_add4(args, off, w.x, w.y, w.z, w.w);
+        if (threadIdx.x == 64) {
+          const uint64_t map = reinterpret_cast<uint64_t>(&tmO);
+          if (args.acc_plain)
+            asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+                         "r"(p0), "r"(q0), "r"(smem_u32(smem))
+                         : "memory");
+          else
+            asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map),
+                         "r"(p0), "r"(q0), "r"(smem_u32(smem))
+                         : "memory");
+          asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          // the fused norm tail reads the sums in this kernel: wait for the writes themselves
+          // and order them (async proxy) before this CTA's generic release; otherwise only the
+          // shared-memory source must stay intact until the copy has read it
+          if (args.norm_out != nullptr) {
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+            asm volatile("fence.proxy.async.global;" ::: "memory");
           } else {
-            const float e[4] = {w.x, w.y, w.z, w.w};
-            for (int k = 0; k < 4 && f + k < args.P_rows; ++k) acc_add1(args, off + k, e[k]);
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
           }
         }
       }
       if constexpr (EPI == kRsPush) {
         const int tid = threadIdx.x - 64;
-        if constexpr (SWAP) {  // 4 consecutive features of one token per step from the staged tile
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+        // Destination table in shared memory (own slot first, then the peers in turn), read once;
+        // every loop below stores without per-element branches on kernel arguments (a branch per
+        // store cut this epilogue's store rate by a factor of five).
+        __shared__ unsigned long long s_dst[8];
+        const int ndst = args.ndst, rk = args.rank;
+        const bool bcast = args.bcast;
+        const size_t ldo = size_t(args.ldo);
+        if (tid < ndst) s_dst[tid] = args.dsts[(rk + tid) % ndst];
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        auto push4 = [&](int tok, int f, float4 w) {
+          uint2 raw;
+          __nv_bfloat162* hh = reinterpret_cast<__nv_bfloat162*>(&raw);
+          hh[0] = __floats2bfloat162_rn(w.x, w.y);
+          hh[1] = __floats2bfloat162_rn(w.z, w.w);
+          if (bcast) {
+            const size_t off = (size_t(rk) * args.slot_rows + tok) * ldo + f;
+            for (int q = 0; q < ndst; ++q) *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(s_dst[q]) + off) = raw;
+          } else {
+            const int owner = tok / args.own_rows;
+            const size_t off = (size_t(rk) * args.slot_rows + (tok - owner * args.own_rows)) * ldo + f;
+            *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(s_dst[(owner - rk + ndst) % ndst]) + off) = raw;
+          }
+        };
+        if constexpr (SWAP) {
           const float* fstage = reinterpret_cast<const float*>(smem);
-          for (int i = tid; i < BN * (BM / 4); i += 128) {
-            const int t = i / (BM / 4), f4 = (i % (BM / 4)) * 4;
-            const int tok = q0 + t, f = p0 + f4;
-            if (tok >= args.Q_rows || f >= args.P_rows) continue;
-            const float4 w = *reinterpret_cast<const float4*>(fstage + t * BM + f4);
-            rs_emit4(args, nsplit > 1, tok, f, w.x, w.y, w.z, w.w);
+          const int ntok = min(BN, args.Q_rows - q0);  // feature rows are whole tiles (N % 128 == 0)
+          if (nsplit > 1) {
+            // split-K partials meet in the local fp32 staging rows through one bulk tensor
+            // reduce-add per CTA (the copy engine clips rows past the tokens)
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (threadIdx.x == 64) {
+              asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+                           ::"l"(reinterpret_cast<uint64_t>(&tmO)), "r"(p0), "r"(q0), "r"(smem_u32(smem))
+                           : "memory");
+              asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+              asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+          } else {
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the staged tile is complete
+            for (int i = tid; i < ntok * (BM / 4); i += 128) {
+              const int t = i / (BM / 4), f4 = (i % (BM / 4)) * 4;
+              push4(q0 + t, p0 + f4, *reinterpret_cast<const float4*>(fstage + t * BM + f4));
+            }
           }
         }
         if (nsplit > 1) {
@@ -689,28 +847,26 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tok0 = SWAP ? q0 : p0, ntok = SWAP ? BN : BM;
             const int f0 = SWAP ? p0 : q0, nf = SWAP ? BM : BN;
             const int T = SWAP ? args.Q_rows : args.P_rows, F = SWAP ? args.P_rows : args.Q_rows;
-            // 8 independent L2 reads in flight per thread before any store: a store to the
-            // staging rows or to a slot could alias the next read, so one read per iteration
-            // would pay a full L2 round trip each (32 of them per thread for a 128 x 128 tile)
+            // 8 independent L2 reads in flight per thread before any store
             constexpr int UN = 8;
-            const int total = ntok * (nf / 4);
+            const int total = min(ntok, T - tok0) * (nf / 4);
             for (int base = tid; base < total; base += 128 * UN) {
               float4 w[UN];
-              float* ap[UN];
 #pragma unroll
               for (int u = 0; u < UN; ++u) {
-                const int i = base + u * 128;
+                const int i = min(base + u * 128, total - 1);
                 const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
-                ap[u] = (i < total && tok < T && f < F) ? args.acc + size_t(tok) * args.ldo + f : nullptr;
-                if (ap[u]) w[u] = __ldcg(reinterpret_cast<const float4*>(ap[u]));
+                w[u] = f < F ? __ldcg(reinterpret_cast<const float4*>(args.acc + size_t(tok) * ldo + f))
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
               }
 #pragma unroll
               for (int u = 0; u < UN; ++u) {
-                if (!ap[u]) continue;
                 const int i = base + u * 128;
+                if (i >= total) break;
                 const int tok = tok0 + i / (nf / 4), f = f0 + (i % (nf / 4)) * 4;
-                *reinterpret_cast<float4*>(ap[u]) = make_float4(0.f, 0.f, 0.f, 0.f);
-                rs_push4(args, tok, f, w[u].x, w[u].y, w[u].z, w[u].w);
+                if (f >= F) continue;
+                *reinterpret_cast<float4*>(args.acc + size_t(tok) * ldo + f) = make_float4(0.f, 0.f, 0.f, 0.f);
+                push4(tok, f, w[u]);
               }
             }
           }
@@ -1060,6 +1216,23 @@ static void launch_gemm_pair(const CUtensorMap& tp, const CUtensorMap& tq, const
   TORCH_CHECK(e == cudaSuccess, "gemm (cluster pair) launch failed: ", cudaGetErrorString(e));
 }
 
+// Reduce-scatter GEMM with the K splits of each weight tile in one thread-block cluster.
+template <int BN>
+static void launch_rs_cluster(const CUtensorMap& tp, const CUtensorMap& tq, GemmArgs a, int tiles_p, int tiles_q,
+                              int splits, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, true, kRsPush, true>;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM) == cudaSuccess);
+    attr = true;
+  }
+  launch_pdl_cluster(kern, dim3(tiles_p, tiles_q, splits), dim3(kThreads), Cfg::SMEM, stream, dim3(1, 1, splits), tp, tq,
+                     tp, a);
+  const cudaError_t e = cudaGetLastError();
+  TORCH_CHECK(e == cudaSuccess, "gemm (reduce-scatter cluster) launch failed: ", cudaGetErrorString(e));
+}
+
 static bool gemm_pair_enabled() {
   static const bool on = [] {
     const char* e = std::getenv("ISB_GEMM_PAIR");
@@ -1094,6 +1267,21 @@ static CUtensorMap make_store_map(const void* ptr, int64_t rows, int64_t cols, i
                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
                            CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (store) failed: ", int(r));
+  return m;
+}
+
+// 2-D fp32 row-major accumulator map for the swap-AB TMA reduce-add: dims {cols, rows}, box
+// {box_cols, box_rows}; rows past ``rows`` are clipped by the copy.
+static CUtensorMap make_acc_map(const void* ptr, int64_t rows, int64_t cols, int box_cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * 4};
+  cuuint32_t box[2] = {cuuint32_t(box_cols), cuuint32_t(box_rows)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                           CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (accumulator) failed: ", int(r));
   return m;
 }
 
@@ -1290,7 +1478,13 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
   args.acc_plain = p.splits == 1;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  if (p.swap) {
+    // the bulk reduce-add needs 16-byte rows; other widths add from registers
+    const bool bulk = N % 4 == 0 && (reinterpret_cast<uintptr_t>(acc.data_ptr()) & 15) == 0;
+    if (!bulk) args.acc_direct = true;
+    const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
+    dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
 }
 
@@ -1341,7 +1535,13 @@ at::Tensor gemm_accum_norm(const at::Tensor& a_in, const at::Tensor& b, at::Tens
   args.norm_rows = M;
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (p.swap) dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  if (p.swap) {
+    // the bulk reduce-add needs 16-byte rows; other widths add from registers
+    const bool bulk = N % 4 == 0 && (reinterpret_cast<uintptr_t>(acc.data_ptr()) & 15) == 0;
+    if (!bulk) args.acc_direct = true;
+    const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
+    dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
   else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   return out;
 }
@@ -1369,15 +1569,27 @@ int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
   TORCH_CHECK(one_shot ? M <= slot_rows
                        : own_rows > 0 && own_rows <= slot_rows && int64_t(own_rows) * slots.numel() >= M,
               "every token row needs an owner rank and a slot row");
-  TORCH_CHECK(N % 4 == 0, "output features must be a multiple of 4");
+  TORCH_CHECK(N % 128 == 0, "output features must be a multiple of 128 (whole 128-feature tiles)");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(staging.data_ptr()) & 15) == 0, "staging rows must be 16-byte aligned");
   if (M == 0) return 0;
   const int kb_total = (int(a.size(1)) + BK - 1) / BK;
   Plan p = plan_gemm(a, b, false, 1);
+  // swap-AB tiles reduce their K splits inside one cluster (at most 8 CTAs, one wave of SMs)
+  static const bool rs_cluster = [] {
+    const char* e = std::getenv("ISB_RS_CLUSTER");
+    return !(e && e[0] == '0');
+  }();
+  const bool clustered = p.swap && rs_cluster;
   int sp = splits > 0 ? int(splits) : 1;
   if (splits <= 0) {
     const int tiles = p.tiles_p * p.tiles_q;
-    while (sp < 16 && tiles * sp * 2 <= 2 * num_sms() && kb_total / (sp * 2) >= 2) sp *= 2;
+    if (clustered) {
+      sp = std::max(1, std::min({8, num_sms() / std::max(tiles, 1), kb_total}));
+    } else {
+      while (sp < 16 && tiles * sp * 2 <= 2 * num_sms() && kb_total / (sp * 2) >= 2) sp *= 2;
+    }
   }
+  if (clustered) sp = std::min(sp, 8);
   p.kb_per = (kb_total + sp - 1) / sp;
   p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
   TORCH_CHECK(p.tiles_p * p.tiles_q <= kCountersPerSlot || p.splits == 1, "too many split-K tiles");
@@ -1396,8 +1608,20 @@ int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
   args.rank = int(rank);
   if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  if (p.swap) dispatch_bn<kRsPush, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
-  else launch_gemm<256, false, kRsPush>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  if (clustered && p.splits > 1) {
+    switch (p.bn) {
+      case 16: launch_rs_cluster<16>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 32: launch_rs_cluster<32>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 64: launch_rs_cluster<64>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 128: launch_rs_cluster<128>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      default: TORCH_CHECK(false, "unsupported tile width");
+    }
+  } else if (p.swap) {  // split-K partials of a swap-AB tile meet in the staging rows by bulk reduce-add
+    const CUtensorMap tst = p.splits > 1 ? make_acc_map(staging.data_ptr(), M, N, BM, p.bn) : p.tp;
+    dispatch_bn<kRsPush, true>(p.bn, p.tp, p.tq, tst, args, p.tiles_p, p.tiles_q, p.splits, st);
+  } else {
+    launch_gemm<256, false, kRsPush>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
   return int64_t(p.tiles_p) * p.tiles_q * p.splits;  // CTAs: each bumps every rank's counter once
 }
 
@@ -1410,6 +1634,45 @@ at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, i
   if (M == 0) return out;
   run_gemm(a, b, out, int(epilogue), int(splits), nullptr);
   return out;
+}
+
+// Diagnostics: the accumulating GEMM (``acc`` fp32 [>= M, N], zero between uses) with per-CTA
+// phase timestamps as ``gemm_timeline``.
+at::Tensor gemm_accum_timeline(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int64_t splits) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.is_contiguous() && acc.size(0) >= M && acc.size(1) == N,
+              "accumulator must be contiguous fp32 [>= M, N]");
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  Plan p = plan_gemm(a, b, false, 1);
+  const int sp = std::max(1, int(splits <= -3000 ? -(splits + 3000) : splits <= -2000 ? -(splits + 2000)
+                                 : splits <= -1000 ? -(splits + 1000) : splits < 0 ? -splits : splits));
+  p.kb_per = (kb_total + sp - 1) / sp;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  at::Tensor ts = at::zeros({int64_t(p.tiles_p) * p.tiles_q * p.splits, 8}, a.options().dtype(at::kLong));
+  GemmArgs args = {};
+  args.acc = acc.data_ptr<float>();
+  args.K = a.size(1);
+  args.ldo = N;
+  args.kb_per_split = p.kb_per;
+  args.acc_plain = p.splits == 1;
+  args.acc_direct = splits < 0;
+  if (splits <= -1000) {  // -1000 - s: TMEM loads only; -2000 - s: stores only; -3000 - s: 17 x stores
+    args.epi_probe = splits <= -3000 ? 3 : splits <= -2000 ? 2 : 1;
+  }
+  args.dbg = reinterpret_cast<unsigned long long*>(ts.data_ptr());
+  if (p.swap) { args.P_rows = N; args.Q_rows = M; } else { args.P_rows = M; args.Q_rows = N; }
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.swap) {
+    // the bulk reduce-add needs 16-byte rows; other widths add from registers
+    const bool bulk = N % 4 == 0 && (reinterpret_cast<uintptr_t>(acc.data_ptr()) & 15) == 0;
+    if (!bulk) args.acc_direct = true;
+    const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
+    dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
+  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  return ts;
 }
 
 // Diagnostics: run the plain GEMM and return per-CTA phase timestamps (ns, %globaltimer):

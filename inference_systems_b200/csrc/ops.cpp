@@ -12,6 +12,7 @@ std::tuple<at::Tensor, at::Tensor> lm_head_sample(const at::Tensor& h, const at:
                                                   const at::Tensor& rng, int64_t vocab_offset);
 int64_t gemm_error_word();
 at::Tensor gemm_timeline(const at::Tensor& a, const at::Tensor& b, int64_t splits);
+at::Tensor gemm_accum_timeline(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, int64_t splits);
 void gemm_accum(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, int64_t splits);
 at::Tensor gemm_accum_norm(const at::Tensor& a, const at::Tensor& b, at::Tensor acc, at::Tensor residual,
                            const at::Tensor& w, double eps, bool zc);
@@ -150,6 +151,7 @@ TORCH_LIBRARY(isb, m) {
   m.def("copy_kv_page(Tensor(a!) k_cache, Tensor(b!) v_cache, int src, int dst, int n) -> ()");
   m.def("error_word() -> int");
   m.def("gemm_timeline(Tensor a, Tensor b, int splits) -> Tensor");
+  m.def("gemm_accum_timeline(Tensor a, Tensor b, Tensor(a!) acc, int splits) -> Tensor");
   m.def("gemm_accum(Tensor a, Tensor b, Tensor(a!) acc, int splits=0) -> ()");
   m.def("gemm_accum_norm(Tensor a, Tensor b, Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, "
         "bool zero_centered) -> Tensor");
@@ -193,6 +195,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("dequantize_state_int8", &isb::dequantize_state_int8);
   m.impl("copy_kv_page", &isb::copy_kv_page);
   m.impl("gemm_timeline", &isb::gemm_timeline);
+  m.impl("gemm_accum_timeline", &isb::gemm_accum_timeline);
   m.impl("gemm_accum", &isb::gemm_accum);
   m.impl("gemm_accum_norm", &isb::gemm_accum_norm);
   m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);

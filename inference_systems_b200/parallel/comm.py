@@ -83,7 +83,8 @@ class TPComm:
         off = 0
         layout = {}
         self.slot_rows = max(shard_rows(t, w), min(t, self.one_shot_elems // h))
-        for name, nbytes in (("slots", w * self.slot_rows * h * 2), ("x0", t * h * 2), ("x1", t * h * 2),
+        for name, nbytes in (("slots0", w * self.slot_rows * h * 2), ("slots1", w * self.slot_rows * h * 2),
+                             ("x0", t * h * 2), ("x1", t * h * 2),
                              ("ctl", 32), ("xbuf", w * self.max_sample_rows * 8), ("xflag", w * 4)):
             layout[name] = off
             off += _align(nbytes)
@@ -108,11 +109,16 @@ class TPComm:
             o = layout[name]
             return self.region[o:o + count * torch.tensor([], dtype=dtype).element_size()].view(dtype)
 
-        self.slot_ptrs = table("slots")
+        # slots and activation buffers alternate by exchange parity: in one-shot mode nothing makes a
+        # rank wait for its peers to finish reading their slots, so a rank one exchange ahead must
+        # push into the other buffer (it cannot get two ahead: its next owner kernel waits for
+        # every peer's pushes of the exchange in between, which follow those peers' reads)
+        self.slot_ptrs = [table("slots0"), table("slots1")]
         self.rs_ptrs = table("ctl", 0)      # ctl[0]: arrivals of row-parallel GEMMs
         self.ag_ptrs = table("ctl", 4)      # ctl[1]: arrivals of owners' activation rows
         self.x_ptrs = [table("x0"), table("x1")]
-        self.slots_local = local("slots", torch.bfloat16, w * self.slot_rows * h).view(w, self.slot_rows, h)
+        self.slots_local = [local(f"slots{i}", torch.bfloat16, w * self.slot_rows * h).view(w, self.slot_rows, h)
+                            for i in range(2)]
         # split-K partial tiles are reduced here before a row leaves this GPU (zero between uses)
         self.staging = torch.zeros(t, h, dtype=torch.float32, device=self.device)
         self.x_local = [local("x0", torch.bfloat16, t * h).view(t, h), local("x1", torch.bfloat16, t * h).view(t, h)]
@@ -152,10 +158,11 @@ class TPComm:
             c = ops.cuda_ops()
             s = shard_rows(t, self.world)
             one = t * self.hidden <= self.one_shot_elems and t <= self.slot_rows
-            ctas = c.tp_gemm_rs(x, w, self.slot_ptrs, self.slot_rows, self.staging, self.rs_ptrs, self.rank, s, 0, one)
             p = self.xpar
             self.xpar ^= 1
-            c.tp_norm_allgather(self.slots_local, residual, norm_w, self.x_ptrs[p], self.ag_ptrs, self.ctl, t, s,
+            ctas = c.tp_gemm_rs(x, w, self.slot_ptrs[p], self.slot_rows, self.staging, self.rs_ptrs, self.rank, s, 0,
+                                one)
+            c.tp_norm_allgather(self.slots_local[p], residual, norm_w, self.x_ptrs[p], self.ag_ptrs, self.ctl, t, s,
                                 self.rank, self.world * ctas, eps, zero_centered, True, one)
             return self.x_local[p][:t]
         y = ops.linear(x, w)
