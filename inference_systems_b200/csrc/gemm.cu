@@ -94,6 +94,8 @@ struct GemmArgs {
   const __nv_bfloat16* norm_w;
   float norm_eps;
   bool acc_direct;         // swap-AB kRedAdd: add straight from TMEM registers (no shared staging)
+  bool tma_out;            // non-swap kStore / kSiluMul / kRedAdd: stage the tile (128-byte swizzle)
+                           // and leave through bulk tensor stores / reduce-adds on ``tmO``
   int epi_probe;           // diagnostics of the direct path: 1 = TMEM loads only, 2 = stores only
   int norm_rows;           // token rows of the accumulator
   bool norm_zc;
@@ -179,6 +181,12 @@ ISB_DEVICE void push_rs4(const unsigned long long* dst, bool bcast, int ndst, in
     const size_t off = (size_t(rk) * slot_rows + (tok - owner * own_rows)) * ldo + f;
     *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(dst[(owner - rk + ndst) % ndst]) + off) = raw;
   }
+}
+
+// Byte offset of 16-byte group ``g`` (8 bf16 or 4 fp32) of row ``r`` in a non-swap output tile
+// staged as boxes of 128-byte rows (128-byte swizzle), one box per ``gpb`` groups of columns.
+ISB_DEVICE uint32_t nstage_off(int r, int g, int gpb) {
+  return uint32_t((g / gpb) * (BM * 128) + r * 128 + (((g % gpb) ^ (r & 7)) << 4));
 }
 
 ISB_DEVICE uint32_t fmix32(uint32_t h) {
@@ -573,6 +581,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             // transpose through shared memory: ostage[token][feature]
 #pragma unroll
             for (int j = 0; j < CH; ++j) ostage[(c * CH + j) * BM + row] = __float2bfloat16(v[j]);
+          } else if (args.tma_out) {
+            // 8 bf16 per 16-byte group; 64-column boxes (8 groups)
+#pragma unroll
+            for (int j = 0; j < CH / 8; ++j) {
+              uint4 pk;
+              __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) h[e] = __floats2bfloat162_rn(v[8 * j + 2 * e], v[8 * j + 2 * e + 1]);
+              *reinterpret_cast<uint4*>(smem + nstage_off(row, (c * CH) / 8 + j, 8)) = pk;
+            }
           } else {
             const int t = p0 + row;
             const int col0 = q0 + c * CH;
@@ -618,7 +636,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int within = (c * CH) % 128;
             const int g = (c * CH) / 128;
             const int col0 = q0 / 2 + g * 64 + within;
-            if (t < args.P_rows) {
+            if (args.tma_out) {  // output column (within the tile) g * 64 + within + j
+#pragma unroll
+              for (int j = 0; j < CH / 8; ++j) {
+                uint4 pk;
+                __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&pk);
+#pragma unroll
+                for (int e = 0; e < 4; ++e)
+                  h[e] = __floats2bfloat162_rn(silu(v[8 * j + 2 * e]) * u[8 * j + 2 * e],
+                                               silu(v[8 * j + 2 * e + 1]) * u[8 * j + 2 * e + 1]);
+                *reinterpret_cast<uint4*>(smem + nstage_off(row, (g * 64 + within) / 8 + j, 8)) = pk;
+              }
+            } else if (t < args.P_rows) {
 #pragma unroll
               for (int j = 0; j < CH; ++j)
                 if (col0 + j < args.Q_rows / 2)
@@ -677,6 +706,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < CH; ++j) fstage[(c * CH + j) * BM + row] = v[j];
             }
+          } else if (args.tma_out) {  // 4 fp32 per 16-byte group; 32-column boxes (8 groups)
+#pragma unroll
+            for (int j = 0; j < CH / 4; ++j)
+              *reinterpret_cast<float4*>(smem + nstage_off(row, (c * CH) / 4 + j, 8)) =
+                  make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
           } else {
             const int t = p0 + row;
             const int col0 = q0 + c * CH;
@@ -750,6 +784,37 @@ __global__ void __launch_bounds__(kThreads, 1)
                 args.part_val[slot] = best;
                 args.part_idx[slot] = bi;
               }
+            }
+          }
+        }
+      }
+      // non-swap staged tiles leave through bulk tensor stores (reduce-adds for the accumulator),
+      // one per 128-byte-wide box; the copy engine clips rows and columns past the output
+      if constexpr (!SWAP && (EPI == kStore || EPI == kSiluMul || EPI == kRedAdd)) {
+        if (args.tma_out) {
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (threadIdx.x == 64) {
+            const uint64_t map = reinterpret_cast<uint64_t>(&tmO);
+            constexpr int NBOX = EPI == kRedAdd ? BN / 32 : EPI == kSiluMul ? BN / 128 : BN / 64;
+            constexpr int BOXC = EPI == kRedAdd ? 32 : 64;  // columns per box
+            const int c0 = EPI == kSiluMul ? q0 / 2 : q0;
+#pragma unroll
+            for (int bx = 0; bx < NBOX; ++bx) {
+              const uint32_t src = smem_u32(smem + bx * (BM * 128));
+              if (EPI == kRedAdd && !args.acc_plain)
+                asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2}], [%3];"
+                             ::"l"(map), "r"(c0 + bx * BOXC), "r"(p0), "r"(src) : "memory");
+              else
+                asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                             ::"l"(map), "r"(c0 + bx * BOXC), "r"(p0), "r"(src) : "memory");
+            }
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            if (EPI == kRedAdd && args.norm_out != nullptr) {
+              asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+              asm volatile("fence.proxy.async.global;" ::: "memory");
+            } else {
+              asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
             }
           }
         }
@@ -1285,6 +1350,32 @@ static CUtensorMap make_acc_map(const void* ptr, int64_t rows, int64_t cols, int
   return m;
 }
 
+// Output map of a non-swap tile staged in 128-byte-swizzled boxes of [128 rows x 128 bytes]:
+// bf16 (``fp32`` false, 64 columns per box) or fp32 (32 columns per box); dims {cols, rows}.
+static CUtensorMap make_out_map_sw128(const void* ptr, int64_t rows, int64_t cols, bool fp32) {
+  CUtensorMap m;
+  const int es = fp32 ? 4 : 2;
+  cuuint64_t dims[2] = {cuuint64_t(cols), cuuint64_t(rows)};
+  cuuint64_t strides[1] = {cuuint64_t(cols) * es};
+  cuuint32_t box[2] = {cuuint32_t(128 / es), cuuint32_t(BM)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                           const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (swizzled output) failed: ", int(r));
+  return m;
+}
+
+// Non-swap tiles leave through bulk tensor copies when the output rows are 16-byte multiples.
+static bool out_map_ok(const void* ptr, int64_t cols, bool fp32) {
+  static const bool on = [] {
+    const char* e = std::getenv("ISB_GEMM_TMA_OUT");
+    return !(e && e[0] == '0');
+  }();
+  return on && (cols * (fp32 ? 4 : 2)) % 16 == 0 && (reinterpret_cast<uintptr_t>(ptr) & 15) == 0;
+}
+
 static int num_sms() {
   static int n = 0;
   if (!n) {
@@ -1427,6 +1518,9 @@ static void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, 
   if (p.swap) {
     TORCH_CHECK(out_cols % 8 == 0, "swap-AB GEMM output width must be a multiple of 8 (16-byte rows)");
     to = make_store_map(out.data_ptr(), M, out_cols, epilogue == kSiluMul ? 64 : BM, pair ? p.bn / 2 : p.bn);
+  } else if (out_map_ok(out.data_ptr(), out_cols, false)) {
+    to = make_out_map_sw128(out.data_ptr(), M, out_cols, false);
+    args.tma_out = true;
   }
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   if (pair) {
@@ -1485,7 +1579,12 @@ void gemm_accum(const at::Tensor& a_in, const at::Tensor& b, at::Tensor acc, int
     const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
     dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
   }
-  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else {
+    const bool bulk = out_map_ok(acc.data_ptr(), N, true);
+    args.tma_out = bulk;
+    const CUtensorMap tacc = bulk ? make_out_map_sw128(acc.data_ptr(), M, N, true) : p.tp;
+    launch_gemm<256, false, kRedAdd>(p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
 }
 
 at::Tensor add_rmsnorm_acc(at::Tensor acc, at::Tensor residual, const at::Tensor& w, double eps, bool zc);
@@ -1542,7 +1641,12 @@ at::Tensor gemm_accum_norm(const at::Tensor& a_in, const at::Tensor& b, at::Tens
     const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
     dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
   }
-  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else {
+    const bool bulk = out_map_ok(acc.data_ptr(), N, true);
+    args.tma_out = bulk;
+    const CUtensorMap tacc = bulk ? make_out_map_sw128(acc.data_ptr(), M, N, true) : p.tp;
+    launch_gemm<256, false, kRedAdd>(p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
   return out;
 }
 
@@ -1671,7 +1775,12 @@ at::Tensor gemm_accum_timeline(const at::Tensor& a_in, const at::Tensor& b, at::
     const CUtensorMap tacc = bulk ? make_acc_map(acc.data_ptr(), M, N, BM, p.bn) : p.tp;
     dispatch_bn<kRedAdd, true>(p.bn, p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
   }
-  else launch_gemm<256, false, kRedAdd>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
+  else {
+    const bool bulk = out_map_ok(acc.data_ptr(), N, true);
+    args.tma_out = bulk;
+    const CUtensorMap tacc = bulk ? make_out_map_sw128(acc.data_ptr(), M, N, true) : p.tp;
+    launch_gemm<256, false, kRedAdd>(p.tp, p.tq, tacc, args, p.tiles_p, p.tiles_q, p.splits, st);
+  }
   return ts;
 }
 
