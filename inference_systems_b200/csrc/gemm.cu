@@ -82,6 +82,12 @@ struct GemmArgs {
   bool bcast;                      // one-shot: every row goes to every rank (slot row = token)
   const unsigned long long* peer_flags;  // [ndst] address of each rank's arrival counter
   int rank;
+  // kRsPush one-shot with the residual add + RMSNorm in the same kernel (``norm_out`` set): this
+  // rank's slots [ndst][slot_rows][ldo], its control words (0 arrivals, 2 arrival target of the
+  // previous exchange, 4 CTA-completion counter) and the exchange error word
+  const __nv_bfloat16* tp_slots;
+  unsigned int* tp_ctl;
+  unsigned int* tp_err;
   // kRedAdd with one K split on one rank: every accumulator element is produced by exactly one
   // CTA and the accumulator is zero between uses, so plain stores replace the atomics
   bool acc_plain;
@@ -270,6 +276,82 @@ __device__ __forceinline__ void fused_add_norm(const GemmArgs& args) {
     if (prev == total - 1) {
       *arrive = 0u;
       *depart = 0u;
+    }
+  }
+}
+
+// Tail of a one-shot reduce-scatter GEMM that also normalises (128 epilogue threads of every CTA):
+// wait (bounded) until every rank's CTAs of this exchange have counted themselves in here, then
+// rows blockIdx, blockIdx + grid, ...: x = residual + sum over the source slots; residual <- bf16(x),
+// norm_out <- RMSNorm(x).  The last CTA out moves the arrival target on.
+__device__ __forceinline__ void rs_oneshot_norm(const GemmArgs& args) {
+  __shared__ float red[4];
+  __shared__ unsigned int s_target;
+  const int tid = threadIdx.x - 64;
+  const unsigned int total = gridDim.x * gridDim.y * gridDim.z;
+  const unsigned int cta = (blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+  unsigned int* ctl = args.tp_ctl;
+  if (tid == 0) {
+    const unsigned int target = *reinterpret_cast<volatile unsigned int*>(ctl + 2) + unsigned(args.ndst) * total;
+    s_target = target;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    for (;;) {
+      unsigned int v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(ctl) : "memory");
+      if (int(v - target) >= 0) break;
+      if ((++spins & 255u) == 0 && globaltimer_ns() - t0 > kWaitTimeoutNs) {
+        atomicOr(args.tp_err, 16u);  // rows are still normalised; the step reports the error
+        break;
+      }
+    }
+  }
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+  const int T = args.norm_rows, H = args.ldo, W = args.ndst;
+  const size_t slot_stride = size_t(args.slot_rows) * H;
+  for (int row = int(cta); row < T; row += int(total)) {
+    __nv_bfloat16* res = args.norm_res + size_t(row) * H;
+    const __nv_bfloat16* src = args.tp_slots + size_t(row) * H;
+    float x[8];
+    float ss = 0.f;
+    const int c = tid * 8;  // H <= 1024: one group of 8 columns per thread
+    if (c < H) {
+      uint4 raw[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        raw[q] = q < W ? __ldcg(reinterpret_cast<const uint4*>(src + q * slot_stride + c)) : make_uint4(0u, 0u, 0u, 0u);
+      const Vec8 r = load8(res + c);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = r.v[e];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&raw[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(hh[e]);
+          x[2 * e] += f.x;
+          x[2 * e + 1] += f.y;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+    }
+    ss = warp_sum(ss);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const float rs = rsqrtf((red[0] + red[1] + red[2] + red[3]) / float(H) + args.norm_eps);
+    if (c < H) {
+      store8(res + c, x);
+      norm_store8(args.norm_out + size_t(row) * H + c, x, args.norm_w + c, rs, args.norm_zc);
+    }
+    asm volatile("bar.sync 1, 128;" ::: "memory");  // ``red`` is reused by the next row
+  }
+  if (tid == 0) {
+    unsigned int prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ctl + 4) : "memory");
+    if (prev == total - 1) {
+      ctl[4] = 0u;
+      ctl[2] = s_target;
     }
   }
 }
@@ -961,7 +1043,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Every CTA counts itself in on every rank once its pushes are issued: one system-scope fence
     // by one thread after the epilogue barrier orders all 128 epilogue threads' stores (and, for
     // the tile's last split, the staged sums it read) before the counts; the owners wait for
-    // world x gridDim CTAs.  No CTA waits for another, no fence drains the whole grid.
+    // world x gridDim CTAs.  No fence drains the whole grid; only the fused one-shot norm makes a
+    // CTA wait for the other ranks' CTAs (bounded).
     if (epi) {
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (threadIdx.x == 64) {
@@ -971,6 +1054,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("red.relaxed.sys.global.add.u32 [%0], 1;" ::"l"(flag) : "memory");
         }
       }
+      if (args.norm_out != nullptr) rs_oneshot_norm(args);
     }
   }
   tc_fence_before();
@@ -1727,6 +1811,73 @@ int64_t tp_gemm_rs(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor
     launch_gemm<256, false, kRsPush>(p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, p.splits, st);
   }
   return int64_t(p.tiles_p) * p.tiles_q * p.splits;  // CTAs: each bumps every rank's counter once
+}
+
+int64_t comm_error_word_address();
+
+// One-shot exchange in ONE kernel (decode, swap-AB tiles, at most 128 tokens): the row-parallel
+// GEMM reduces its K splits in a cluster, pushes every row to every rank's slot, waits (bounded)
+// until all ranks' CTAs have pushed, then adds the residual and applies the RMSNorm of all rows
+// into ``xout`` (and ``residual``).  Every CTA of the grid must be resident at once: the split
+// count keeps the grid within one wave of SMs.
+void tp_gemm_rs_norm(const at::Tensor& a_in, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
+                     const at::Tensor& flags, int64_t rank, const at::Tensor& slots_local, at::Tensor residual,
+                     const at::Tensor& w, at::Tensor xout, at::Tensor ctl, double eps, bool zc) {
+  at::Tensor a = a_in.contiguous();
+  check_operands(a, b);
+  const int M = a.size(0), N = b.size(0);
+  TORCH_CHECK(M <= 128 && M <= slot_rows, "fused one-shot exchange serves at most 128 tokens");
+  TORCH_CHECK(N % 128 == 0 && N <= 1024, "fused one-shot exchange: hidden size a multiple of 128, at most 1024");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && flags.scalar_type() == at::kLong && slots.numel() == flags.numel() &&
+                  slots.numel() <= 8, "slots / flags: int64 device tables, one entry per rank (<= 8)");
+  TORCH_CHECK(residual.scalar_type() == at::kBFloat16 && residual.is_contiguous() && residual.size(0) >= M &&
+                  residual.size(1) == N, "residual must be contiguous bf16 [>= T, H]");
+  TORCH_CHECK(xout.scalar_type() == at::kBFloat16 && xout.is_contiguous() && xout.size(0) >= M && xout.size(1) == N,
+              "output must be contiguous bf16 [>= T, H]");
+  TORCH_CHECK(ctl.scalar_type() == at::kInt && ctl.numel() >= 8, "control words: int32 [8]");
+  if (M == 0) return;
+  const int kb_total = (int(a.size(1)) + BK - 1) / BK;
+  Plan p = plan_gemm(a, b, false, 1);
+  TORCH_CHECK(p.swap, "fused one-shot exchange needs swap-AB tiles");
+  const int tiles = p.tiles_p * p.tiles_q;
+  const int sp = std::max(1, std::min({8, num_sms() / std::max(tiles, 1), kb_total}));
+  p.kb_per = (kb_total + sp - 1) / sp;
+  p.splits = (kb_total + p.kb_per - 1) / p.kb_per;
+  TORCH_CHECK(tiles * p.splits <= num_sms(), "fused exchange grid must fit on the SMs");
+  GemmArgs args = {};
+  args.K = a.size(1);
+  args.ldo = N;
+  args.kb_per_split = p.kb_per;
+  args.dsts = reinterpret_cast<const unsigned long long*>(slots.data_ptr<int64_t>());
+  args.ndst = int(slots.numel());
+  args.own_rows = M;
+  args.slot_rows = int(slot_rows);
+  args.bcast = true;
+  args.peer_flags = reinterpret_cast<const unsigned long long*>(flags.data_ptr<int64_t>());
+  args.rank = int(rank);
+  args.tp_slots = reinterpret_cast<const __nv_bfloat16*>(slots_local.data_ptr());
+  args.tp_ctl = reinterpret_cast<unsigned int*>(ctl.data_ptr<int>());
+  args.tp_err = reinterpret_cast<unsigned int*>(comm_error_word_address());
+  args.norm_out = reinterpret_cast<__nv_bfloat16*>(xout.data_ptr());
+  args.norm_res = reinterpret_cast<__nv_bfloat16*>(residual.data_ptr());
+  args.norm_w = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  args.norm_eps = float(eps);
+  args.norm_zc = zc;
+  args.norm_rows = M;
+  args.P_rows = N;
+  args.Q_rows = M;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (p.splits > 1) {
+    switch (p.bn) {
+      case 16: launch_rs_cluster<16>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 32: launch_rs_cluster<32>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 64: launch_rs_cluster<64>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      case 128: launch_rs_cluster<128>(p.tp, p.tq, args, p.tiles_p, p.tiles_q, p.splits, st); break;
+      default: TORCH_CHECK(false, "unsupported tile width");
+    }
+  } else {
+    dispatch_bn<kRsPush, true>(p.bn, p.tp, p.tq, p.tp, args, p.tiles_p, p.tiles_q, 1, st);
+  }
 }
 
 at::Tensor gemm(const at::Tensor& a_in, const at::Tensor& b, int64_t epilogue, int64_t splits) {

@@ -69,6 +69,9 @@ void copy_kv_page(at::Tensor kc, at::Tensor vc, int64_t src, int64_t dst, int64_
 
 int64_t attn_error_word();
 int64_t comm_error_word();
+void tp_gemm_rs_norm(const at::Tensor& a, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
+                     const at::Tensor& flags, int64_t rank, const at::Tensor& slots_local, at::Tensor residual,
+                     const at::Tensor& w, at::Tensor xout, at::Tensor ctl, double eps, bool zc);
 int64_t tp_gemm_rs(const at::Tensor& a, const at::Tensor& b, const at::Tensor& slots, int64_t slot_rows,
                    at::Tensor staging, const at::Tensor& flags, int64_t rank, int64_t own_rows, int64_t splits,
                    bool one_shot);
@@ -157,6 +160,8 @@ TORCH_LIBRARY(isb, m) {
         "bool zero_centered) -> Tensor");
   m.def("add_rmsnorm_acc(Tensor(a!) acc, Tensor(b!) residual, Tensor w, float eps, bool zero_centered) -> Tensor");
   m.def("silu_mul_acc(Tensor(a!) acc, int rows) -> Tensor");
+  m.def("tp_gemm_rs_norm(Tensor a, Tensor b, Tensor slots, int slot_rows, Tensor flags, int rank, Tensor slots_local, "
+        "Tensor(a!) residual, Tensor w, Tensor(b!) xout, Tensor(c!) ctl, float eps, bool zero_centered) -> ()");
   m.def("tp_gemm_rs(Tensor a, Tensor b, Tensor slots, int slot_rows, Tensor(a!) staging, Tensor flags, "
         "int rank, int own_rows, int splits=0, bool one_shot=False) -> int");
   m.def("tp_norm_allgather(Tensor slots, Tensor(b!) residual, Tensor w, Tensor xdst, Tensor ag_flags, "
@@ -201,6 +206,7 @@ TORCH_LIBRARY_IMPL(isb, CUDA, m) {
   m.impl("add_rmsnorm_acc", &isb::add_rmsnorm_acc);
   m.impl("silu_mul_acc", &isb::silu_mul_acc);
   m.impl("tp_gemm_rs", &isb::tp_gemm_rs);
+  m.impl("tp_gemm_rs_norm", &isb::tp_gemm_rs_norm);
   m.impl("tp_norm_allgather", &isb::tp_norm_allgather);
   m.impl("step_status", &isb::step_status);
   m.impl("xrank_argmax", &isb::xrank_argmax);

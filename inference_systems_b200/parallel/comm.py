@@ -56,6 +56,9 @@ def shard_rows(T: int, world: int) -> int:
     return max((T + world - 1) // world, 1)
 
 
+# ISB_TP_FUSED_ONE_SHOT=0: one-shot exchanges run the GEMM and the owner-norm kernel separately
+_FUSED_ONE_SHOT = os.environ.get("ISB_TP_FUSED_ONE_SHOT", "1") != "0"
+
 class TPComm:
     def __init__(self, device: torch.device, rank: int, world: int, hidden: int, config=None,
                  max_tokens: int | None = None, max_sample_rows: int | None = None, group=None):
@@ -160,6 +163,11 @@ class TPComm:
             one = t * self.hidden <= self.one_shot_elems and t <= self.slot_rows
             p = self.xpar
             self.xpar ^= 1
+            if one and t <= 128 and self.hidden <= 1024 and _FUSED_ONE_SHOT:
+                # one kernel: GEMM, push to every rank, bounded wait for all ranks, residual + norm
+                c.tp_gemm_rs_norm(x, w, self.slot_ptrs[p], self.slot_rows, self.rs_ptrs, self.rank,
+                                  self.slots_local[p], residual, norm_w, self.x_local[p], self.ctl, eps, zero_centered)
+                return self.x_local[p][:t]
             ctas = c.tp_gemm_rs(x, w, self.slot_ptrs[p], self.slot_rows, self.staging, self.rs_ptrs, self.rank, s, 0,
                                 one)
             c.tp_norm_allgather(self.slots_local[p], residual, norm_w, self.x_ptrs[p], self.ag_ptrs, self.ctl, t, s,
