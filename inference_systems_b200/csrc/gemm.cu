@@ -1969,8 +1969,11 @@ at::Tensor gemm_timeline(const at::Tensor& a_in, const at::Tensor& b, int64_t sp
     return ts;
   }
   at::Tensor out = at::empty({M, N}, a.options());
-  Plan p = plan_gemm(a, b, false, int(splits));
-  at::Tensor ts = at::zeros({int64_t(p.tiles_p) * p.tiles_q * p.splits, 8}, a.options().dtype(at::kLong));
+  // the same plan run_gemm makes (two token tiles per weight tile when it halves them, a cluster
+  // pair for narrow tiles): one row of timestamps per CTA it may launch (unused rows stay zero)
+  Plan p = plan_gemm(a, b, false, int(splits), /*halve_tokens=*/splits == 0);
+  const int64_t ctas = int64_t(p.tiles_p) * p.tiles_q * std::max(p.splits, 2);
+  at::Tensor ts = at::zeros({ctas, 8}, a.options().dtype(at::kLong));
   run_gemm(a, b, out, kStore, int(splits), reinterpret_cast<unsigned long long*>(ts.data_ptr()));
   return ts;
 }
