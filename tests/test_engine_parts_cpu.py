@@ -122,3 +122,25 @@ def test_registry_builds_both_families():
     m = create_model(*normalize_hf_config(_qwen35_wrapper()))
     assert isinstance(m, Qwen3_5ForCausalLM)
     assert [layer.is_linear for layer in m.layers] == [True, True, True, False]
+
+
+def test_decode_metadata_fast_path_matches_the_general_packer():
+    """The column-wise decode packer produces exactly the general packer's int32 array, layout
+    and metadata (with graph padding, scratch-slot rows and mixed temperatures)."""
+    import numpy as np
+
+    from inference_systems_b200.engine.model_runner import ModelRunner
+
+    seqs = []
+    for i in range(37):
+        s = Sequence(list(range(200 + 7 * i)), SamplingParams(temperature=0.1 * (i % 3), max_tokens=8))
+        s.block_table = [i * 4 + j for j in range(-(-len(s) // 256))]
+        s.state_slot = i if i % 5 else None
+        s.is_prefill = False
+        seqs.append(s)
+    runner = SimpleNamespace(block_size=256, state_manager=SimpleNamespace(scratch_slot_id=99), max_blocks_per_seq=8,
+                             config=SimpleNamespace(seed=3), sample_step=7)
+    for pad in (None, 48):
+        a = ModelRunner._pack_general(runner, seqs, False, pad)
+        b = ModelRunner._pack_decode(runner, seqs, pad)
+        assert np.array_equal(a[0], b[0]) and a[1] == b[1] and a[2] == b[2]
